@@ -1,0 +1,160 @@
+"""Kernel tables for the two engines (analysis engine, synthesis engine).
+
+Analysis engine (``bands_fwd`` over the untangled half spectrum X = rfft(x)):
+    coef[band, n] = sum_m gain[m] * X~[src[m]] * exp(+2 pi i m n / M)
+with X~ = X or conj(X) per tap.  One table set per use:
+
+* ``analysis``  src = window gather bin (``oct_cqt.py:84-96``; mirrored taps
+  conjugated), gain = window / M  (the ifft's 1/M folded in);
+* ``adj_synth`` the transpose of the synthesis (``fused.py:466-474`` proves
+  the constants): src = scatter bin, gain = dual * (2/N), halved on the DC
+  and Nyquist bins.
+
+Synthesis engine (``bands_inv`` into colour planes, then ``spectrum_inv``):
+    E[plane, bin] = (Re S[m] * gre[m], Im S[m] * gim[m]),  S = DFT_M(coef)
+    y = irfft(sum over the planes flagged in mask[bin])
+
+* ``synth``   dest = scatter bin of live dual taps (``oct_cqt.py:98-117``),
+  gre = gim = dual * M;
+* ``adj_an``  the transpose of the analysis (``fused.py:452-464``): dest =
+  analysis gather bin, gre = window / M * N/2 (doubled on DC / Nyquist), gim
+  = +-gre (sign = conjugation, zero on DC / Nyquist).
+
+Colour planes replace the reference's atomic scatter (``radix_impl.cuh:100-
+129``): every live tap gets a (plane, bin) slot of its own, chosen greedily per
+band run, so the reduction in ``spectrum_inv`` reads each slot exactly once in
+a fixed plane order -- deterministic, no zeroing, no atomics.
+"""
+import math
+
+import numpy as np
+
+N_SLICE = 65536
+HALF = N_SLICE // 2
+PLANE_STRIDE = HALF + 8   # complex elements per colour plane (64-B multiple)
+MAX_PLANES = 4
+FWD_SETS = ("analysis", "adj_synth")
+INV_SETS = ("synth", "adj_an")
+BAND_ORDER = (2048, 1024, 512, 256, 128, 64, 32)   # scheduling classes
+
+
+def _assign_planes(runs, nbins):
+    """Greedy colouring of tap runs: each run (array of bins, distinct within
+    the run) gets the lowest plane where none of its bins is taken."""
+    used = np.zeros((MAX_PLANES, nbins), bool)
+    plane = []
+    for bins in runs:
+        for p in range(MAX_PLANES):
+            if not used[p, bins].any():
+                used[p, bins] = True
+                plane.append(p)
+                break
+        else:
+            raise RuntimeError("scatter overlap exceeds %d planes" % MAX_PLANES)
+    mask = np.zeros(nbins, np.uint8)
+    for p in range(MAX_PLANES):
+        mask |= (used[p].astype(np.uint8) << p)
+    nplanes = int(max(plane) + 1) if plane else 1
+    return plane, mask, nplanes
+
+
+def build_tables(heap):
+    """All host tables for one HeapLayout (numpy, float32 / int32)."""
+    bank = heap.bank
+    N = bank.nn
+    if N != N_SLICE:
+        raise ValueError("the CUDA engines are built for 65536-sample slices, "
+                         "got %d" % N)
+    half = N // 2
+    nc = heap.ncoef
+    groups = heap.groups + heap.side_groups
+    src_an = np.full(nc, -1, np.int32)
+    gain_an = np.zeros(nc, np.float64)
+    src_as = np.full(nc, -1, np.int32)
+    gain_as = np.zeros(nc, np.float64)
+    dest_bins = {s: np.full(nc, -1, np.int64) for s in INV_SETS}
+    gre = {s: np.zeros(nc, np.float64) for s in INV_SETS}
+    gim = {s: np.zeros(nc, np.float64) for s in INV_SETS}
+    runs = {s: [] for s in INV_SETS}     # (tap indices) per run
+    for (b, M, off), (idx, gv, pos, gdv, conj) in zip(heap.gspec, groups):
+        for r in range(b):
+            o = off + r * M
+            sl = slice(o, o + M)
+            live_a = gv[r] != 0
+            live_s = gdv[r] != 0
+            k = idx[r]
+            cj = conj[r]
+            # analysis gather
+            src_an[sl] = np.where(live_a, k | (cj.astype(np.int64) << 16), -1)
+            gain_an[sl] = np.where(live_a, gv[r] / M, 0.0)
+            # transpose of the synthesis: gather at the scatter bins
+            edge_s = (pos[r] == 0) | (pos[r] == half)
+            src_as[sl] = np.where(live_s, pos[r], -1)
+            gain_as[sl] = np.where(live_s, gdv[r] * (2.0 / N)
+                                   * np.where(edge_s, 0.5, 1.0), 0.0)
+            # synthesis scatter
+            dest_bins["synth"][sl] = np.where(live_s, pos[r], -1)
+            gre["synth"][sl] = gim["synth"][sl] = np.where(live_s, gdv[r], 0.0)
+            taps = np.arange(o, o + M)
+            runs["synth"].append(taps[live_s])
+            # transpose of the analysis: scatter at the gather bins
+            edge_a = (k == 0) | (k == half)
+            ga = gv[r] / M * (N / 2.0)
+            dest_bins["adj_an"][sl] = np.where(live_a, k, -1)
+            gre["adj_an"][sl] = np.where(live_a, ga * np.where(edge_a, 2.0, 1.0), 0.0)
+            gim["adj_an"][sl] = np.where(live_a & ~edge_a,
+                                         ga * np.where(cj, -1.0, 1.0), 0.0)
+            # mirrored and direct taps of a side band may hit the same bin:
+            # they form separate runs
+            runs["adj_an"].append(taps[live_a & ~cj])
+            if (live_a & cj).any():
+                runs["adj_an"].append(taps[live_a & cj])
+
+    t = {}
+    t["fwd"] = {
+        "analysis": (src_an, gain_an.astype(np.float32)),
+        "adj_synth": (src_as, gain_as.astype(np.float32)),
+    }
+    t["inv"] = {}
+    for s in INV_SETS:
+        rr = [rn for rn in runs[s] if rn.size]
+        plane, mask, nplanes = _assign_planes(
+            [dest_bins[s][rn] for rn in rr], half + 1)
+        dest = np.full(nc, -1, np.int64)
+        for rn, p in zip(rr, plane):
+            dest[rn] = p * PLANE_STRIDE + dest_bins[s][rn]
+        maskp = np.zeros(PLANE_STRIDE, np.uint8)
+        maskp[:half + 1] = mask
+        t["inv"][s] = (dest.astype(np.int32), gre[s].astype(np.float32),
+                       gim[s].astype(np.float32), maskp, nplanes)
+    t["nplanes"] = max(v[4] for v in t["inv"].values())
+
+    # band scheduling classes, largest block length first
+    bands = heap.bands
+    cls = []
+    order = []
+    for M in BAND_ORDER:
+        ids = [i for i, (m, _) in enumerate(bands) if m == M]
+        if ids:
+            cls.append((M, len(ids), len(order)))
+            order.extend(ids)
+    t["classes"] = cls
+    t["band_list"] = np.array(order, np.int32)
+    t["band_off"] = np.array([o for _, o in bands], np.int32)
+    t["band_len"] = np.array([m for m, _ in bands], np.int32)
+
+    # twiddles: W_2048^e for the band FFTs, two-level W_65536 for the packed
+    # FFT engine (W^e = hi[e >> 8] * lo[e & 255]); float64 maths, one rounding
+    e = np.arange(2048)
+    t["tw2048"] = _cplx32(np.exp(-2j * math.pi * e / 2048))
+    e = np.arange(256)
+    t["tw_hi"] = _cplx32(np.exp(-2j * math.pi * (256 * e) / 65536))
+    t["tw_lo"] = _cplx32(np.exp(-2j * math.pi * e / 65536))
+    return t
+
+
+def _cplx32(z):
+    out = np.empty(z.shape + (2,), np.float32)
+    out[..., 0] = z.real
+    out[..., 1] = z.imag
+    return out

@@ -1,0 +1,110 @@
+"""CPU checks of the product table builder and of the kernels' dataflow model.
+
+* the product filterbank / heap layout reproduces the oracle (itself pinned to
+  the reference);
+* ``kernel_model`` (the exact index arithmetic of the CUDA kernels, in numpy
+  float64) reproduces numpy's FFTs and, driven by the product tables, the
+  oracle's analysis, synthesis and both adjoints.
+"""
+import numpy as np
+import pytest
+
+import kernel_model as km
+from fixtures import gc_seed, gy_seed, oracle, x_noise
+from flash_cqt_b200.layout import Filterbank, HeapLayout
+from flash_cqt_b200.tables import PLANE_STRIDE, build_tables
+from oracle.cqt_oracle import snr_db
+
+
+@pytest.fixture(scope="module")
+def heap():
+    return HeapLayout(Filterbank([3, 4, 2], [8, 16, 32], 44100, 65536))
+
+
+@pytest.fixture(scope="module")
+def tabs(heap):
+    return build_tables(heap)
+
+
+def test_filterbank_matches_oracle(heap):
+    o = oracle()
+    bank = heap.bank
+    assert bank.oct_bins == o.bank.oct_bins
+    assert bank.size_per_oct == o.bank.size_per_oct
+    assert (bank.M0, bank.Mnyq, bank.fbins) == (o.bank.M0, o.bank.Mnyq, o.bank.fbins)
+    for a, b in zip(bank.ranges, o.bank.wins):
+        np.testing.assert_array_equal(a, b)
+    for a, b in zip(bank.gd, o.bank.gd):
+        np.testing.assert_allclose(a, b, rtol=1e-12, atol=0)
+    for (i1, g1, p1, d1, c1), (i2, g2, p2, d2, c2) in zip(
+            heap.groups + heap.side_groups, o.all_groups):
+        np.testing.assert_array_equal(i1, i2)
+        np.testing.assert_array_equal(p1, p2)
+        np.testing.assert_array_equal(c1, c2)
+        np.testing.assert_allclose(g1, g2, rtol=1e-12, atol=0)
+        np.testing.assert_allclose(d1, d2, rtol=1e-12, atol=0)
+    assert heap.ncoef == o.ncoef == 132992
+    assert len(heap.bands) == 154
+
+
+def test_plane_assignment(tabs):
+    for s, (dest, gre, gim, mask, npl) in tabs["inv"].items():
+        live = dest >= 0
+        assert np.unique(dest[live]).size == live.sum(), s
+        assert npl <= 4
+        # every bin of the half spectrum is covered by some window
+        assert np.all(mask[:32769] != 0), s
+        assert np.all(mask[32769:] == 0)
+
+
+def test_stockham_schedules_match_fft():
+    rng = np.random.default_rng(3)
+    for M, (P, rad) in km.BAND_CFG.items():
+        assert np.prod(rad) == M and max(rad) <= P
+        v = rng.standard_normal((2, M)) + 1j * rng.standard_normal((2, M))
+        assert snr_db(np.fft.fft(v), km.stockham(v, rad, -1)) > 250
+        assert snr_db(np.fft.ifft(v) * M, km.stockham(v, rad, +1)) > 250
+
+
+def test_packed_spectrum_model():
+    x = x_noise().astype(np.float64)
+    X = km.spectrum_fwd(x)
+    assert snr_db(np.fft.rfft(x), X) > 250
+    F = np.fft.rfft(x) + 1j * 0.3   # imag on DC / Nyquist must be ignored
+    assert snr_db(np.fft.irfft(F, n=65536), km.spectrum_inv(F)) > 250
+
+
+def test_analysis_model_vs_oracle(heap, tabs):
+    o = oracle()
+    x = x_noise().astype(np.float64)
+    src, gain = tabs["fwd"]["analysis"]
+    h = km.bands_fwd(km.spectrum_fwd(x), {"src": src, "gain": gain}, heap.bands)
+    assert snr_db(o.heap(o.fwd(x)), h) > 140
+
+
+def _synth(tabs, heap, s, K):
+    dest, gre, gim, mask, npl = tabs["inv"][s]
+    E = km.bands_inv(K, {"dest": dest, "gre": gre, "gim": gim}, heap.bands,
+                     npl, PLANE_STRIDE)
+    return km.spectrum_inv(km.planes_reduce(E, mask, npl, PLANE_STRIDE))
+
+
+def test_synthesis_model_vs_oracle(heap, tabs):
+    o = oracle()
+    x = x_noise().astype(np.float64)
+    K = o.heap(o.fwd(x))
+    y = _synth(tabs, heap, "synth", K)
+    assert snr_db(o.bwd(o.unheap(K)), y) > 140
+    assert snr_db(x, y) > 140
+
+
+def test_adjoint_models_vs_oracle(heap, tabs):
+    o = oracle()
+    gc = gc_seed(o.ncoef).astype(np.complex128)
+    gx = _synth(tabs, heap, "adj_an", gc)
+    assert snr_db(o.adj_fwd(o.unheap(gc)), gx) > 140
+    gy = gy_seed().astype(np.float64)
+    src, gain = tabs["fwd"]["adj_synth"]
+    gk = km.bands_fwd(km.spectrum_fwd(gy), {"src": src, "gain": gain},
+                      heap.bands)
+    assert snr_db(o.heap(o.adj_bwd(gy)), gk) > 140
