@@ -1,0 +1,416 @@
+#!/usr/bin/env python
+"""Benchmark: 65536-sample CQT round trips/s on 1..8 B200 (+ train step ms).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
+    python bench.py --impl reference ...      # CPU reference-port arm
+
+One step = one analysis + synthesis round trip of B slices per GPU (default
+1024, inputs larger than L2) through the sm_100a engines, replayed as one CUDA
+graph.  Under torchrun every rank runs its own batch (weak scaling, no
+collective on the data path); the time is the max over ranks.  Rank 0 prints
+one JSON line.
+"""
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N = 65536
+METRIC = "65536-sample CQT round trips/s"
+# algorithmic bytes per slice (x in, coefficients out, coefficients in, y out)
+RT_BYTES = 262144 + 1063936 + 1063936 + 262144
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1024, help="slices per GPU per step")
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the batch sweep, train step, e2e and CPU baseline")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            p = [s.strip() for s in ln.split(",")]
+            if len(p) < 7:
+                continue
+            try:
+                sm.append(float(p[0]))
+                smax = float(p[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- reference arm
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    from oracle.cpu_port import CPUPort, cpu_model
+    import torch
+    port = CPUPort()
+    B = 16   # bounded sample of the workload per step
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(B, N, generator=g)
+    for _ in range(max(args.warmup, 1)):
+        port.round_trip(x)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        port.round_trip(x)
+        ts.append(time.perf_counter() - t0)
+    tot = sum(ts)
+    value = B * args.steps / tot
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "round_trips/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "FusedOctCQT round trip, OctCQT([3,4,2],[8,16,32]) "
+                               "65536-sample N(0,1) slices (config 4)",
+                   "global_batch": B, "seq_len": N, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "round_trips/s",
+                         "cores": port.threads, "kind": "port",
+                         "sample": f"{args.steps} round trips of {B} slices on the host "
+                                   f"({cpu_model()}), torch CPU float32 restatement "
+                                   "of OctCQT.fwd/bwd"},
+        "e2e": {"value": value, "unit": "round_trips/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------------- b200
+def load_traffic():
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+def main():
+    args = parse()
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        if args.impl == "b200":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        else:
+            dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    import numpy as np
+    from flash_cqt_b200 import FusedOctCQT, Graphed, OctCQT, TrainableCQT
+    from flash_cqt_b200 import _native
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B = args.batch
+    W = max(args.warmup, 3)
+    K = args.steps
+    cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=N, device=dev)
+    t = TrainableCQT(cqt, dev)
+    eng = t.eng
+    g = torch.Generator(device=dev).manual_seed(4 + rank)
+    x = torch.randn(B, N, device=dev, generator=g)
+    coef = torch.empty(B, eng.ncoef, dtype=torch.complex64, device=dev)
+    y = torch.empty(B, N, device=dev)
+
+    def round_trip():
+        eng.analysis(x, out=coef)
+        eng.synthesis(coef, out=y)
+
+    # correctness guard on the benchmarked buffers
+    round_trip()
+    torch.cuda.synchronize()
+    err = ((y.double() - x.double()) ** 2).sum() / (x.double() ** 2).sum()
+    rt_db = float(-10 * torch.log10(err))
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(W):
+            round_trip()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        round_trip()
+    for _ in range(W):
+        graph.replay()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(K):
+            graph.replay()
+        ev1.record()
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_step = ms / K
+    value = world * B * K / (ms / 1e3)
+
+    # ---- per-kernel CUDA-event timing (eager launches of each stage)
+    stream = torch.cuda.current_stream()
+    ws = eng.workspace(B)
+    sp = int(stream.cuda_stream)
+    names = ["spectrum_fwd", "bands_fwd", "bands_inv", "spectrum_inv"]
+    kev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(4)] for _ in range(K)]
+
+    def stage(s):
+        eng.tables.stage(s, x.data_ptr(), y.data_ptr(), coef.data_ptr(), None,
+                         _native.CQT_LAYOUT_COMPLEX, B, ws.data_ptr(), ws.numel(), sp)
+
+    for _ in range(W):
+        for s in range(4):
+            stage(s)
+    torch.cuda.synchronize()
+    for k in range(K):
+        for s in range(4):
+            kev[k][s][0].record()
+            stage(s)
+            kev[k][s][1].record()
+    torch.cuda.synchronize()
+    kms = [statistics.mean(kev[k][s][0].elapsed_time(kev[k][s][1]) for k in range(K))
+           for s in range(4)]
+    tabs = eng.host_tables
+    live_syn = int((tabs["inv"]["synth"][0] >= 0).sum())
+    spec_bytes = 32769 * 8
+    kbytes = [262144 + spec_bytes, spec_bytes + 1063936,
+              1063936 + live_syn * 8, live_syn * 8 + 262144]
+    dom = max(range(4), key=lambda i: kms[i])
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    hbm = peaks.get("hbm_gbs")
+    peak_src = "measured" if hbm else "fallback"
+    hbm = hbm or 6650.0
+    ach = kbytes[dom] * B / (kms[dom] / 1e3) / 1e9
+    traffic = None
+    tr = load_traffic()
+    if tr and names[dom] in tr.get("dram_bytes_per_slice", {}):
+        traffic = tr["dram_bytes_per_slice"][names[dom]] * B
+    roofline = {"bound": "hbm", "kernel": names[dom], "achieved": ach, "peak": hbm,
+                "unit": "GB/s", "frac": ach / hbm, "traffic": traffic,
+                "peak_source": peak_src,
+                "algorithmic_bytes_per_launch": kbytes[dom] * B}
+    rt_ach = RT_BYTES * B / (ms_step / 1e3) / 1e9
+    pipeline = {"achieved": rt_ach, "peak": hbm, "unit": "GB/s", "frac": rt_ach / hbm,
+                "algorithmic_bytes_per_step": RT_BYTES * B}
+    kernels = {nm: {"ms": kms[i], "share": kms[i] / sum(kms),
+                    "algorithmic_gbs": kbytes[i] * B / (kms[i] / 1e3) / 1e9}
+               for i, nm in enumerate(names)}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "round_trips/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "FusedOctCQT round trip (analysis + synthesis), "
+                               "OctCQT([3,4,2],[8,16,32]) fs 44100, 65536-sample "
+                               "N(0,1) slices, CUDA-graph replay (config 4)",
+                   "global_batch": B * world, "per_gpu_batch": B, "seq_len": N,
+                   "parallelism": f"batch-sharded x{world}, no communication",
+                   "l2": "inputs larger than L2 (x %d MiB, coefficients %d MiB per GPU)"
+                         % (B * N * 4 >> 20, B * eng.ncoef * 8 >> 20)},
+        "round_trip_snr_db": rt_db,
+        "gpu_launches": 4 * K,
+        "roofline": roofline,
+        "pipeline_roofline": pipeline,
+        "kernels": kernels,
+        "clocks": clk.summary(),
+    }
+
+    if not args.no_extras:
+        line.update(extras(args, eng, t, dev, world, rank, barrier, W, K))
+        if world == 1 and rank == 0:
+            from oracle.cpu_port import time_round_trips
+            r = time_round_trips(batch=16, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = {
+                "value": r["round_trips_per_s"], "unit": "round_trips/s",
+                "cores": r["threads"], "kind": "port",
+                "sample": "%d calls of a 16-slice round trip (~%.0f s) on %s, torch CPU "
+                          "float32 restatement of OctCQT.fwd/bwd, %.1f dB"
+                          % (r["calls"], args.cpu_seconds, r["cpu"], r["snr_db"])}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def extras(args, eng, t, dev, world, rank, barrier, W, K):
+    """e2e through the public API, the batch sweep and the train step."""
+    import torch
+    from flash_cqt_b200 import FusedOctCQT, Graphed
+    out = {}
+    B = args.batch
+    # ---- e2e: pinned host buffers, H2D + graphed FusedOctCQT round trip + D2H
+    f = FusedOctCQT(t.cqt, dev)
+    xh = torch.randn(B, N).pin_memory()
+    yh = torch.empty(B, N).pin_memory()
+    xd = torch.empty(B, N, device=dev)
+    gr = Graphed(lambda inp: f.bwd(*f.fwd(inp)), xd)
+    xin = gr.static_inputs[0]
+    for _ in range(W):
+        xin.copy_(xh, non_blocking=True)
+        yh.copy_(gr.run(), non_blocking=True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        xin.copy_(xh, non_blocking=True)
+        yh.copy_(gr.run(), non_blocking=True)
+    e1.record()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    out["e2e"] = {"value": world * B * K / (ms / 1e3), "unit": "round_trips/s",
+                  "h2d_bytes_per_step": B * N * 4, "d2h_bytes_per_step": B * N * 4,
+                  "api": "Graphed(FusedOctCQT.fwd -> .bwd) with pinned host x / y"}
+    del gr, f
+    # ---- batch sweep (config 2 is B = 1), graphed, per GPU
+    sweep = {}
+    for Bs in (1, 4, 16, 64, 256, 1024):
+        xs = torch.randn(Bs, N, device=dev)
+        cs = torch.empty(Bs, eng.ncoef, dtype=torch.complex64, device=dev)
+        ys = torch.empty(Bs, N, device=dev)
+
+        def rt():
+            eng.analysis(xs, out=cs)
+            eng.synthesis(cs, out=ys)
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                rt()
+        torch.cuda.current_stream().wait_stream(s)
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg):
+            rt()
+        reps = 50 if Bs <= 64 else 10
+        ts = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            gg.replay()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        med = statistics.median(ts)
+        sweep[str(Bs)] = {"ms": med, "round_trips_per_s": Bs / (med / 1e3)}
+        del gg
+    out["sweep_per_gpu"] = sweep
+    # ---- train step, batch 16: analysis -> synthesis -> MSE -> backward
+    Bt = 16
+    gx = torch.Generator(device=dev).manual_seed(2)
+    xt = torch.randn(Bt, N, device=dev, generator=gx)
+    tgt = torch.randn(Bt, N, device=dev, generator=torch.Generator(device=dev).manual_seed(3))
+
+    def step():
+        xg = xt.clone().requires_grad_(True)
+        yy = t.bwd(*t.fwd(xg))
+        ((yy - tgt) ** 2).mean().backward()
+        return xg.grad
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(max(K, 20)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    out["train_step_ms_b16"] = statistics.median(ts)
+    return out
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,13 @@
+"""B200-native (sm_100a) factored constant-Q transform.
+
+Drop-in for the Flash-CQT API: ``OctCQT``, ``FusedOctCQT``, ``TrainableCQT``,
+``SlicedCQT`` and ``Graphed``, all running on hand-written CUDA kernels behind
+the C ABI of ``include/flash_cqt_b200.h``.
+"""
+from .oct_cqt import OctCQT
+from .sliced import SlicedCQT
+from .graphed import Graphed
+from .fused import FusedOctCQT
+from .trainable import TrainableCQT
+
+__all__ = ["OctCQT", "SlicedCQT", "Graphed", "FusedOctCQT", "TrainableCQT"]

@@ -1,0 +1,173 @@
+"""ctypes binding of ``libflashcqt_b200.so`` (C ABI in include/flash_cqt_b200.h).
+
+The shared library is built in-tree by ``flash_cqt_b200.build`` (or by
+``__graft_entry__.build()``).  There is no fallback: if the library is missing
+or a call fails, a ``RuntimeError`` carrying the library's own message is
+raised.
+"""
+import ctypes
+import pathlib
+import threading
+
+import numpy as np
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libflashcqt_b200.so"
+
+CQT_LAYOUT_PLANAR = 0
+CQT_LAYOUT_COMPLEX = 1
+
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+
+class HostTables(ctypes.Structure):
+    _fields_ = [
+        ("nbands", ctypes.c_int32), ("ncoef", ctypes.c_int32),
+        ("band_off", _i32p), ("band_list", _i32p),
+        ("nclasses", ctypes.c_int32),
+        ("class_len", _i32p), ("class_count", _i32p), ("class_first", _i32p),
+        ("an_src", _i32p), ("an_gain", _f32p),
+        ("as_src", _i32p), ("as_gain", _f32p),
+        ("sy_dest", _i32p), ("sy_gre", _f32p), ("sy_gim", _f32p),
+        ("sy_mask", _u8p), ("sy_nplanes", ctypes.c_int32),
+        ("aa_dest", _i32p), ("aa_gre", _f32p), ("aa_gim", _f32p),
+        ("aa_mask", _u8p), ("aa_nplanes", ctypes.c_int32),
+        ("tw2048", _f32p), ("tw_hi", _f32p), ("tw_lo", _f32p),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib():
+    """Load the shared library once; raise if it has not been built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH.name} is not built; run `python -m "
+                    "flash_cqt_b200.build` (needs nvcc) -- there is no CPU "
+                    "fallback for the CUDA transform")
+            L = ctypes.CDLL(str(LIB_PATH))
+            vp, sz, ci = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+            L.cqt_version.restype = ci
+            L.cqt_last_error.restype = ctypes.c_char_p
+            L.cqt_tables_upload.argtypes = [ctypes.POINTER(HostTables), ci,
+                                            ctypes.POINTER(vp)]
+            L.cqt_tables_upload.restype = ci
+            L.cqt_tables_free.argtypes = [vp]
+            L.cqt_tables_free.restype = ci
+            L.cqt_ncoef.argtypes = [vp]
+            L.cqt_ncoef.restype = ctypes.c_int32
+            L.cqt_workspace_bytes.argtypes = [vp, ci]
+            L.cqt_workspace_bytes.restype = sz
+            for name in ("cqt_analysis", "cqt_synthesis", "cqt_adj_analysis",
+                         "cqt_adj_synthesis"):
+                fn = getattr(L, name)
+                if name in ("cqt_analysis", "cqt_adj_synthesis"):
+                    fn.argtypes = [vp, vp, vp, vp, ci, ci, vp, sz, vp]
+                else:
+                    fn.argtypes = [vp, vp, vp, ci, vp, ci, vp, sz, vp]
+                fn.restype = ci
+            L.cqt_launch_stage.argtypes = [vp, ci, vp, vp, vp, vp, ci, ci, vp, sz, vp]
+            L.cqt_launch_stage.restype = ci
+            _lib = L
+    return _lib
+
+
+def exported_symbols():
+    """Names the C header declares (checked by the CPU tests)."""
+    return ["cqt_tables_upload", "cqt_tables_free", "cqt_ncoef",
+            "cqt_workspace_bytes", "cqt_analysis", "cqt_synthesis",
+            "cqt_adj_analysis", "cqt_adj_synthesis", "cqt_launch_stage",
+            "cqt_last_error", "cqt_version"]
+
+
+def _check(rc, what):
+    if rc != 0:
+        msg = lib().cqt_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({rc}): {msg}")
+
+
+def _ptr(a, ctype):
+    return a.ctypes.data_as(ctypes.POINTER(ctype))
+
+
+class DeviceTables:
+    """Device-resident copy of the host tables (owns the cqt_tables handle)."""
+
+    def __init__(self, tabs, device_index):
+        L = lib()
+        keep = []
+
+        def arr(a, dt, ct):
+            a = np.ascontiguousarray(a, dtype=dt)
+            keep.append(a)
+            return _ptr(a, ct)
+
+        cls = tabs["classes"]
+        h = HostTables()
+        h.nbands = len(tabs["band_off"])
+        h.ncoef = len(tabs["fwd"]["analysis"][0])
+        h.band_off = arr(tabs["band_off"], np.int32, ctypes.c_int32)
+        h.band_list = arr(tabs["band_list"], np.int32, ctypes.c_int32)
+        h.nclasses = len(cls)
+        h.class_len = arr([c[0] for c in cls], np.int32, ctypes.c_int32)
+        h.class_count = arr([c[1] for c in cls], np.int32, ctypes.c_int32)
+        h.class_first = arr([c[2] for c in cls], np.int32, ctypes.c_int32)
+        src, gain = tabs["fwd"]["analysis"]
+        h.an_src = arr(src, np.int32, ctypes.c_int32)
+        h.an_gain = arr(gain, np.float32, ctypes.c_float)
+        src, gain = tabs["fwd"]["adj_synth"]
+        h.as_src = arr(src, np.int32, ctypes.c_int32)
+        h.as_gain = arr(gain, np.float32, ctypes.c_float)
+        d, gr, gi, mk, npl = tabs["inv"]["synth"]
+        h.sy_dest = arr(d, np.int32, ctypes.c_int32)
+        h.sy_gre = arr(gr, np.float32, ctypes.c_float)
+        h.sy_gim = arr(gi, np.float32, ctypes.c_float)
+        h.sy_mask = arr(mk, np.uint8, ctypes.c_uint8)
+        h.sy_nplanes = npl
+        d, gr, gi, mk, npl = tabs["inv"]["adj_an"]
+        h.aa_dest = arr(d, np.int32, ctypes.c_int32)
+        h.aa_gre = arr(gr, np.float32, ctypes.c_float)
+        h.aa_gim = arr(gi, np.float32, ctypes.c_float)
+        h.aa_mask = arr(mk, np.uint8, ctypes.c_uint8)
+        h.aa_nplanes = npl
+        h.tw2048 = arr(tabs["tw2048"], np.float32, ctypes.c_float)
+        h.tw_hi = arr(tabs["tw_hi"], np.float32, ctypes.c_float)
+        h.tw_lo = arr(tabs["tw_lo"], np.float32, ctypes.c_float)
+        handle = ctypes.c_void_p()
+        _check(L.cqt_tables_upload(ctypes.byref(h), int(device_index),
+                                   ctypes.byref(handle)), "cqt_tables_upload")
+        self.handle = handle
+        self.device_index = int(device_index)
+        self.ncoef = int(L.cqt_ncoef(handle))
+
+    def workspace_bytes(self, batch):
+        return int(lib().cqt_workspace_bytes(self.handle, int(batch)))
+
+    def call(self, name, a, b, c, layout, batch, ws, ws_bytes, stream):
+        fn = getattr(lib(), name)
+        if name in ("cqt_analysis", "cqt_adj_synthesis"):
+            rc = fn(self.handle, a, b, c, layout, int(batch), ws, ws_bytes, stream)
+        else:
+            rc = fn(self.handle, a, b, layout, c, int(batch), ws, ws_bytes, stream)
+        _check(rc, name)
+
+    def stage(self, stage, sig_in, sig_out, c_re, c_im, layout, batch, ws,
+              ws_bytes, stream):
+        _check(lib().cqt_launch_stage(self.handle, int(stage), sig_in, sig_out,
+                                      c_re, c_im, layout, int(batch), ws,
+                                      ws_bytes, stream), "cqt_launch_stage")
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and _lib is not None:
+            try:
+                _lib.cqt_tables_free(h)
+            except Exception:
+                pass
+            self.handle = None

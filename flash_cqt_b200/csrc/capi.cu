@@ -1,0 +1,343 @@
+// C ABI (include/flash_cqt_b200.h): table upload and the four stream-ordered
+// entry points.  Each entry point validates its arguments, launches two
+// kernels on the caller's stream and reports launch errors; none allocates
+// or synchronises.
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/flash_cqt_b200.h"
+#include "engine.cuh"
+#include "internal.h"
+
+namespace fcqt {
+cudaError_t init_spectrum_attributes();
+cudaError_t init_band_attributes();
+}  // namespace fcqt
+
+using namespace fcqt;
+
+struct cqt_tables {
+    int device;
+    int ncoef;
+    int nbands;
+    int ncls;
+    int cls_M[kMaxClasses], cls_nb[kMaxClasses], cls_first[kMaxClasses];
+    FwdTab fwd[2];   // 0 analysis, 1 transpose of synthesis
+    InvTab inv[2];   // 0 synthesis, 1 transpose of analysis
+    BandCommon bc;
+    const float2* tw_hi;
+    const float2* tw_lo;
+    int max_planes;
+    void* blob;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* msg) {
+    g_err = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+    char buf[512];
+    std::snprintf(buf, sizeof buf, "%s: %s", where, cudaGetErrorString(e));
+    g_err = buf;
+    return CQT_ERR_CUDA;
+}
+
+int check_device(const cqt_tables* t) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev != t->device) {
+        char buf[160];
+        std::snprintf(buf, sizeof buf,
+                      "tables live on device %d but device %d is current", t->device, dev);
+        g_err = buf;
+        return CQT_ERR_DEVICE;
+    }
+    return CQT_OK;
+}
+
+size_t ws_need(const cqt_tables* t, int batch) {
+    return (size_t)batch * (size_t)t->max_planes * kPlaneStride * sizeof(float2);
+}
+
+int check_common(const cqt_tables* t, int batch, void* ws, size_t ws_bytes, int layout) {
+    if (!t) return fail(CQT_ERR_ARG, "null tables");
+    if (batch < 0) return fail(CQT_ERR_ARG, "negative batch");
+    if (layout != CQT_LAYOUT_PLANAR && layout != CQT_LAYOUT_COMPLEX)
+        return fail(CQT_ERR_ARG, "unknown coefficient layout");
+    if (batch > 0 && (!ws || ws_bytes < ws_need(t, batch)))
+        return fail(CQT_ERR_ARG, "workspace missing or smaller than cqt_workspace_bytes");
+    if (((uintptr_t)ws & 15u) != 0) return fail(CQT_ERR_ARG, "workspace not 16-byte aligned");
+    return check_device(t);
+}
+
+int coef_ptr(const float* re, const float* im, int layout, CoefPtr* out) {
+    if (!re) return fail(CQT_ERR_ARG, "null coefficient pointer");
+    if (layout == CQT_LAYOUT_PLANAR && !im)
+        return fail(CQT_ERR_ARG, "planar layout needs both coefficient planes");
+    if (layout == CQT_LAYOUT_COMPLEX && ((uintptr_t)re & 7u))
+        return fail(CQT_ERR_ARG, "complex coefficient array not 8-byte aligned");
+    out->re = const_cast<float*>(re);
+    out->im = const_cast<float*>(im);
+    out->interleaved = layout == CQT_LAYOUT_COMPLEX;
+    return CQT_OK;
+}
+
+BandSched sched(const cqt_tables* t, int batch) {
+    return make_sched(t->ncls, t->cls_M, t->cls_nb, t->cls_first, batch);
+}
+
+// one analysis-engine pass: real signal -> spectrum -> bands
+int run_fwd_engine(const cqt_tables* t, int which, const float* sig, CoefPtr out,
+                   int batch, void* ws, cudaStream_t s) {
+    if (batch == 0) return CQT_OK;
+    float2* X = static_cast<float2*>(ws);
+    cudaError_t e = launch_spectrum_fwd(sig, X, t->tw_hi, t->tw_lo, batch, s);
+    if (e != cudaSuccess) return cuda_fail(e, "spectrum_fwd launch");
+    e = launch_bands_fwd(X, t->fwd[which], t->bc, sched(t, batch), out, s);
+    if (e != cudaSuccess) return cuda_fail(e, "bands_fwd launch");
+    return CQT_OK;
+}
+
+// one synthesis-engine pass: bands -> colour planes -> real signal
+int run_inv_engine(const cqt_tables* t, int which, CoefPtr in, float* sig, int batch,
+                   void* ws, cudaStream_t s) {
+    if (batch == 0) return CQT_OK;
+    float2* E = static_cast<float2*>(ws);
+    cudaError_t e = launch_bands_inv(in, t->inv[which], t->bc, sched(t, batch), E, s);
+    if (e != cudaSuccess) return cuda_fail(e, "bands_inv launch");
+    e = launch_spectrum_inv(E, t->inv[which], sig, t->tw_hi, t->tw_lo, batch, s);
+    if (e != cudaSuccess) return cuda_fail(e, "spectrum_inv launch");
+    return CQT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cqt_version(void) { return 100; }
+
+const char* cqt_last_error(void) { return g_err.c_str(); }
+
+int32_t cqt_ncoef(const cqt_tables* t) { return t ? t->ncoef : -1; }
+
+size_t cqt_workspace_bytes(const cqt_tables* t, int batch) {
+    if (!t || batch < 0) return 0;
+    return ws_need(t, batch);
+}
+
+int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
+    if (!h || !out) return fail(CQT_ERR_ARG, "null argument");
+    *out = nullptr;
+    if (h->nclasses < 1 || h->nclasses > kMaxClasses)
+        return fail(CQT_ERR_ARG, "class count out of range");
+    if (h->sy_nplanes < 1 || h->sy_nplanes > kMaxPlanes || h->aa_nplanes < 1 ||
+        h->aa_nplanes > kMaxPlanes)
+        return fail(CQT_ERR_ARG, "plane count out of range");
+    if (h->ncoef <= 0 || h->nbands <= 0) return fail(CQT_ERR_ARG, "empty tables");
+    for (int c = 0; c < h->nclasses; ++c) {
+        const int M = h->class_len[c];
+        if (M < 32 || M > 2048 || (M & (M - 1)))
+            return fail(CQT_ERR_ARG, "block length must be a power of two in 32..2048");
+    }
+    // host-side bounds check of every table index, so no kernel can read or
+    // write outside its buffers whatever tables it is handed
+    const int nc = h->ncoef;
+    for (int b = 0; b < h->nbands; ++b) {
+        if (h->band_list[b] < 0 || h->band_list[b] >= h->nbands)
+            return fail(CQT_ERR_ARG, "band_list entry out of range");
+        if (h->band_off[b] < 0 || h->band_off[b] > nc)
+            return fail(CQT_ERR_ARG, "band offset out of range");
+    }
+    for (int c = 0; c < h->nclasses; ++c) {
+        const int M = h->class_len[c];
+        if (h->class_first[c] < 0 || h->class_first[c] + h->class_count[c] > h->nbands)
+            return fail(CQT_ERR_ARG, "class range out of band_list");
+        for (int i = 0; i < h->class_count[c]; ++i)
+            if (h->band_off[h->band_list[h->class_first[c] + i]] + M > nc)
+                return fail(CQT_ERR_ARG, "band runs past the heap");
+    }
+    for (int i = 0; i < nc; ++i) {
+        for (const int32_t* s : {h->an_src, h->as_src})
+            if (s[i] >= 0 && ((s[i] & 0xFFFF) > kHalf || (s[i] & ~0x1FFFF)))
+                return fail(CQT_ERR_ARG, "gather bin out of range");
+        if (h->sy_dest[i] >= h->sy_nplanes * kPlaneStride ||
+            h->aa_dest[i] >= h->aa_nplanes * kPlaneStride ||
+            (h->sy_dest[i] >= 0 && h->sy_dest[i] % kPlaneStride > kHalf) ||
+            (h->aa_dest[i] >= 0 && h->aa_dest[i] % kPlaneStride > kHalf))
+            return fail(CQT_ERR_ARG, "scatter slot out of range");
+    }
+
+    for (int q = 0; q < kPlaneStride; ++q)
+        if ((h->sy_mask[q] >> h->sy_nplanes) || (h->aa_mask[q] >> h->aa_nplanes) ||
+            (q > kHalf && (h->sy_mask[q] | h->aa_mask[q])))
+            return fail(CQT_ERR_ARG, "plane mask names a plane or bin out of range");
+
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+
+    // one blob: [int32 arrays][float arrays][uint8 masks][float2 twiddles]
+    struct Part { const void* src; size_t bytes; size_t off; };
+    std::vector<Part> parts;
+    size_t total = 0;
+    auto add = [&](const void* p, size_t bytes) {
+        total = (total + 255) & ~(size_t)255;
+        parts.push_back({p, bytes, total});
+        total += bytes;
+        return parts.size() - 1;
+    };
+    const size_t nI = (size_t)nc * 4, nB = (size_t)h->nbands * 4;
+    const size_t maskB = (size_t)kPlaneStride;
+    size_t i_boff = add(h->band_off, nB), i_blist = add(h->band_list, nB);
+    size_t i_ans = add(h->an_src, nI), i_ang = add(h->an_gain, nI);
+    size_t i_ass = add(h->as_src, nI), i_asg = add(h->as_gain, nI);
+    size_t i_syd = add(h->sy_dest, nI), i_syr = add(h->sy_gre, nI), i_syi = add(h->sy_gim, nI);
+    size_t i_sym = add(h->sy_mask, maskB);
+    size_t i_aad = add(h->aa_dest, nI), i_aar = add(h->aa_gre, nI), i_aai = add(h->aa_gim, nI);
+    size_t i_aam = add(h->aa_mask, maskB);
+    size_t i_tw = add(h->tw2048, 2048 * 8), i_hi = add(h->tw_hi, 256 * 8), i_lo = add(h->tw_lo, 256 * 8);
+
+    void* blob = nullptr;
+    e = cudaMalloc(&blob, total);
+    if (e != cudaSuccess) {
+        cudaSetDevice(prev);
+        return cuda_fail(e, "cudaMalloc(tables)");
+    }
+    for (const Part& p : parts) {
+        e = cudaMemcpy(static_cast<char*>(blob) + p.off, p.src, p.bytes, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(blob);
+            cudaSetDevice(prev);
+            return cuda_fail(e, "cudaMemcpy(tables)");
+        }
+    }
+    e = init_spectrum_attributes();
+    if (e == cudaSuccess) e = init_band_attributes();
+    if (e != cudaSuccess) {
+        cudaFree(blob);
+        cudaSetDevice(prev);
+        return cuda_fail(e, "cudaFuncSetAttribute");
+    }
+
+    auto P = [&](size_t i) { return static_cast<char*>(blob) + parts[i].off; };
+    cqt_tables* t = new cqt_tables{};
+    t->device = device;
+    t->ncoef = nc;
+    t->nbands = h->nbands;
+    t->ncls = h->nclasses;
+    for (int c = 0; c < h->nclasses; ++c) {
+        t->cls_M[c] = h->class_len[c];
+        t->cls_nb[c] = h->class_count[c];
+        t->cls_first[c] = h->class_first[c];
+    }
+    t->fwd[0] = FwdTab{(const int*)P(i_ans), (const float*)P(i_ang)};
+    t->fwd[1] = FwdTab{(const int*)P(i_ass), (const float*)P(i_asg)};
+    t->inv[0] = InvTab{(const int*)P(i_syd), (const float*)P(i_syr), (const float*)P(i_syi),
+                       (const unsigned char*)P(i_sym), h->sy_nplanes};
+    t->inv[1] = InvTab{(const int*)P(i_aad), (const float*)P(i_aar), (const float*)P(i_aai),
+                       (const unsigned char*)P(i_aam), h->aa_nplanes};
+    t->bc = BandCommon{(const int*)P(i_blist), (const int*)P(i_boff), (const float2*)P(i_tw), nc};
+    t->tw_hi = (const float2*)P(i_hi);
+    t->tw_lo = (const float2*)P(i_lo);
+    t->max_planes = h->sy_nplanes > h->aa_nplanes ? h->sy_nplanes : h->aa_nplanes;
+    t->blob = blob;
+    *out = t;
+    if (prev >= 0) cudaSetDevice(prev);
+    return CQT_OK;
+}
+
+int cqt_tables_free(cqt_tables* t) {
+    if (!t) return CQT_OK;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(t->device);
+    cudaError_t e = cudaFree(t->blob);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete t;
+    return e == cudaSuccess ? CQT_OK : cuda_fail(e, "cudaFree(tables)");
+}
+
+int cqt_analysis(const cqt_tables* t, const float* x, float* c_re, float* c_im, int layout,
+                 int batch, void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_common(t, batch, ws, ws_bytes, layout);
+    if (rc) return rc;
+    if (batch && !x) return fail(CQT_ERR_ARG, "null input");
+    CoefPtr out;
+    if (batch && (rc = coef_ptr(c_re, c_im, layout, &out))) return rc;
+    return run_fwd_engine(t, 0, x, out, batch, ws, static_cast<cudaStream_t>(stream));
+}
+
+int cqt_adj_synthesis(const cqt_tables* t, const float* gy, float* g_re, float* g_im,
+                      int layout, int batch, void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_common(t, batch, ws, ws_bytes, layout);
+    if (rc) return rc;
+    if (batch && !gy) return fail(CQT_ERR_ARG, "null input");
+    CoefPtr out;
+    if (batch && (rc = coef_ptr(g_re, g_im, layout, &out))) return rc;
+    return run_fwd_engine(t, 1, gy, out, batch, ws, static_cast<cudaStream_t>(stream));
+}
+
+int cqt_synthesis(const cqt_tables* t, const float* c_re, const float* c_im, int layout,
+                  float* y, int batch, void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_common(t, batch, ws, ws_bytes, layout);
+    if (rc) return rc;
+    if (batch && !y) return fail(CQT_ERR_ARG, "null output");
+    CoefPtr in;
+    if (batch && (rc = coef_ptr(c_re, c_im, layout, &in))) return rc;
+    return run_inv_engine(t, 0, in, y, batch, ws, static_cast<cudaStream_t>(stream));
+}
+
+int cqt_adj_analysis(const cqt_tables* t, const float* g_re, const float* g_im, int layout,
+                     float* gx, int batch, void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_common(t, batch, ws, ws_bytes, layout);
+    if (rc) return rc;
+    if (batch && !gx) return fail(CQT_ERR_ARG, "null output");
+    CoefPtr in;
+    if (batch && (rc = coef_ptr(g_re, g_im, layout, &in))) return rc;
+    return run_inv_engine(t, 1, in, gx, batch, ws, static_cast<cudaStream_t>(stream));
+}
+
+int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float* sig_out,
+                     float* c_re, float* c_im, int layout, int batch, void* ws,
+                     size_t ws_bytes, void* stream) {
+    int rc = check_common(t, batch, ws, ws_bytes, layout);
+    if (rc) return rc;
+    if (batch == 0) return CQT_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    CoefPtr cp;
+    switch (stage) {
+    case 0:
+        if (!sig_in) return fail(CQT_ERR_ARG, "null input");
+        e = launch_spectrum_fwd(sig_in, static_cast<float2*>(ws), t->tw_hi, t->tw_lo, batch, s);
+        break;
+    case 1:
+        if ((rc = coef_ptr(c_re, c_im, layout, &cp))) return rc;
+        e = launch_bands_fwd(static_cast<const float2*>(ws), t->fwd[0], t->bc, sched(t, batch),
+                             cp, s);
+        break;
+    case 2:
+        if ((rc = coef_ptr(c_re, c_im, layout, &cp))) return rc;
+        e = launch_bands_inv(cp, t->inv[0], t->bc, sched(t, batch), static_cast<float2*>(ws), s);
+        break;
+    case 3:
+        if (!sig_out) return fail(CQT_ERR_ARG, "null output");
+        e = launch_spectrum_inv(static_cast<const float2*>(ws), t->inv[0], sig_out, t->tw_hi,
+                                t->tw_lo, batch, s);
+        break;
+    default:
+        return fail(CQT_ERR_ARG, "unknown stage");
+    }
+    return e == cudaSuccess ? CQT_OK : cuda_fail(e, "stage launch");
+}
+
+}  // extern "C"

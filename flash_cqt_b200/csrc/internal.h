@@ -1,0 +1,62 @@
+// Internal declarations shared by the kernel files and the C-ABI layer.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace fcqt {
+
+struct FwdTab {            // analysis-engine tap table (one per use)
+    const int* src;        // bin | conj << 16, or -1 for a zero tap
+    const float* gain;     // window gain with all constants folded in
+};
+
+struct InvTab {            // synthesis-engine tap table (one per use)
+    const int* dest;       // plane * kPlaneStride + bin, or -1
+    const float* gre;      // gain on the real part
+    const float* gim;      // gain on the imaginary part
+    const unsigned char* mask;  // per bin: bit p set when plane p holds a term
+    int nplanes;
+};
+
+constexpr int kMaxClasses = 8;
+
+struct BandSched {         // CTA ranges of the block-length classes for one launch
+    int ncls;
+    int M[kMaxClasses];
+    int nb[kMaxClasses];       // bands in the class
+    int first[kMaxClasses];    // first entry of the class in band_list
+    int cta0[kMaxClasses + 1]; // first CTA of each class, cta0[ncls] = grid
+    int batch;
+};
+
+struct BandCommon {
+    const int* band_list;  // band ids grouped by class
+    const int* band_off;   // heap offset of every band
+    const float2* tw2048;  // W_2048^e, forward sign
+    int ncoef;
+};
+
+struct CoefPtr {           // coefficient heap addressing
+    float* re;             // planar: real plane; interleaved: complex base
+    float* im;             // planar: imaginary plane; interleaved: unused
+    int interleaved;       // 0 planar [B, ncoef] x 2, 1 complex [B, ncoef]
+};
+
+constexpr int kBandThreads = 256;
+constexpr int kBandCap = 8192;            // points per band CTA
+constexpr int kSpecThreads = 512;
+
+BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, int batch);
+
+cudaError_t init_kernel_attributes();
+cudaError_t launch_spectrum_fwd(const float* x, float2* X, const float2* tw_hi,
+                                const float2* tw_lo, int batch, cudaStream_t s);
+cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, float* y,
+                                const float2* tw_hi, const float2* tw_lo,
+                                int batch, cudaStream_t s);
+cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandCommon& bc,
+                             const BandSched& sc, CoefPtr out, cudaStream_t s);
+cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, const BandCommon& bc,
+                             const BandSched& sc, float2* E, cudaStream_t s);
+
+}  // namespace fcqt

@@ -1,0 +1,176 @@
+"""Streamable sliced CQT: 50%-overlap Tukey slices through the per-slice engine.
+
+Drop-in for ``flash_cqt/sliced.py:41-209`` (``SlicedCQT``): same constructor,
+``fwd`` / ``bwd`` / ``stream_fwd`` / ``stream_bwd`` and latency helpers, and
+the same plugin point -- ``self.cqt`` is any object with OctCQT-shaped
+``fwd(sl[..., sl_len]) -> (blocks, side)`` and ``bwd(blocks, side)``.  The
+default engine is this package's ``OctCQT``, i.e. the B200 kernels.
+
+Slicing (sliced.py:102-117): pad 2H in front, cut 4H windows every 2H, apply
+the Tukey window, roll even slices by -H and odd ones by +H.  The coefficient
+arrangement (sliced.py:119-146) rolls each octave block by +-M/4 per parity
+and lays slices out along the time axis; ``bwd`` undoes both and overlap-adds
+(sliced.py:148-167).
+"""
+import math
+
+import torch
+
+from .layout import periodic_hann
+from .oct_cqt import OctCQT
+
+
+def makewnd(sl_len, tr_area, device="cpu", dtype=torch.float32):
+    """Tukey slice window: zero, Hann rise centred at sl_len/4, flat top, Hann
+    fall centred at 3 sl_len/4, zero (sliced.py:26-38)."""
+    hhop = sl_len // 4
+    htr = tr_area // 2
+    w = torch.as_tensor(periodic_hann(2 * tr_area))
+    tw = torch.zeros(sl_len, dtype=torch.float64)
+    tw[hhop - htr:hhop + htr] = w[tr_area:]
+    tw[hhop + htr:3 * hhop - htr] = 1.0
+    tw[3 * hhop - htr:3 * hhop + htr] = w[:tr_area]
+    return tw.to(dtype).to(device)
+
+
+class SlicedCQT:
+    def __init__(self, num_octs=[3, 4, 2], bins_per_oct=[8, 16, 32], fs=44100,
+                 sl_len=65536, tr_area=None, device="cuda", dtype=torch.float32):
+        if sl_len % 4:
+            raise ValueError("sl_len must be a multiple of 4")
+        if tr_area is None:
+            tr_area = sl_len // 4
+        if tr_area % 2 or not 0 < 2 * tr_area <= sl_len:
+            raise ValueError("tr_area must be even and 0 < 2 tr_area <= sl_len")
+        self.fs = fs
+        self.sl_len = sl_len
+        self.tr_area = tr_area
+        self.H = sl_len // 4
+        self.hop = sl_len // 2
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.cqt = OctCQT(num_octs, bins_per_oct, fs=fs, audio_len=sl_len,
+                          device=device, dtype=dtype)
+        self.oct_bins = self.cqt.oct_bins
+        self.size_per_oct = self.cqt.size_per_oct
+        self.frqs_hz = self.cqt.frqs_hz
+        self.tw = makewnd(sl_len, tr_area, device=device, dtype=dtype)
+        self._roll = [m // 4 for m in self.size_per_oct]
+
+    # latency helpers (sliced.py:71-98)
+    def latency_ms(self, sl_len=None):
+        return 1000.0 * (sl_len if sl_len is not None else self.sl_len) / self.fs
+
+    def lowest_fmin(self, sl_len=None):
+        sl = sl_len if sl_len is not None else self.sl_len
+        n0 = 1
+        while n0 < len(self.oct_bins) and self.oct_bins[n0] == self.oct_bins[0]:
+            n0 += 1
+        b0 = self.oct_bins[0]
+        ratio = 2.0 ** ((n0 + 1) / ((n0 + 1) * b0 - 1))
+        q0 = math.sqrt(ratio) / (ratio - 1.0) / 2.0
+        return 8.0 * self.fs * q0 / sl
+
+    def latency_table(self, sl_lens=(8192, 16384, 32768, 65536, 131072)):
+        need = float(self.frqs_hz[0])
+        lines = [f"{'sl_len':>8} {'latency_ms':>11} {'lowest_fmin_hz':>15}   "
+                 f"covers fmin {need:.1f} hz"]
+        for sl in sl_lens:
+            fmin = self.lowest_fmin(sl)
+            lines.append(f"{sl:>8} {self.latency_ms(sl):>11.1f} {fmin:>15.1f}   "
+                         f"{'yes' if fmin <= need else 'no'}")
+        return "\n".join(lines)
+
+    # slicing
+    def _num_slices(self, L):
+        nb = -(-L // self.H)
+        return (nb + 1) // 2 + 1
+
+    def _slice(self, x):
+        B, C, L = x.shape
+        H = self.H
+        S = self._num_slices(L)
+        nb = -(-L // H)
+        xp = torch.nn.functional.pad(x, (2 * H, nb * H - L + 3 * H))
+        sl = xp.unfold(-1, 4 * H, 2 * H)[:, :, :S, :] * self.tw
+        even = (torch.arange(S, device=x.device) % 2 == 0).view(1, 1, -1, 1)
+        return torch.where(even, torch.roll(sl, -H, -1), torch.roll(sl, H, -1))
+
+    def _arrange(self, blocks, S, fwd):
+        out = []
+        even = (torch.arange(S, device=blocks[0].device) % 2 == 0).view(1, 1, -1, 1, 1)
+        s = 1 if fwd else -1
+        for c, r in zip(blocks, self._roll):
+            out.append(torch.where(even, torch.roll(c, s * r, -1),
+                                   torch.roll(c, -s * r, -1)))
+        return out
+
+    # whole-buffer API
+    def fwd(self, x):
+        """x [B, C, L] real -> (blocks, side); blocks[i] is
+        [B, C, oct_bins[i], S * size_per_oct[i]] complex (slices in time
+        order), side is (dc, nyq) kept per slice, [B, C, S, 1, M]"""
+        B, C, L = x.shape
+        sl = self._slice(x)
+        S = sl.shape[2]
+        blocks, side = self.cqt.fwd(sl)
+        blocks = self._arrange(blocks, S, fwd=True)
+        blocks = [c.permute(0, 1, 3, 2, 4).reshape(B, C, b, S * m)
+                  for c, b, m in zip(blocks, self.oct_bins, self.size_per_oct)]
+        return blocks, side
+
+    def bwd(self, blocks, side=None, length=None):
+        """inverse of fwd; length trims the tail padding"""
+        B, C = blocks[0].shape[:2]
+        S = blocks[0].shape[-1] // self.size_per_oct[0]
+        blocks = [c.reshape(B, C, b, S, m).permute(0, 1, 3, 2, 4)
+                  for c, b, m in zip(blocks, self.oct_bins, self.size_per_oct)]
+        blocks = self._arrange(blocks, S, fwd=False)
+        y = self.cqt.bwd(blocks, side)
+        H = self.H
+        even = (torch.arange(S, device=y.device) % 2 == 0).view(1, 1, -1, 1)
+        y = torch.where(even, torch.roll(y, H, -1), torch.roll(y, -H, -1))
+        out = torch.zeros(B, C, (S + 1) * 2 * H, dtype=y.dtype, device=y.device)
+        out[..., :S * 2 * H] += y[..., :2 * H].reshape(B, C, -1)
+        out[..., 2 * H:] += y[..., 2 * H:].reshape(B, C, -1)
+        out = out[..., 2 * H:]
+        return out if length is None else out[..., :length]
+
+    # streaming API, state of one half slice (sliced.py:171-209)
+    def stream_fwd(self, chunks):
+        """chunks yields [B, C, hop] pieces (pad the last one); yields one
+        (blocks, side) per slice, blocks[i] [B, C, oct_bins[i], M_i]"""
+        prev = None
+        k = 0
+
+        def one(prev, chunk, k):
+            sl = torch.cat([prev, chunk], dim=-1) * self.tw
+            sl = torch.roll(sl, -self.H if k % 2 == 0 else self.H, -1)
+            blocks, side = self.cqt.fwd(sl.unsqueeze(2))
+            blocks = self._arrange(blocks, 1, fwd=(k % 2 == 0))
+            return [c[:, :, 0] for c in blocks], [c[:, :, 0] for c in side]
+
+        for chunk in chunks:
+            if prev is None:
+                prev = torch.zeros_like(chunk)
+            yield one(prev, chunk, k)
+            prev = chunk
+            k += 1
+        if prev is not None:
+            yield one(prev, torch.zeros_like(prev), k)
+
+    def stream_bwd(self, slice_coeffs):
+        """slice_coeffs yields (blocks, side) per slice as stream_fwd emits;
+        yields [B, C, hop] output pieces, one slice behind the input"""
+        tail = None
+        k = 0
+        for blocks, side in slice_coeffs:
+            blocks = [c.unsqueeze(2) for c in blocks]
+            side = [c.unsqueeze(2) for c in side] if side is not None else None
+            blocks = self._arrange(blocks, 1, fwd=not (k % 2 == 0))
+            y = self.cqt.bwd(blocks, side)[:, :, 0]
+            y = torch.roll(y, self.H if k % 2 == 0 else -self.H, -1)
+            if tail is not None:
+                yield tail + y[..., :self.hop]
+            tail = y[..., self.hop:]
+            k += 1

@@ -1,0 +1,120 @@
+"""Differentiable constant-Q transform on the B200 engines.
+
+Drop-in for ``flash_cqt/trainable.py:28-191`` (``TrainableCQT``): the
+transform is linear, so the backward of the analysis is the transpose of the
+analysis (synthesis engine with the analysis window, ``cqt_adj_analysis``) and
+the backward of the synthesis is the transpose of the synthesis (analysis
+engine with the dual window, ``cqt_adj_synthesis``).  Nothing is saved for
+backward.
+
+Differences from the reference, all in the data path, none in the interface:
+the coefficients come out of the kernel already interleaved, so the blocks
+returned by ``fwd`` are zero-copy views of one complex64 heap (the reference
+builds them with ``torch.complex`` copies, trainable.py:146-152), and ``bwd``
+hands such views back to the kernel without a ``torch.cat`` when they are
+still laid out as ``fwd`` produced them.
+"""
+import torch
+
+from .engine import N, Engine
+
+
+class _Analysis(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, eng):
+        ctx.eng = eng
+        return eng.analysis(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.eng.adj_analysis(g.contiguous()), None
+
+
+class _Synthesis(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, c, eng):
+        ctx.eng = eng
+        return eng.synthesis(c)
+
+    @staticmethod
+    def backward(ctx, gy):
+        return ctx.eng.adj_synthesis(gy.contiguous()), None
+
+
+def _engine_for(cqt, device):
+    """One Engine per (filterbank, device), cached on the OctCQT object."""
+    dev = torch.device(device) if device is not None else None
+    cache = cqt.__dict__.setdefault("_b200_engines", {})
+    key = str(dev)
+    if key not in cache:
+        cache[key] = Engine(cqt.heap, dev)
+    return cache[key]
+
+
+class TrainableCQT:
+    """OctCQT-shaped ``fwd`` / ``bwd`` on the CUDA engines, with gradients.
+
+        cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=65536,
+                     device="cuda")
+        t = TrainableCQT(cqt)
+        blocks, side = t.fwd(x)       # x [..., 65536] float32
+        y = t.bwd(blocks, side)       # gradients flow both ways
+    """
+
+    def __init__(self, cqt, device="cuda"):
+        if cqt.nn != N:
+            raise ValueError(f"the CUDA engines are built for {N}-sample slices")
+        self.cqt = cqt
+        self.eng = _engine_for(cqt, device)
+        self.dev = self.eng.dev
+        self.gspec = cqt.heap.gspec
+        self.ncoef = cqt.heap.ncoef
+        self.ngroups = len(cqt.heap.groups)
+
+    def split(self, h, lead):
+        """heap [B, ncoef] complex -> (blocks, side) views with leading dims."""
+        vs = [h[:, off:off + b * M].view(*lead, b, M) for b, M, off in self.gspec]
+        return vs[:self.ngroups], vs[self.ngroups:]
+
+    def fwd(self, x):
+        """x [..., 65536] real -> (blocks, side), complex64, gradients flow."""
+        lead = x.shape[:-1]
+        h = _Analysis.apply(x.reshape(-1, N).contiguous(), self.eng)
+        return self.split(h, lead)
+
+    def heap_of(self, blocks, side=None):
+        """(blocks, side) -> one [B, ncoef] complex64 heap (zero-copy when the
+        blocks are untouched views of one heap, as ``fwd`` returns them)."""
+        allb = list(blocks) + list(side if side is not None else [])
+        lead = allb[0].shape[:-2]
+        B = 1
+        for d in lead:
+            B *= d
+        base = allb[0]._base
+        if (side is not None and len(allb) == len(self.gspec) and base is not None
+                and base.dim() == 2 and base.shape == (B, self.ncoef)
+                and base.dtype == torch.complex64 and base.is_contiguous()
+                and all(c._base is base for c in allb)
+                and all(c.storage_offset() - base.storage_offset() == off
+                        and c.stride()[-1] == 1 and c.stride()[-2] == M
+                        for c, (b, M, off) in zip(allb, self.gspec))):
+            return base
+        parts = [c.reshape(B, -1).to(torch.complex64) for c in allb]
+        if side is None:
+            nside = sum(b * M for b, M, _ in self.gspec[self.ngroups:])
+            parts.append(torch.zeros(B, nside, dtype=torch.complex64,
+                                     device=parts[0].device))
+        return torch.cat(parts, dim=-1)
+
+    def bwd(self, blocks, side=None):
+        """inverse of fwd (side None drops the DC and Nyquist bands)."""
+        lead = blocks[0].shape[:-2]
+        h = self.heap_of(blocks, side)
+        return _Synthesis.apply(h, self.eng).reshape(*lead, N)
+
+    # flat-heap entry points (no per-group views), used by the fused sliced path
+    def analysis_heap(self, x):
+        return _Analysis.apply(x, self.eng)
+
+    def synthesis_heap(self, h):
+        return _Synthesis.apply(h, self.eng)

@@ -1,0 +1,140 @@
+/* flash_cqt_b200.h -- C ABI of the B200 (sm_100a) constant-Q transform engines.
+ *
+ * The reference (Flash-CQT) binds its CUDA code through pybind11 functions that
+ * take torch tensors (flash_cqt/csrc/packedfft.cu:256-262, radix.cu:116-121)
+ * and are JIT-built on first use (flash_cqt/fused.py:39-146).  This library
+ * replaces that boundary with plain pointers, sizes and a CUDA stream:
+ *
+ *   reference entry point(s)                          replaced by
+ *   -----------------------------------------------   ----------------------
+ *   FusedOctCQT.__init__ table build + .to(dev)       cqt_tables_upload
+ *     (fused.py:229-476, trainable.py:39-61)
+ *   trainable.py:75-89   _analysis  = pack + fft3     cqt_analysis
+ *     (packedfft.cu:100-126) + fwd_bands (radix.cu:46-62)
+ *   trainable.py:100-109 _synthesis = zero + inv_bands cqt_synthesis
+ *     (radix.cu:64-91) + inv_tail (packedfft.cu:233-254)
+ *   trainable.py:111-122 _adj_analysis = adj_bands    cqt_adj_analysis
+ *     (radix.cu:93-114) + inv_tail
+ *   trainable.py:124-139 _adj_synthesis = fft3 +      cqt_adj_synthesis
+ *     fwd_bands with the route_b table
+ *   FusedOctCQT._workspace (fused.py:517-523)         cqt_workspace_bytes
+ *
+ * Conventions
+ *   - Every pointer except the host tables of cqt_tables_upload is a device
+ *     pointer on the device the tables were uploaded to; that device must be
+ *     current when an entry point is called.
+ *   - x, y, gx, gy: float32 [batch][65536].
+ *   - coefficients: the heap of one slice is ncoef complex values (octave
+ *     groups lowest first, then the DC and the Nyquist side block, each group
+ *     [bins][M] row-major).  layout CQT_LAYOUT_PLANAR: c_re and c_im are two
+ *     float32 [batch][ncoef] arrays; CQT_LAYOUT_COMPLEX: c_re is an interleaved
+ *     complex64 [batch][ncoef] array and c_im is ignored (may be NULL).
+ *   - workspace: caller-owned device scratch of at least
+ *     cqt_workspace_bytes(t, batch) bytes, 16-byte aligned; it may be reused
+ *     between calls that are ordered on one stream.
+ *   - All entry points are asynchronous on `stream` (a cudaStream_t, NULL =
+ *     legacy default stream), allocate nothing, never synchronise, and may be
+ *     captured into a CUDA graph.  One cqt_tables may serve several streams.
+ *   - Return value: CQT_OK or a negative error code; cqt_last_error() gives a
+ *     message for the calling thread.
+ */
+#ifndef FLASH_CQT_B200_H
+#define FLASH_CQT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CQT_OK 0
+#define CQT_ERR_ARG (-1)    /* bad argument (null pointer, size, layout) */
+#define CQT_ERR_CUDA (-2)   /* CUDA runtime error (launch, allocation, copy) */
+#define CQT_ERR_DEVICE (-3) /* wrong current device or no device */
+
+#define CQT_LAYOUT_PLANAR 0
+#define CQT_LAYOUT_COMPLEX 1
+
+#define CQT_SLICE 65536
+
+/* Host-side tables, built once per filterbank (the Python side builds them in
+ * float64 and rounds once).  Per-tap arrays have ncoef entries in heap order. */
+typedef struct cqt_host_tables {
+    int32_t nbands;
+    int32_t ncoef;
+    const int32_t* band_off;    /* [nbands] heap offset of each band */
+    const int32_t* band_list;   /* [nbands] band ids grouped by class */
+    int32_t nclasses;           /* <= 8 block-length classes, largest first */
+    const int32_t* class_len;   /* [nclasses] block length M (32..2048) */
+    const int32_t* class_count; /* [nclasses] bands in the class */
+    const int32_t* class_first; /* [nclasses] first class entry in band_list */
+    /* analysis-engine tap tables: src = bin | conj << 16, or -1 */
+    const int32_t* an_src;  const float* an_gain;   /* analysis */
+    const int32_t* as_src;  const float* as_gain;   /* transpose of synthesis */
+    /* synthesis-engine tap tables: dest = plane * 32776 + bin, or -1 */
+    const int32_t* sy_dest; const float* sy_gre; const float* sy_gim;
+    const uint8_t* sy_mask; int32_t sy_nplanes;     /* synthesis */
+    const int32_t* aa_dest; const float* aa_gre; const float* aa_gim;
+    const uint8_t* aa_mask; int32_t aa_nplanes;     /* transpose of analysis */
+    const float* tw2048;        /* [2048][2] W_2048^e */
+    const float* tw_hi;         /* [256][2]  W_65536^(256 e) */
+    const float* tw_lo;         /* [256][2]  W_65536^e */
+} cqt_host_tables;
+
+typedef struct cqt_tables cqt_tables; /* device-resident tables (opaque) */
+
+/* Copy the tables to `device` (cudaMalloc + cudaMemcpy, done once). */
+int cqt_tables_upload(const cqt_host_tables* host, int device, cqt_tables** out);
+int cqt_tables_free(cqt_tables* t);
+int32_t cqt_ncoef(const cqt_tables* t);
+
+/* Scratch bytes needed by any entry point at this batch size. */
+size_t cqt_workspace_bytes(const cqt_tables* t, int batch);
+
+/* x [batch][65536] -> coefficient heap (OctCQT.fwd, oct_cqt.py:84-96). */
+int cqt_analysis(const cqt_tables* t, const float* x, float* c_re, float* c_im,
+                 int layout, int batch, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* coefficient heap -> y [batch][65536] (OctCQT.bwd, oct_cqt.py:98-117). */
+int cqt_synthesis(const cqt_tables* t, const float* c_re, const float* c_im,
+                  int layout, float* y, int batch, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* transpose of the analysis: coefficient gradients (dL/dRe, dL/dIm) -> dL/dx. */
+int cqt_adj_analysis(const cqt_tables* t, const float* g_re, const float* g_im,
+                     int layout, float* gx, int batch, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* transpose of the synthesis: dL/dy -> coefficient gradients. */
+int cqt_adj_synthesis(const cqt_tables* t, const float* gy, float* g_re,
+                      float* g_im, int layout, int batch, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Diagnostic: launch one kernel of the pipeline on its own, for per-kernel
+ * timing and profiling.  stage: 0 spectrum_fwd (in = signal, out = workspace
+ * spectrum), 1 bands_fwd analysis (in = workspace spectrum, out = coefficients
+ * c_re/c_im), 2 bands_inv synthesis (in = coefficients, out = workspace
+ * planes), 3 spectrum_inv synthesis (in = workspace planes, out = signal).
+ * Stages 1 and 3 read what stages 0 and 2 left in the workspace. */
+#define CQT_STAGE_SPECTRUM_FWD 0
+#define CQT_STAGE_BANDS_FWD 1
+#define CQT_STAGE_BANDS_INV 2
+#define CQT_STAGE_SPECTRUM_INV 3
+int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in,
+                     float* sig_out, float* c_re, float* c_im, int layout,
+                     int batch, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* cqt_last_error(void);
+
+/* ABI version of this header (major * 100 + minor). */
+int cqt_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_CQT_B200_H */

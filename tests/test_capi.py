@@ -1,0 +1,64 @@
+"""CPU checks of the C ABI library: it loads, exports every function the
+header declares, and rejects bad arguments before touching a GPU."""
+import ctypes
+import pathlib
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from flash_cqt_b200 import _native
+from flash_cqt_b200.layout import Filterbank, HeapLayout
+from flash_cqt_b200.tables import build_tables
+
+HEADER = pathlib.Path(__file__).resolve().parents[1] / "include" / "flash_cqt_b200.h"
+
+
+def declared_functions():
+    txt = HEADER.read_text()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]*?\b(cqt_\w+)\s*\(",
+                                 txt, flags=re.M)))
+
+
+def test_library_exports_header_symbols():
+    L = _native.lib()
+    names = declared_functions()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_native.exported_symbols())
+    assert L.cqt_version() == 100
+
+
+def test_bad_arguments_rejected_without_gpu():
+    L = _native.lib()
+    h = _native.HostTables()
+    out = ctypes.c_void_p()
+    assert L.cqt_tables_upload(ctypes.byref(h), 0, ctypes.byref(out)) == -1
+    assert b"class count" in L.cqt_last_error()
+    assert L.cqt_workspace_bytes(None, 4) == 0
+    assert L.cqt_analysis(None, None, None, None, 0, 1, None, 0, None) == -1
+
+
+def test_out_of_range_tables_rejected():
+    """the upload bounds-checks every gather and scatter index on the host"""
+    tabs = build_tables(HeapLayout(Filterbank([3, 4, 2], [8, 16, 32], 44100, 65536)))
+    src, gain = tabs["fwd"]["analysis"]
+    bad = src.copy()
+    bad[5] = 40000
+    tabs["fwd"]["analysis"] = (bad, gain)
+    with pytest.raises(RuntimeError, match="gather bin out of range"):
+        _native.DeviceTables(tabs, 0)
+
+
+def test_engine_refuses_cpu():
+    from flash_cqt_b200.engine import Engine
+    with pytest.raises(RuntimeError):
+        Engine.from_params([3, 4, 2], [8, 16, 32], 44100, 65536, device="cpu")
+    if not torch.cuda.is_available():
+        from flash_cqt_b200 import OctCQT
+        cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=65536)
+        with pytest.raises(RuntimeError):
+            cqt.fwd(torch.zeros(1, 65536))

@@ -1,0 +1,228 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle.
+
+Tolerances (from the north star): coefficients >= 120 dB relative SNR against
+the oracle, reconstruction >= 125 dB, gradients >= 120 dB against the oracle's
+exact adjoints (which are pinned to torch autograd through the reference).
+"""
+import numpy as np
+import pytest
+import torch
+
+from fixtures import STRIDE, gc_seed, gy_seed, oracle, ref, sinusoids, x_noise
+from oracle.cqt_oracle import snr_db
+
+pytestmark = pytest.mark.gpu
+
+COEF_DB = 120.0
+RT_DB = 125.0
+GRAD_DB = 120.0
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def eng(dev):
+    from flash_cqt_b200.engine import Engine
+    return Engine.from_params([3, 4, 2], [8, 16, 32], 44100, 65536, dev)
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def test_analysis_matches_oracle_and_reference(eng, dev):
+    o, r = oracle(), ref()
+    x = x_noise()
+    h = _np(eng.analysis(torch.from_numpy(x).to(dev)))
+    want = o.heap(o.fwd(x.astype(np.float64)))
+    assert snr_db(want, h) >= COEF_DB
+    assert snr_db(r["coef_noise_s"], h.reshape(-1)[::STRIDE]) >= COEF_DB
+    # every band on its own, not just the aggregate
+    for b, M, off in o.gspec:
+        for i in range(b):
+            s = slice(off + i * M, off + (i + 1) * M)
+            assert snr_db(want[:, s], h[:, s]) >= 110, (M, off, i)
+
+
+def test_analysis_sinusoids(eng, dev):
+    o, r = oracle(), ref()
+    x = sinusoids(1)
+    h = _np(eng.analysis(torch.from_numpy(x).to(dev)))
+    assert snr_db(o.heap(o.fwd(x.astype(np.float64))), h) >= COEF_DB
+    assert snr_db(r["coef_sines_s"], h.reshape(-1)[::STRIDE]) >= COEF_DB - 5
+
+
+def test_synthesis_matches_oracle(eng, dev):
+    o = oracle()
+    x = x_noise()
+    want = o.heap(o.fwd(x.astype(np.float64)))
+    c = torch.from_numpy(want.astype(np.complex64)).to(dev)
+    y = _np(eng.synthesis(c))
+    assert snr_db(o.bwd(o.unheap(want)), y) >= RT_DB
+    assert snr_db(x, y) >= RT_DB
+
+
+@pytest.mark.parametrize("B", [1, 3, 5, 17, 64])
+def test_round_trip_batches(eng, dev, B):
+    g = torch.Generator(device="cpu").manual_seed(100 + B)
+    x = torch.randn(B, 65536, generator=g).to(dev)
+    y = eng.synthesis(eng.analysis(x))
+    xs, ys = _np(x).astype(np.float64), _np(y).astype(np.float64)
+    for b in range(B):
+        assert snr_db(xs[b], ys[b]) >= RT_DB, b
+
+
+def test_adjoints_match_oracle(eng, dev):
+    o = oracle()
+    gc = gc_seed(o.ncoef)
+    gx = _np(eng.adj_analysis(torch.from_numpy(gc).to(dev)))
+    assert snr_db(o.adj_fwd(o.unheap(gc.astype(np.complex128))), gx) >= GRAD_DB
+    gy = gy_seed()
+    gk = _np(eng.adj_synthesis(torch.from_numpy(gy).to(dev)))
+    assert snr_db(o.heap(o.adj_bwd(gy.astype(np.float64))), gk) >= GRAD_DB
+
+
+def test_adjoints_match_reference_autograd_fixtures(eng, dev):
+    r = ref()
+    o = oracle()
+    gx = _np(eng.adj_analysis(torch.from_numpy(gc_seed(o.ncoef)).to(dev)))
+    assert snr_db(r["gx_an_s"], gx.reshape(-1)[::STRIDE]) >= GRAD_DB - 5
+    gk = _np(eng.adj_synthesis(torch.from_numpy(gy_seed()).to(dev)))
+    assert snr_db(r["gk_syn_s"], gk.reshape(-1)[::STRIDE]) >= GRAD_DB - 5
+
+
+def test_trainable_gradients(dev):
+    """TrainableCQT through torch autograd vs the oracle's exact transposes."""
+    from flash_cqt_b200 import OctCQT, TrainableCQT
+    o = oracle()
+    cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=65536, device=dev)
+    t = TrainableCQT(cqt, dev)
+    x = torch.from_numpy(x_noise()).to(dev).requires_grad_(True)
+    gc = torch.from_numpy(gc_seed(o.ncoef)).to(dev)
+    blocks, side = t.fwd(x)
+    h = torch.cat([c.reshape(2, -1) for c in list(blocks) + list(side)], -1)
+    (torch.view_as_real(h) * torch.view_as_real(gc)).sum().backward()
+    want = o.adj_fwd(o.unheap(gc_seed(o.ncoef).astype(np.complex128)))
+    assert snr_db(want, _np(x.grad)) >= GRAD_DB
+    # synthesis gradient w.r.t. leaf blocks
+    leaves = [c.detach().clone().requires_grad_(True) for c in list(blocks) + list(side)]
+    gy = torch.from_numpy(gy_seed()).to(dev)
+    (t.bwd(leaves[:9], leaves[9:]) * gy).sum().backward()
+    gk = torch.cat([lv.grad.reshape(2, -1) for lv in leaves], -1)
+    assert snr_db(o.heap(o.adj_bwd(gy_seed().astype(np.float64))), _np(gk)) >= GRAD_DB
+
+
+def test_train_step_chain_gradient(dev):
+    """analysis -> synthesis -> MSE -> backward vs the oracle chain rule."""
+    from flash_cqt_b200 import OctCQT, TrainableCQT
+    o = oracle()
+    t = TrainableCQT(OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=65536,
+                            device=dev), dev)
+    x0 = x_noise()
+    tgt = gy_seed()
+    x = torch.from_numpy(x0).to(dev).requires_grad_(True)
+    y = t.bwd(*t.fwd(x))
+    loss = (y - torch.from_numpy(tgt).to(dev)).square().mean()
+    loss.backward()
+    yo = o.bwd(o.fwd(x0.astype(np.float64)))
+    gy = 2.0 * (yo - tgt) / yo.size
+    want = o.adj_fwd(o.adj_bwd(gy))
+    assert snr_db(want, _np(x.grad)) >= GRAD_DB - 5
+
+
+def test_planar_and_interleaved_agree_bitwise(dev):
+    from flash_cqt_b200 import FusedOctCQT, OctCQT
+    cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=65536, device=dev)
+    f = FusedOctCQT(cqt, dev)
+    x = torch.from_numpy(x_noise()).to(dev)
+    KR, KI = f.fwd(x)
+    h = f.eng.analysis(x)
+    assert torch.equal(KR, h.real) and torch.equal(KI, h.imag)
+    XO = f.bwd(KR, KI)
+    assert torch.equal(XO, f.eng.synthesis(h))
+    bl = f.blocks_view(KR, KI)
+    assert [tuple(b.shape[1:]) for b in bl] == [(b, M) for b, M, _ in f.gspec]
+
+
+def test_deterministic(eng, dev):
+    x = torch.from_numpy(x_noise()).to(dev)
+    a1 = eng.analysis(x)
+    a2 = eng.analysis(x)
+    assert torch.equal(a1, a2)
+    y1 = eng.synthesis(a1)
+    y2 = eng.synthesis(a1)
+    assert torch.equal(y1, y2)
+
+
+def test_linearity_large_batch(eng, dev):
+    """size-independent property at a large batch: A(x1 + 2 x2) = A x1 + 2 A x2"""
+    g = torch.Generator(device="cpu").manual_seed(7)
+    x1 = torch.randn(256, 65536, generator=g).to(dev)
+    x2 = torch.randn(256, 65536, generator=g).to(dev)
+    a = eng.analysis(x1 + 2 * x2)
+    b = eng.analysis(x1) + 2 * eng.analysis(x2)
+    assert snr_db(_np(a), _np(b)) >= 120
+    y = eng.synthesis(a)
+    assert snr_db(_np(x1 + 2 * x2).astype(np.float64), _np(y)) >= RT_DB
+
+
+def test_graph_replay_rebuilds_outputs(eng, dev):
+    from flash_cqt_b200 import Graphed
+    x = torch.from_numpy(sinusoids(1)).to(dev)
+
+    def rt(inp):
+        return eng.synthesis(eng.analysis(inp))
+
+    g = Graphed(rt, x)
+    eager = rt(x)
+    g._out.fill_(1e9)   # poison the static output, the replay must rebuild it
+    y = g(x)
+    assert torch.equal(y, eager)
+    assert snr_db(_np(x).astype(np.float64), _np(y)) >= RT_DB
+
+
+def test_zero_and_impulse(eng, dev):
+    z = torch.zeros(2, 65536, device=dev)
+    assert torch.count_nonzero(eng.analysis(z)) == 0
+    imp = torch.zeros(1, 65536, device=dev)
+    imp[0, 12345] = 1.0
+    o = oracle()
+    assert snr_db(o.heap(o.fwd(_np(imp).astype(np.float64))),
+                  _np(eng.analysis(imp))) >= COEF_DB
+
+
+def test_bad_inputs_raise(eng, dev):
+    with pytest.raises(TypeError):
+        eng.analysis(torch.zeros(1, 65536, device=dev, dtype=torch.float64))
+    with pytest.raises(ValueError):
+        eng.analysis(torch.zeros(1, 4096, device=dev))
+    with pytest.raises(ValueError):
+        eng.analysis(torch.zeros(1, 65536))
+    with pytest.raises(ValueError):
+        eng.synthesis(torch.zeros(1, 100, dtype=torch.complex64, device=dev))
+
+
+def test_sliced_matches_oracle(dev):
+    from flash_cqt_b200 import SlicedCQT
+    from fixtures import STRIDE_SLICED, chirp
+    from oracle.cqt_oracle import SlicedOracle
+    r = ref()
+    L = 150000
+    x = chirp(5, L)
+    sl = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
+    xt = torch.from_numpy(x).to(dev).view(1, 1, L)
+    blocks, side = sl.fwd(xt)
+    so = SlicedOracle()
+    ob, os_ = so.fwd(x[None].astype(np.float64))
+    got = np.concatenate([_np(c).reshape(-1) for c in blocks])
+    want = np.concatenate([c.reshape(-1) for c in ob])
+    assert snr_db(want, got) >= COEF_DB
+    bs = np.concatenate([_np(c).reshape(-1)[::STRIDE_SLICED] for c in blocks])
+    assert snr_db(r["sliced_blocks_s"], bs) >= COEF_DB - 5
+    y = sl.bwd(blocks, side, length=L)
+    assert snr_db(x.astype(np.float64), _np(y).reshape(-1)) >= RT_DB
