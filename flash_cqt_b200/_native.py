@@ -27,8 +27,8 @@ class HostTables(ctypes.Structure):
         ("band_off", _i32p), ("band_list", _i32p),
         ("nclasses", ctypes.c_int32),
         ("class_len", _i32p), ("class_count", _i32p), ("class_first", _i32p),
-        ("an_src", _i32p), ("an_gain", _f32p),
-        ("as_src", _i32p), ("as_gain", _f32p),
+        ("an_src", _i32p), ("an_gain", _f32p), ("an_seg", _i32p),
+        ("as_src", _i32p), ("as_gain", _f32p), ("as_seg", _i32p),
         ("sy_dest", _i32p), ("sy_gre", _f32p), ("sy_gim", _f32p),
         ("sy_mask", _u8p), ("sy_nplanes", ctypes.c_int32),
         ("aa_dest", _i32p), ("aa_gre", _f32p), ("aa_gim", _f32p),
@@ -121,9 +121,11 @@ class DeviceTables:
         src, gain = tabs["fwd"]["analysis"]
         h.an_src = arr(src, np.int32, ctypes.c_int32)
         h.an_gain = arr(gain, np.float32, ctypes.c_float)
+        h.an_seg = arr(tabs["seg"]["analysis"], np.int32, ctypes.c_int32)
         src, gain = tabs["fwd"]["adj_synth"]
         h.as_src = arr(src, np.int32, ctypes.c_int32)
         h.as_gain = arr(gain, np.float32, ctypes.c_float)
+        h.as_seg = arr(tabs["seg"]["adj_synth"], np.int32, ctypes.c_int32)
         d, gr, gi, mk, npl = tabs["inv"]["synth"]
         h.sy_dest = arr(d, np.int32, ctypes.c_int32)
         h.sy_gre = arr(gr, np.float32, ctypes.c_float)

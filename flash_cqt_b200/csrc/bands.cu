@@ -46,6 +46,7 @@ struct Inst {
     int il;       // instance index within the CTA
     bool valid;
     int slice;
+    int band;
     int off;      // heap offset of the band
 };
 
@@ -60,7 +61,8 @@ __device__ __forceinline__ Inst locate(const BandCommon& bc, const BandSched& sc
     const int B = sc.batch;
     in.valid = inst < sc.nb[c] * B;
     in.slice = in.valid ? inst % B : 0;
-    in.off = in.valid ? __ldg(bc.band_off + __ldg(bc.band_list + sc.first[c] + inst / B)) : 0;
+    in.band = in.valid ? __ldg(bc.band_list + sc.first[c] + inst / B) : 0;
+    in.off = in.valid ? __ldg(bc.band_off + in.band) : 0;
     return in;
 }
 
@@ -93,6 +95,15 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, int t,
     }
 }
 
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(sa), "l"(gmem));
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
 template <int M>
 __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const BandCommon& bc,
                          const BandSched& sc, int c, CoefPtr out, float2* smem) {
@@ -104,25 +115,40 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     const Tw2048 tw{bc.tw2048};
     const float2* Xs = X + (long)in.slice * kPlaneStride;
 
-    // stage 1: routed gather, element r of butterfly b is tap t + T b + r M / R1
-    float2 v[kP];
+    // stage the band's contiguous spectrum segment (<= M bins) into shared
+    // memory with asynchronous copies, independent of the tap-table loads
+    int lo = 0;
+    if (in.valid) {
+        const int2 sg = __ldg(tab.seg + in.band);
+        lo = sg.x;
+        for (int i = t; i < sg.y; i += T) cp_async8(buf + PADI(i), Xs + lo + i);
+    }
+    // stage 1 taps: element r of butterfly b is tap t + T b + r M / R1
+    int src[kP];
+    float gain[kP];
 #pragma unroll
     for (int b = 0; b < kP / R1; ++b)
 #pragma unroll
         for (int r = 0; r < R1; ++r) {
             const int m = in.off + t + T * b + r * (M / R1);
-            float2 val = make_float2(0.f, 0.f);
-            if (in.valid) {
-                const int s = __ldg(tab.src + m);
-                if (s >= 0) {
-                    const float g = __ldg(tab.gain + m);
-                    float2 xv = Xs[s & 0xFFFF];
-                    if (s & 0x10000) xv.y = -xv.y;
-                    val = cscale(xv, g);
-                }
-            }
-            v[b * R1 + r] = val;
+            src[b * R1 + r] = in.valid ? __ldg(tab.src + m) : -1;
+            gain[b * R1 + r] = in.valid ? __ldg(tab.gain + m) : 0.f;
         }
+    cp_async_wait_all();
+    __syncthreads();
+    float2 v[kP];
+#pragma unroll
+    for (int i = 0; i < kP; ++i) {
+        const int s = src[i];
+        float2 val = make_float2(0.f, 0.f);
+        if (s >= 0) {
+            float2 xv = buf[PADI((s & 0xFFFF) - lo)];
+            if (s & 0x10000) xv.y = -xv.y;
+            val = cscale(xv, gain[i]);
+        }
+        v[i] = val;
+    }
+    __syncthreads();   // the segment is dead; stage 1 reuses the buffer
     static_for<0, kP / R1>([&](auto Bb) {
         dft<R1, +1, decltype(Bb)::value * R1, 1>(v);
     });

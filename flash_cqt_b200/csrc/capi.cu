@@ -164,6 +164,31 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
             if (h->band_off[h->band_list[h->class_first[c] + i]] + M > nc)
                 return fail(CQT_ERR_ARG, "band runs past the heap");
     }
+    for (int b = 0; b < h->nbands; ++b) {
+        for (const int32_t* sg : {h->an_seg, h->as_seg}) {
+            const int lo = sg[2 * b], n = sg[2 * b + 1];
+            if (lo < 0 || n < 0 || lo + n > kHalf + 1)
+                return fail(CQT_ERR_ARG, "band segment out of the half spectrum");
+        }
+    }
+    for (int c = 0; c < h->nclasses; ++c) {
+        const int M = h->class_len[c];
+        for (int i = 0; i < h->class_count[c]; ++i) {
+            const int b = h->band_list[h->class_first[c] + i];
+            const int o = h->band_off[b];
+            for (int w = 0; w < 2; ++w) {
+                const int32_t* sg = w ? h->as_seg : h->an_seg;
+                const int32_t* src = w ? h->as_src : h->an_src;
+                const int lo = sg[2 * b], n = sg[2 * b + 1];
+                if (n > M) return fail(CQT_ERR_ARG, "band segment longer than its block");
+                for (int m = 0; m < M; ++m) {
+                    const int s = src[o + m];
+                    if (s >= 0 && ((s & 0xFFFF) < lo || (s & 0xFFFF) >= lo + n))
+                        return fail(CQT_ERR_ARG, "gather bin outside its band segment");
+                }
+            }
+        }
+    }
     for (int i = 0; i < nc; ++i) {
         for (const int32_t* s : {h->an_src, h->as_src})
             if (s[i] >= 0 && ((s[i] & 0xFFFF) > kHalf || (s[i] & ~0x1FFFF)))
@@ -200,6 +225,7 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     size_t i_boff = add(h->band_off, nB), i_blist = add(h->band_list, nB);
     size_t i_ans = add(h->an_src, nI), i_ang = add(h->an_gain, nI);
     size_t i_ass = add(h->as_src, nI), i_asg = add(h->as_gain, nI);
+    size_t i_ansg = add(h->an_seg, nB * 2), i_assg = add(h->as_seg, nB * 2);
     size_t i_syd = add(h->sy_dest, nI), i_syr = add(h->sy_gre, nI), i_syi = add(h->sy_gim, nI);
     size_t i_sym = add(h->sy_mask, maskB);
     size_t i_aad = add(h->aa_dest, nI), i_aar = add(h->aa_gre, nI), i_aai = add(h->aa_gim, nI);
@@ -239,8 +265,8 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
         t->cls_nb[c] = h->class_count[c];
         t->cls_first[c] = h->class_first[c];
     }
-    t->fwd[0] = FwdTab{(const int*)P(i_ans), (const float*)P(i_ang)};
-    t->fwd[1] = FwdTab{(const int*)P(i_ass), (const float*)P(i_asg)};
+    t->fwd[0] = FwdTab{(const int*)P(i_ans), (const float*)P(i_ang), (const int2*)P(i_ansg)};
+    t->fwd[1] = FwdTab{(const int*)P(i_ass), (const float*)P(i_asg), (const int2*)P(i_assg)};
     t->inv[0] = InvTab{(const int*)P(i_syd), (const float*)P(i_syr), (const float*)P(i_syi),
                        (const unsigned char*)P(i_sym), h->sy_nplanes};
     t->inv[1] = InvTab{(const int*)P(i_aad), (const float*)P(i_aar), (const float*)P(i_aai),

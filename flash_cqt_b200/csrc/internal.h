@@ -8,6 +8,7 @@ namespace fcqt {
 struct FwdTab {            // analysis-engine tap table (one per use)
     const int* src;        // bin | conj << 16, or -1 for a zero tap
     const float* gain;     // window gain with all constants folded in
+    const int2* seg;       // per band: first bin and length of its segment
 };
 
 struct InvTab {            // synthesis-engine tap table (one per use)

@@ -118,15 +118,20 @@ spectrum_fwd_kernel(const float* __restrict__ x, float2* __restrict__ X,
     }
 }
 
-// F[q] from the colour planes: planes flagged in mask[q], fixed plane order
+// F[q] from the colour planes, planes flagged in mask[q], fixed plane order.
+// Planes 0 and 1 cover almost every bin, so they are loaded unconditionally
+// (in parallel with the mask) and selected; planes 2 and 3 are rare.
 __device__ __forceinline__ float2 plane_sum(const float2* __restrict__ Es,
                                             const unsigned char* __restrict__ mask,
-                                            int q) {
+                                            int q, int nplanes) {
     const unsigned mk = __ldg(mask + q);
+    const float2 e0 = Es[q];
+    const float2 e1 = nplanes > 1 ? Es[kPlaneStride + q] : make_float2(0.f, 0.f);
     float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int p = 0; p < kMaxPlanes; ++p)
-        if (mk & (1u << p)) acc = cadd(acc, Es[p * kPlaneStride + q]);
+    if (mk & 1u) acc = cadd(acc, e0);
+    if (mk & 2u) acc = cadd(acc, e1);
+    if (mk & 4u) acc = cadd(acc, Es[2 * kPlaneStride + q]);
+    if (mk & 8u) acc = cadd(acc, Es[3 * kPlaneStride + q]);
     return acc;
 }
 
@@ -141,7 +146,7 @@ __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
 __global__ void __launch_bounds__(kSpecThreads, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restrict__ mask,
                     float* __restrict__ y, const float2* __restrict__ ghi,
-                    const float2* __restrict__ glo, int plane_block) {
+                    const float2* __restrict__ glo, int nplanes) {
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
     float2* hi = buf + padded(kQuarter);
@@ -152,15 +157,15 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
     load_twiddles(hi, lo, ghi, glo);
     __syncthreads();
     const Tw64k tw{hi, lo};
-    const float2* Es = E + slice * (long)plane_block;
+    const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
 
     // quads {n, L - n, Q + n, Q - n}: four bins in, u_h[n] and u_h[Q - n] out
     for (int n = t; n <= kQuarter / 2; n += kSpecT) {
         const int m = (kQuarter - n) & (kQuarter - 1);
-        float2 fA = plane_sum(Es, mask, n);
-        float2 fB = plane_sum(Es, mask, kHalf - n);
-        const float2 fC = plane_sum(Es, mask, kQuarter + n);
-        const float2 fD = plane_sum(Es, mask, kQuarter - n);
+        float2 fA = plane_sum(Es, mask, n, nplanes);
+        float2 fB = plane_sum(Es, mask, kHalf - n, nplanes);
+        const float2 fC = plane_sum(Es, mask, kQuarter + n, nplanes);
+        const float2 fD = plane_sum(Es, mask, kQuarter - n, nplanes);
         if (n == 0) {  // irfft ignores the imaginary parts of DC and Nyquist
             fA.y = 0.f;
             fB.y = 0.f;
@@ -209,7 +214,7 @@ cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, float* y,
                                 int batch, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
     spectrum_inv_kernel<<<2 * batch, kSpecThreads, kSpecSmem, s>>>(
-        E, tab.mask, y, tw_hi, tw_lo, tab.nplanes * kPlaneStride);
+        E, tab.mask, y, tw_hi, tw_lo, tab.nplanes);
     return cudaGetLastError();
 }
 

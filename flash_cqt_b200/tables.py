@@ -115,6 +115,20 @@ def build_tables(heap):
         "analysis": (src_an, gain_an.astype(np.float32)),
         "adj_synth": (src_as, gain_as.astype(np.float32)),
     }
+    # per band: the contiguous half-spectrum segment [lo, lo + n) holding all
+    # live gather bins of the band (staged into shared memory by bands_fwd)
+    t["seg"] = {}
+    for nm, (src, _) in t["fwd"].items():
+        seg = np.zeros((len(heap.bands), 2), np.int32)
+        for i, (M, o) in enumerate(heap.bands):
+            s_ = src[o:o + M]
+            bins = (s_[s_ >= 0] & 0xFFFF).astype(np.int64)
+            if bins.size:
+                lo, hi = int(bins.min()), int(bins.max())
+                if hi - lo + 1 > M:
+                    raise RuntimeError("band %d gathers from more than M bins" % i)
+                seg[i] = (lo, hi - lo + 1)
+        t["seg"][nm] = seg
     t["inv"] = {}
     for s in INV_SETS:
         rr = [rn for rn in runs[s] if rn.size]

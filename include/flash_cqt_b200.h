@@ -69,9 +69,13 @@ typedef struct cqt_host_tables {
     const int32_t* class_len;   /* [nclasses] block length M (32..2048) */
     const int32_t* class_count; /* [nclasses] bands in the class */
     const int32_t* class_first; /* [nclasses] first class entry in band_list */
-    /* analysis-engine tap tables: src = bin | conj << 16, or -1 */
+    /* analysis-engine tap tables: src = bin | conj << 16, or -1; seg =
+     * [nbands][2] (first bin, bin count) of the contiguous half-spectrum
+     * segment that holds every live tap of the band (count <= M) */
     const int32_t* an_src;  const float* an_gain;   /* analysis */
+    const int32_t* an_seg;
     const int32_t* as_src;  const float* as_gain;   /* transpose of synthesis */
+    const int32_t* as_seg;
     /* synthesis-engine tap tables: dest = plane * 32776 + bin, or -1 */
     const int32_t* sy_dest; const float* sy_gre; const float* sy_gim;
     const uint8_t* sy_mask; int32_t sy_nplanes;     /* synthesis */
