@@ -24,7 +24,7 @@ _u8p = ctypes.POINTER(ctypes.c_uint8)
 class HostTables(ctypes.Structure):
     _fields_ = [
         ("nbands", ctypes.c_int32), ("ncoef", ctypes.c_int32),
-        ("band_off", _i32p), ("band_list", _i32p),
+        ("band_off", _i32p), ("band_list", _i32p), ("band_geom", _i32p),
         ("nclasses", ctypes.c_int32),
         ("class_len", _i32p), ("class_count", _i32p), ("class_first", _i32p),
         ("an_src", _i32p), ("an_gain", _f32p), ("an_seg", _i32p),
@@ -114,6 +114,7 @@ class DeviceTables:
         h.ncoef = len(tabs["fwd"]["analysis"][0])
         h.band_off = arr(tabs["band_off"], np.int32, ctypes.c_int32)
         h.band_list = arr(tabs["band_list"], np.int32, ctypes.c_int32)
+        h.band_geom = arr(tabs["band_geom"], np.int32, ctypes.c_int32)
         h.nclasses = len(cls)
         h.class_len = arr([c[0] for c in cls], np.int32, ctypes.c_int32)
         h.class_count = arr([c[1] for c in cls], np.int32, ctypes.c_int32)

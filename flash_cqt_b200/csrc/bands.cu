@@ -2,21 +2,30 @@
 // analysis and synthesis (block lengths M = 32 ... 2048, 154 bands a slice).
 //
 // bands_fwd (analysis engine; also the transpose of the synthesis):
-//   gather   v[m] = gain[m] * X~[src[m]]        (window / routing table)
+//   gather   v[m] = gain[m] * X~[bin(m)]          (window / routing)
 //   DFT      coef[n] = sum_m v[m] e^{+2 pi i m n / M}   (1/M folded in gain)
 //   store    natural-order coefficient heap, coalesced
 // bands_inv (synthesis engine; also the transpose of the analysis):
 //   load     coefficient heap, coalesced
 //   DFT      S[m] = sum_n coef[n] e^{-2 pi i m n / M}
-//   scatter  E[dest[m]] = (Re S gre[m], Im S gim[m])   one owned slot per tap
+//   scatter  E[plane, bin(m)] = (Re S gre[m], Im S gim[m])  one owned slot per tap
 //
-// Replaces the reference's radix band engine (radix_impl.cuh:146-443), which
-// runs warp-shuffle radix-8/16/32 butterflies, one CTA per (band, slice):
-// here each thread holds 32 points in registers and runs whole radix-32 /
-// radix-2..32 butterflies (no shuffles), the stages exchange through padded
-// shared memory, and one 256-thread CTA processes 8192 points = 8192 / M
-// (band, slice) instances of one block length, so small bands batch up and
-// the tables are reused across the slices of a CTA.
+// Octave bands (all but the DC and Nyquist side bands) have a closed-form
+// tap -> bin map: tap m reads / writes bin lo + ((m + l) mod M), live when
+// (m + l) mod M < Lg (the window support, oct_cqt.py:44-58), no conjugation,
+// one colour plane per band -- so they need one gain load per tap and no
+// index tables.  The two side bands take the table path (src / dest tables,
+// conjugated mirror taps).  Band descriptors travel in the kernel parameters
+// (constant bank), so a CTA starts its memory traffic without any dependent
+// global loads.
+//
+// Replaces the reference's radix band engine (radix_impl.cuh:146-443: warp
+// shuffle radix-8/16/32 butterflies, one CTA per (band, slice), atomics in
+// the inverse): here each thread holds 32 points in registers and runs whole
+// radix-2..32 butterflies, stages exchange through padded shared memory, the
+// inter-stage twiddles sit in conflict-free shared rows, and one 256-thread
+// CTA processes 8192 points = 8192 / M (band, slice) instances of one block
+// length so small bands batch up.
 #include "engine.cuh"
 #include "internal.h"
 
@@ -24,55 +33,109 @@ namespace fcqt {
 
 namespace {
 
-constexpr int kP = 32;
-constexpr int kBandSmem = (kBandCap / 32) * 33 * 8;   // padded(kBandCap) float2
+constexpr int kP = kBandP;
+constexpr int kBandData = padded(kBandCap);              // float2 per CTA
+constexpr int kBandTw = 2048;                            // >= largest twiddle set
+constexpr int kBandSmem = (kBandData + kBandTw) * 8;
+constexpr int kBandMinBlocks = kP == 32 ? 2 : 4;        // 128 / 64 registers a thread
 
-struct Tw2048 {
-    const float2* w;
-    __device__ __forceinline__ float2 operator()(int e) const { return __ldg(w + (e & 2047)); }
+template <int M, int P = kP> struct Sched;   // stage radices per block length
+template <> struct Sched<32, 32>   { static constexpr int R1 = 32, R2 = 1,  R3 = 1; };
+template <> struct Sched<64, 32>   { static constexpr int R1 = 32, R2 = 2,  R3 = 1; };
+template <> struct Sched<128, 32>  { static constexpr int R1 = 32, R2 = 4,  R3 = 1; };
+template <> struct Sched<256, 32>  { static constexpr int R1 = 32, R2 = 8,  R3 = 1; };
+template <> struct Sched<512, 32>  { static constexpr int R1 = 32, R2 = 16, R3 = 1; };
+template <> struct Sched<1024, 32> { static constexpr int R1 = 32, R2 = 32, R3 = 1; };
+template <> struct Sched<2048, 32> { static constexpr int R1 = 32, R2 = 32, R3 = 2; };
+template <> struct Sched<32, 16>   { static constexpr int R1 = 16, R2 = 2,  R3 = 1; };
+template <> struct Sched<64, 16>   { static constexpr int R1 = 16, R2 = 4,  R3 = 1; };
+template <> struct Sched<128, 16>  { static constexpr int R1 = 16, R2 = 8,  R3 = 1; };
+template <> struct Sched<256, 16>  { static constexpr int R1 = 16, R2 = 16, R3 = 1; };
+template <> struct Sched<512, 16>  { static constexpr int R1 = 16, R2 = 16, R3 = 2; };
+template <> struct Sched<1024, 16> { static constexpr int R1 = 16, R2 = 16, R3 = 4; };
+template <> struct Sched<2048, 16> { static constexpr int R1 = 16, R2 = 16, R3 = 8; };
+
+// shared twiddle rows of one block length: stage 2 rows W_{NS R}^{r k}
+// (r = 1..R2-1, k < NS2 = R1), then stage 3 rows (r = 1..R3-1, k < R1 R2)
+template <int M>
+struct TwLayout {
+    static constexpr int R1 = Sched<M>::R1, R2 = Sched<M>::R2, R3 = Sched<M>::R3;
+    static constexpr int n2 = (R2 - 1) * R1;
+    static constexpr int n3 = (R3 - 1) * R1 * R2;
+    static_assert(n2 + n3 <= kBandTw, "twiddle rows exceed their shared slot");
 };
 
-template <int M> struct Sched;       // stage radices per block length
-template <> struct Sched<32>   { static constexpr int R1 = 32, R2 = 1,  R3 = 1; };
-template <> struct Sched<64>   { static constexpr int R1 = 32, R2 = 2,  R3 = 1; };
-template <> struct Sched<128>  { static constexpr int R1 = 32, R2 = 4,  R3 = 1; };
-template <> struct Sched<256>  { static constexpr int R1 = 32, R2 = 8,  R3 = 1; };
-template <> struct Sched<512>  { static constexpr int R1 = 32, R2 = 16, R3 = 1; };
-template <> struct Sched<1024> { static constexpr int R1 = 32, R2 = 32, R3 = 1; };
-template <> struct Sched<2048> { static constexpr int R1 = 32, R2 = 32, R3 = 2; };
+template <int M>
+__device__ __forceinline__ void fill_twiddles(float2* tws, const float2* __restrict__ w2048) {
+    using L = TwLayout<M>;
+    for (int e = threadIdx.x; e < L::n2 + L::n3; e += kBandThreads) {
+        int r, k, span, R;
+        if (e < L::n2) {
+            r = e / L::R1 + 1;
+            k = e % L::R1;
+            span = L::R1;
+            R = L::R2;
+        } else {
+            const int f = e - L::n2;
+            span = L::R1 * L::R2;
+            R = L::R3;
+            r = f / span + 1;
+            k = f % span;
+        }
+        tws[e] = __ldg(w2048 + ((r * k * (2048 / (span * R))) & 2047));
+    }
+}
+
+// Twiddle (span NS > 1) and DFT for all butterflies of a thread; twiddles
+// from shared rows (row r - 1 at rows + (r - 1) NS), conjugated for S = +1
+template <int M, int T, int R, int NS, int S, int P>
+__device__ __forceinline__ void stage_compute_rows(float2 (&v)[P], int t, const float2* rows) {
+    static_for<0, P / R>([&](auto Bb) {
+        constexpr int b = decltype(Bb)::value;
+        if constexpr (NS > 1) {
+            const int k = (t + T * b) % NS;
+#pragma unroll
+            for (int r = 1; r < R; ++r) {
+                float2 w = rows[(r - 1) * NS + k];
+                if constexpr (S > 0) w.y = -w.y;
+                v[b * R + r] = cmul(v[b * R + r], w);
+            }
+        }
+        dft<R, S, b * R, 1>(v);
+    });
+}
 
 struct Inst {
     int t;        // thread index within the instance
     int il;       // instance index within the CTA
     bool valid;
     int slice;
-    int band;
-    int off;      // heap offset of the band
+    int4 d;       // band descriptor
 };
 
 template <int M>
-__device__ __forceinline__ Inst locate(const BandCommon& bc, const BandSched& sc, int c) {
+__device__ __forceinline__ Inst locate(const BandParams& bp, int c) {
     constexpr int T = M / kP;
     constexpr int IPC = kBandThreads / T;
     Inst in;
     in.t = threadIdx.x % T;
     in.il = threadIdx.x / T;
-    const int inst = (blockIdx.x - sc.cta0[c]) * IPC + in.il;
-    const int B = sc.batch;
-    in.valid = inst < sc.nb[c] * B;
+    const int inst = (blockIdx.x - bp.sc.cta0[c]) * IPC + in.il;
+    const int B = bp.sc.batch;
+    in.valid = inst < bp.sc.nb[c] * B;
     in.slice = in.valid ? inst % B : 0;
-    in.band = in.valid ? __ldg(bc.band_list + sc.first[c] + inst / B) : 0;
-    in.off = in.valid ? __ldg(bc.band_off + in.band) : 0;
+    in.d = bp.desc[bp.sc.first[c] + (in.valid ? inst / B : 0)];
     return in;
 }
 
-// remaining stages (2 and 3) of a block-length-M transform after stage 1's
-// DFT; the last stage's outputs (index n = j + r M / R_last) go to `emit`
+// stages 2 and 3 after stage 1's DFT; the last stage's outputs (index
+// n = j + r M / R_last, j = t + T b) go to `emit`
 template <int M, int S, class Emit>
-__device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, int t,
-                                          const Tw2048& tw, Emit emit) {
+__device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const float2* tws,
+                                          int t, Emit emit) {
     constexpr int T = M / kP;
-    constexpr int R1 = Sched<M>::R1, R2 = Sched<M>::R2, R3 = Sched<M>::R3;
+    using L = TwLayout<M>;
+    constexpr int R1 = L::R1, R2 = L::R2, R3 = L::R3;
     using std::integral_constant;
     if constexpr (R2 == 1) {
         emit(v, integral_constant<int, R1>{}, integral_constant<int, 1>{});
@@ -81,7 +144,7 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, int t,
         __syncthreads();
         stage_load<M, T, R2>(v, buf, t);
         __syncthreads();
-        stage_compute<M, T, R2, R1, S, 2048>(v, t, tw);
+        stage_compute_rows<M, T, R2, R1, S>(v, t, tws);
         if constexpr (R3 == 1) {
             emit(v, integral_constant<int, R2>{}, integral_constant<int, R1>{});
         } else {
@@ -89,7 +152,7 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, int t,
             __syncthreads();
             stage_load<M, T, R3>(v, buf, t);
             __syncthreads();
-            stage_compute<M, T, R3, R1 * R2, S, 2048>(v, t, tw);
+            stage_compute_rows<M, T, R3, R1 * R2, S>(v, t, tws + L::n2);
             emit(v, integral_constant<int, R3>{}, integral_constant<int, R1 * R2>{});
         }
     }
@@ -104,35 +167,57 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
 }
 
+// descriptor fields: {heap offset, lo (octave) | band id (side), l | Lg << 16,
+// flags: bit 0 side band, bits 4-7 synthesis plane, bits 8-11 adjoint plane}
+__device__ __forceinline__ bool d_side(int4 d) { return d.w & 1; }
+__device__ __forceinline__ int d_l(int4 d) { return d.z & 0xFFFF; }
+__device__ __forceinline__ int d_lg(int4 d) { return d.z >> 16; }
+__device__ __forceinline__ int d_plane(int4 d, int which) { return (d.w >> (4 + 4 * which)) & 15; }
+
 template <int M>
-__device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const BandCommon& bc,
-                         const BandSched& sc, int c, CoefPtr out, float2* smem) {
+__device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const BandParams& bp,
+                         int c, CoefPtr out, float2* smem, float2* tws) {
     constexpr int T = M / kP;
     constexpr int R1 = Sched<M>::R1;
-    const Inst in = locate<M>(bc, sc, c);
+    const Inst in = locate<M>(bp, c);
     const int t = in.t;
     float2* buf = smem + in.il * padded(M);
-    const Tw2048 tw{bc.tw2048};
     const float2* Xs = X + (long)in.slice * kPlaneStride;
+    const int off = in.d.x;
+    const bool side = d_side(in.d);
 
     // stage the band's contiguous spectrum segment (<= M bins) into shared
-    // memory with asynchronous copies, independent of the tap-table loads
-    int lo = 0;
+    // memory with asynchronous copies, independent of the gain loads
+    int lo = 0, n = 0;
     if (in.valid) {
-        const int2 sg = __ldg(tab.seg + in.band);
-        lo = sg.x;
-        for (int i = t; i < sg.y; i += T) cp_async8(buf + PADI(i), Xs + lo + i);
+        if (side) {
+            const int2 sg = __ldg(tab.seg + in.d.y);
+            lo = sg.x;
+            n = sg.y;
+        } else {
+            lo = in.d.y;
+            n = d_lg(in.d);
+        }
+        for (int i = t; i < n; i += T) cp_async8(buf + PADI(i), Xs + lo + i);
     }
+    fill_twiddles<M>(tws, bp.tw2048);
     // stage 1 taps: element r of butterfly b is tap t + T b + r M / R1
-    int src[kP];
     float gain[kP];
+    int src[kP];
+    const int l = d_l(in.d);
 #pragma unroll
     for (int b = 0; b < kP / R1; ++b)
 #pragma unroll
         for (int r = 0; r < R1; ++r) {
-            const int m = in.off + t + T * b + r * (M / R1);
-            src[b * R1 + r] = in.valid ? __ldg(tab.src + m) : -1;
-            gain[b * R1 + r] = in.valid ? __ldg(tab.gain + m) : 0.f;
+            const int m = t + T * b + r * (M / R1);
+            gain[b * R1 + r] = in.valid ? __ldg(tab.gain + off + m) : 0.f;
+            if (side) {
+                const int s = in.valid ? __ldg(tab.src + off + m) : -1;
+                src[b * R1 + r] = s < 0 ? -1 : (((s & 0xFFFF) - lo) | (s & 0x10000));
+            } else {
+                const int i = (m + l) & (M - 1);
+                src[b * R1 + r] = i < n ? i : -1;
+            }
         }
     cp_async_wait_all();
     __syncthreads();
@@ -142,83 +227,92 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
         const int s = src[i];
         float2 val = make_float2(0.f, 0.f);
         if (s >= 0) {
-            float2 xv = buf[PADI((s & 0xFFFF) - lo)];
+            float2 xv = buf[PADI(s & 0xFFFF)];
             if (s & 0x10000) xv.y = -xv.y;
             val = cscale(xv, gain[i]);
         }
         v[i] = val;
     }
-    __syncthreads();   // the segment is dead; stage 1 reuses the buffer
     static_for<0, kP / R1>([&](auto Bb) {
         dft<R1, +1, decltype(Bb)::value * R1, 1>(v);
     });
+    __syncthreads();   // the staged segment is dead; stage 1 reuses the buffer
 
-    const long hb = (long)in.slice * bc.ncoef + in.off;
-    band_rest<M, +1>(v, buf, t, tw, [&](float2 (&w)[kP], auto Rc, auto NSc) {
+    const long hb = (long)in.slice * bp.ncoef + off;
+    band_rest<M, +1>(v, buf, tws, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
-        // last stage: j = t + T b < NS, output index n = j + r NS
 #pragma unroll
         for (int b = 0; b < kP / R; ++b)
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                const int n = t + T * b + r * NS;
+                const int nn = t + T * b + r * NS;
                 const float2 val = w[b * R + r];
                 if (out.interleaved) {
-                    reinterpret_cast<float2*>(out.re)[hb + n] = val;
+                    reinterpret_cast<float2*>(out.re)[hb + nn] = val;
                 } else {
-                    out.re[hb + n] = val.x;
-                    out.im[hb + n] = val.y;
+                    out.re[hb + nn] = val.x;
+                    out.im[hb + nn] = val.y;
                 }
             }
     });
 }
 
 template <int M>
-__device__ void band_inv(CoefPtr in_c, const InvTab& tab, const BandCommon& bc,
-                         const BandSched& sc, int c, float2* __restrict__ E, float2* smem) {
+__device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandParams& bp, int c,
+                         float2* __restrict__ E, float2* smem, float2* tws) {
     constexpr int T = M / kP;
     constexpr int R1 = Sched<M>::R1;
-    const Inst in = locate<M>(bc, sc, c);
+    const Inst in = locate<M>(bp, c);
     const int t = in.t;
     float2* buf = smem + in.il * padded(M);
-    const Tw2048 tw{bc.tw2048};
-    const long hb = (long)in.slice * bc.ncoef + in.off;
+    const int off = in.d.x;
+    const long hb = (long)in.slice * bp.ncoef + off;
 
     float2 v[kP];
 #pragma unroll
     for (int b = 0; b < kP / R1; ++b)
 #pragma unroll
         for (int r = 0; r < R1; ++r) {
-            const int n = t + T * b + r * (M / R1);
+            const int nn = t + T * b + r * (M / R1);
             float2 val = make_float2(0.f, 0.f);
             if (in.valid) {
                 if (in_c.interleaved) {
-                    val = __ldg(reinterpret_cast<const float2*>(in_c.re) + hb + n);
+                    val = __ldg(reinterpret_cast<const float2*>(in_c.re) + hb + nn);
                 } else {
-                    val.x = __ldg(in_c.re + hb + n);
-                    val.y = __ldg(in_c.im + hb + n);
+                    val.x = __ldg(in_c.re + hb + nn);
+                    val.y = __ldg(in_c.im + hb + nn);
                 }
             }
             v[b * R1 + r] = val;
         }
+    fill_twiddles<M>(tws, bp.tw2048);
     static_for<0, kP / R1>([&](auto Bb) {
         dft<R1, -1, decltype(Bb)::value * R1, 1>(v);
     });
 
     float2* Es = E + (long)in.slice * tab.nplanes * kPlaneStride;
-    band_rest<M, -1>(v, buf, t, tw, [&](float2 (&w)[kP], auto Rc, auto NSc) {
+    const bool side = d_side(in.d);
+    const int lo = in.d.y, l = d_l(in.d), lg = d_lg(in.d);
+    const int pbase = d_plane(in.d, which) * kPlaneStride + lo;
+    band_rest<M, -1>(v, buf, tws, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
 #pragma unroll
         for (int b = 0; b < kP / R; ++b)
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                const int m = in.off + t + T * b + r * NS;
-                const int d = __ldg(tab.dest + m);
-                if (d >= 0) {
-                    const float2 val = w[b * R + r];
-                    Es[d] = make_float2(val.x * __ldg(tab.gre + m), val.y * __ldg(tab.gim + m));
+                const int m = t + T * b + r * NS;
+                const float2 val = w[b * R + r];
+                if (side) {
+                    const int d = __ldg(tab.dest + off + m);
+                    if (d >= 0)
+                        Es[d] = make_float2(val.x * __ldg(tab.gre + off + m),
+                                            val.y * __ldg(tab.gim + off + m));
+                } else {
+                    const int i = (m + l) & (M - 1);
+                    const float g = __ldg(tab.gre + off + m);
+                    if (i < lg && g != 0.f) Es[pbase + i] = cscale(val, g);
                 }
             }
     });
@@ -230,37 +324,40 @@ __device__ __forceinline__ int find_class(const BandSched& sc) {
     return c;
 }
 
-__global__ void __launch_bounds__(kBandThreads, 2)
-bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, BandCommon bc, BandSched sc,
+__global__ void __launch_bounds__(kBandThreads, kBandMinBlocks)
+bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant__ BandParams bp,
                  CoefPtr out) {
     extern __shared__ float4 smem_raw[];
     float2* smem = reinterpret_cast<float2*>(smem_raw);
-    const int c = find_class(sc);
-    switch (sc.M[c]) {
-    case 2048: band_fwd<2048>(X, tab, bc, sc, c, out, smem); break;
-    case 1024: band_fwd<1024>(X, tab, bc, sc, c, out, smem); break;
-    case 512:  band_fwd<512>(X, tab, bc, sc, c, out, smem); break;
-    case 256:  band_fwd<256>(X, tab, bc, sc, c, out, smem); break;
-    case 128:  band_fwd<128>(X, tab, bc, sc, c, out, smem); break;
-    case 64:   band_fwd<64>(X, tab, bc, sc, c, out, smem); break;
-    case 32:   band_fwd<32>(X, tab, bc, sc, c, out, smem); break;
+    float2* tws = smem + kBandData;
+    const int c = find_class(bp.sc);
+    switch (bp.sc.M[c]) {
+    case 2048: band_fwd<2048>(X, tab, bp, c, out, smem, tws); break;
+    case 1024: band_fwd<1024>(X, tab, bp, c, out, smem, tws); break;
+    case 512:  band_fwd<512>(X, tab, bp, c, out, smem, tws); break;
+    case 256:  band_fwd<256>(X, tab, bp, c, out, smem, tws); break;
+    case 128:  band_fwd<128>(X, tab, bp, c, out, smem, tws); break;
+    case 64:   band_fwd<64>(X, tab, bp, c, out, smem, tws); break;
+    case 32:   band_fwd<32>(X, tab, bp, c, out, smem, tws); break;
     default: break;
     }
 }
 
-__global__ void __launch_bounds__(kBandThreads, 2)
-bands_inv_kernel(CoefPtr in, InvTab tab, BandCommon bc, BandSched sc, float2* __restrict__ E) {
+__global__ void __launch_bounds__(kBandThreads, kBandMinBlocks)
+bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ BandParams bp,
+                 float2* __restrict__ E) {
     extern __shared__ float4 smem_raw[];
     float2* smem = reinterpret_cast<float2*>(smem_raw);
-    const int c = find_class(sc);
-    switch (sc.M[c]) {
-    case 2048: band_inv<2048>(in, tab, bc, sc, c, E, smem); break;
-    case 1024: band_inv<1024>(in, tab, bc, sc, c, E, smem); break;
-    case 512:  band_inv<512>(in, tab, bc, sc, c, E, smem); break;
-    case 256:  band_inv<256>(in, tab, bc, sc, c, E, smem); break;
-    case 128:  band_inv<128>(in, tab, bc, sc, c, E, smem); break;
-    case 64:   band_inv<64>(in, tab, bc, sc, c, E, smem); break;
-    case 32:   band_inv<32>(in, tab, bc, sc, c, E, smem); break;
+    float2* tws = smem + kBandData;
+    const int c = find_class(bp.sc);
+    switch (bp.sc.M[c]) {
+    case 2048: band_inv<2048>(in, tab, which, bp, c, E, smem, tws); break;
+    case 1024: band_inv<1024>(in, tab, which, bp, c, E, smem, tws); break;
+    case 512:  band_inv<512>(in, tab, which, bp, c, E, smem, tws); break;
+    case 256:  band_inv<256>(in, tab, which, bp, c, E, smem, tws); break;
+    case 128:  band_inv<128>(in, tab, which, bp, c, E, smem, tws); break;
+    case 64:   band_inv<64>(in, tab, which, bp, c, E, smem, tws); break;
+    case 32:   band_inv<32>(in, tab, which, bp, c, E, smem, tws); break;
     default: break;
     }
 }
@@ -285,19 +382,19 @@ BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, in
     return sc;
 }
 
-cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandCommon& bc,
-                             const BandSched& sc, CoefPtr out, cudaStream_t s) {
-    const int grid = sc.cta0[sc.ncls];
+cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParams& bp,
+                             CoefPtr out, cudaStream_t s) {
+    const int grid = bp.sc.cta0[bp.sc.ncls];
     if (grid <= 0) return cudaSuccess;
-    bands_fwd_kernel<<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bc, sc, out);
+    bands_fwd_kernel<<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bp, out);
     return cudaGetLastError();
 }
 
-cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, const BandCommon& bc,
-                             const BandSched& sc, float2* E, cudaStream_t s) {
-    const int grid = sc.cta0[sc.ncls];
+cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const BandParams& bp,
+                             float2* E, cudaStream_t s) {
+    const int grid = bp.sc.cta0[bp.sc.ncls];
     if (grid <= 0) return cudaSuccess;
-    bands_inv_kernel<<<grid, kBandThreads, kBandSmem, s>>>(in, tab, bc, sc, E);
+    bands_inv_kernel<<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E);
     return cudaGetLastError();
 }
 

@@ -26,7 +26,8 @@ struct cqt_tables {
     int cls_M[kMaxClasses], cls_nb[kMaxClasses], cls_first[kMaxClasses];
     FwdTab fwd[2];   // 0 analysis, 1 transpose of synthesis
     InvTab inv[2];   // 0 synthesis, 1 transpose of analysis
-    BandCommon bc;
+    const float2* tw2048;
+    int4 desc[kMaxBands];   // class order, see BandParams
     const float2* tw_hi;
     const float2* tw_lo;
     int max_planes;
@@ -90,8 +91,13 @@ int coef_ptr(const float* re, const float* im, int layout, CoefPtr* out) {
     return CQT_OK;
 }
 
-BandSched sched(const cqt_tables* t, int batch) {
-    return make_sched(t->ncls, t->cls_M, t->cls_nb, t->cls_first, batch);
+BandParams band_params(const cqt_tables* t, int batch) {
+    BandParams bp;
+    bp.sc = make_sched(t->ncls, t->cls_M, t->cls_nb, t->cls_first, batch);
+    bp.tw2048 = t->tw2048;
+    bp.ncoef = t->ncoef;
+    std::memcpy(bp.desc, t->desc, sizeof bp.desc);
+    return bp;
 }
 
 // one analysis-engine pass: real signal -> spectrum -> bands
@@ -101,7 +107,7 @@ int run_fwd_engine(const cqt_tables* t, int which, const float* sig, CoefPtr out
     float2* X = static_cast<float2*>(ws);
     cudaError_t e = launch_spectrum_fwd(sig, X, t->tw_hi, t->tw_lo, batch, s);
     if (e != cudaSuccess) return cuda_fail(e, "spectrum_fwd launch");
-    e = launch_bands_fwd(X, t->fwd[which], t->bc, sched(t, batch), out, s);
+    e = launch_bands_fwd(X, t->fwd[which], band_params(t, batch), out, s);
     if (e != cudaSuccess) return cuda_fail(e, "bands_fwd launch");
     return CQT_OK;
 }
@@ -111,7 +117,7 @@ int run_inv_engine(const cqt_tables* t, int which, CoefPtr in, float* sig, int b
                    void* ws, cudaStream_t s) {
     if (batch == 0) return CQT_OK;
     float2* E = static_cast<float2*>(ws);
-    cudaError_t e = launch_bands_inv(in, t->inv[which], t->bc, sched(t, batch), E, s);
+    cudaError_t e = launch_bands_inv(in, t->inv[which], which, band_params(t, batch), E, s);
     if (e != cudaSuccess) return cuda_fail(e, "bands_inv launch");
     e = launch_spectrum_inv(E, t->inv[which], sig, t->tw_hi, t->tw_lo, batch, s);
     if (e != cudaSuccess) return cuda_fail(e, "spectrum_inv launch");
@@ -185,6 +191,46 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
                     const int s = src[o + m];
                     if (s >= 0 && ((s & 0xFFFF) < lo || (s & 0xFFFF) >= lo + n))
                         return fail(CQT_ERR_ARG, "gather bin outside its band segment");
+                }
+            }
+        }
+    }
+    if (h->nbands > kMaxBands) return fail(CQT_ERR_ARG, "too many bands");
+    // the closed-form octave path must compute exactly what the tables say
+    for (int c = 0; c < h->nclasses; ++c) {
+        const int M = h->class_len[c];
+        for (int i = 0; i < h->class_count[c]; ++i) {
+            const int b = h->band_list[h->class_first[c] + i];
+            const int32_t* g = h->band_geom + 4 * b;
+            if (g[3] & 1) continue;
+            const int lo = g[0], l = g[1], lg = g[2];
+            const int psy = (g[3] >> 4) & 15, paa = (g[3] >> 8) & 15;
+            if (lo < 0 || l < 0 || l >= M || lg < 0 || lg > M || lo + lg > kHalf + 1 ||
+                psy >= h->sy_nplanes || paa >= h->aa_nplanes)
+                return fail(CQT_ERR_ARG, "band geometry out of range");
+            const int o = h->band_off[b];
+            for (int m = 0; m < M; ++m) {
+                const int ii = (m + l) & (M - 1);
+                const bool in_win = ii < lg;
+                const int bin = lo + ii;
+                for (int w = 0; w < 2; ++w) {   // analysis-engine sets
+                    const int s = (w ? h->as_src : h->an_src)[o + m];
+                    const float gn = (w ? h->as_gain : h->an_gain)[o + m];
+                    const bool ok = s >= 0 ? (in_win && s == bin) : gn == 0.f;
+                    if (!ok) return fail(CQT_ERR_ARG, "octave gather table disagrees with geometry");
+                }
+                for (int w = 0; w < 2; ++w) {   // synthesis-engine sets
+                    const int32_t* dst = w ? h->aa_dest : h->sy_dest;
+                    const float gr = (w ? h->aa_gre : h->sy_gre)[o + m];
+                    const float gi = (w ? h->aa_gim : h->sy_gim)[o + m];
+                    const uint8_t* mk = w ? h->aa_mask : h->sy_mask;
+                    const int pl = w ? paa : psy;
+                    const bool writes = in_win && gr != 0.f;
+                    if (writes != (dst[o + m] >= 0))
+                        return fail(CQT_ERR_ARG, "octave scatter table disagrees with geometry");
+                    if (writes && (dst[o + m] != pl * kPlaneStride + bin || gi != gr ||
+                                   !((mk[bin] >> pl) & 1)))
+                        return fail(CQT_ERR_ARG, "octave scatter slot disagrees with geometry");
                 }
             }
         }
@@ -271,7 +317,13 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
                        (const unsigned char*)P(i_sym), h->sy_nplanes};
     t->inv[1] = InvTab{(const int*)P(i_aad), (const float*)P(i_aar), (const float*)P(i_aai),
                        (const unsigned char*)P(i_aam), h->aa_nplanes};
-    t->bc = BandCommon{(const int*)P(i_blist), (const int*)P(i_boff), (const float2*)P(i_tw), nc};
+    t->tw2048 = (const float2*)P(i_tw);
+    for (int i = 0; i < h->nbands; ++i) {
+        const int b = h->band_list[i];
+        const int32_t* g = h->band_geom + 4 * b;
+        const bool side = g[3] & 1;
+        t->desc[i] = make_int4(h->band_off[b], side ? b : g[0], g[1] | (g[2] << 16), g[3]);
+    }
     t->tw_hi = (const float2*)P(i_hi);
     t->tw_lo = (const float2*)P(i_lo);
     t->max_planes = h->sy_nplanes > h->aa_nplanes ? h->sy_nplanes : h->aa_nplanes;
@@ -348,12 +400,13 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
         break;
     case 1:
         if ((rc = coef_ptr(c_re, c_im, layout, &cp))) return rc;
-        e = launch_bands_fwd(static_cast<const float2*>(ws), t->fwd[0], t->bc, sched(t, batch),
+        e = launch_bands_fwd(static_cast<const float2*>(ws), t->fwd[0], band_params(t, batch),
                              cp, s);
         break;
     case 2:
         if ((rc = coef_ptr(c_re, c_im, layout, &cp))) return rc;
-        e = launch_bands_inv(cp, t->inv[0], t->bc, sched(t, batch), static_cast<float2*>(ws), s);
+        e = launch_bands_inv(cp, t->inv[0], 0, band_params(t, batch), static_cast<float2*>(ws),
+                             s);
         break;
     case 3:
         if (!sig_out) return fail(CQT_ERR_ARG, "null output");

@@ -30,11 +30,18 @@ struct BandSched {         // CTA ranges of the block-length classes for one lau
     int batch;
 };
 
-struct BandCommon {
-    const int* band_list;  // band ids grouped by class
-    const int* band_off;   // heap offset of every band
+constexpr int kMaxBands = 160;
+
+// everything a band kernel needs besides the per-tap tables, passed by value
+// (kernel parameters live in the constant bank: no dependent global loads)
+struct BandParams {
+    BandSched sc;
     const float2* tw2048;  // W_2048^e, forward sign
     int ncoef;
+    // per band in class order: {heap offset, lo (octave) | band id (side),
+    // l | Lg << 16, flags: bit 0 side band, bits 4-7 synthesis plane,
+    // bits 8-11 adjoint plane}
+    int4 desc[kMaxBands];
 };
 
 struct CoefPtr {           // coefficient heap addressing
@@ -43,8 +50,14 @@ struct CoefPtr {           // coefficient heap addressing
     int interleaved;       // 0 planar [B, ncoef] x 2, 1 complex [B, ncoef]
 };
 
+// points held in registers per band-kernel thread (16 or 32); the band
+// schedules in bands.cu follow it
+#ifndef FCQT_BAND_P
+#define FCQT_BAND_P 32
+#endif
+constexpr int kBandP = FCQT_BAND_P;
 constexpr int kBandThreads = 256;
-constexpr int kBandCap = 8192;            // points per band CTA
+constexpr int kBandCap = kBandThreads * kBandP;   // points per band CTA
 constexpr int kSpecThreads = 512;
 
 BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, int batch);
@@ -55,9 +68,9 @@ cudaError_t launch_spectrum_fwd(const float* x, float2* X, const float2* tw_hi,
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, float* y,
                                 const float2* tw_hi, const float2* tw_lo,
                                 int batch, cudaStream_t s);
-cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandCommon& bc,
-                             const BandSched& sc, CoefPtr out, cudaStream_t s);
-cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, const BandCommon& bc,
-                             const BandSched& sc, float2* E, cudaStream_t s);
+cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParams& bp,
+                             CoefPtr out, cudaStream_t s);
+cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const BandParams& bp,
+                             float2* E, cudaStream_t s);
 
 }  // namespace fcqt

@@ -143,6 +143,25 @@ def build_tables(heap):
                        gim[s].astype(np.float32), maskp, nplanes)
     t["nplanes"] = max(v[4] for v in t["inv"].values())
 
+    # per band geometry for the closed-form octave path: lo, l, Lg, flags
+    geom = np.zeros((len(heap.bands), 4), np.int32)
+    nocts = sum(g[0].shape[0] for g in heap.groups)
+    for i, (M, o) in enumerate(heap.bands):
+        if i >= nocts:
+            geom[i] = (0, 0, 0, 1)              # side band: table path
+            continue
+        rg = bank.ranges[i + 1]                 # octave bands are windows 1..nb
+        lg = rg.size
+        flags = 0
+        for w, s in enumerate(INV_SETS):
+            d = t["inv"][s][0][o:o + M]
+            planes = np.unique(d[d >= 0] // PLANE_STRIDE)
+            if planes.size != 1:
+                raise RuntimeError("octave band %d spans several colour planes" % i)
+            flags |= int(planes[0]) << (4 + 4 * w)
+        geom[i] = (int(rg[0]), lg // 2, lg, flags)
+    t["band_geom"] = geom
+
     # band scheduling classes, largest block length first
     bands = heap.bands
     cls = []

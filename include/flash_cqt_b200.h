@@ -65,6 +65,12 @@ typedef struct cqt_host_tables {
     int32_t ncoef;
     const int32_t* band_off;    /* [nbands] heap offset of each band */
     const int32_t* band_list;   /* [nbands] band ids grouped by class */
+    /* [nbands][4] geometry {lo, l, Lg, flags}: an octave band's tap m maps to
+     * bin lo + ((m + l) mod M) when (m + l) mod M < Lg; flags bit 0 marks the
+     * side (DC / Nyquist) bands that use the per-tap tables instead, bits 4-7
+     * and 8-11 hold the colour plane of the band for synthesis and for the
+     * transpose of the analysis.  Upload checks it against the per-tap tables. */
+    const int32_t* band_geom;
     int32_t nclasses;           /* <= 8 block-length classes, largest first */
     const int32_t* class_len;   /* [nclasses] block length M (32..2048) */
     const int32_t* class_count; /* [nclasses] bands in the class */

@@ -103,10 +103,15 @@ def spectrum_inv(F):
     return y
 
 
-# band FFT configurations: (points per thread P, stage radices)
-BAND_CFG = {32: (32, (32,)), 64: (32, (32, 2)), 128: (32, (32, 4)),
-            256: (32, (32, 8)), 512: (32, (32, 16)), 1024: (32, (32, 32)),
-            2048: (32, (32, 32, 2))}
+# band FFT configurations: (points per thread P, stage radices), for the two
+# register budgets the band kernels compile for (FCQT_BAND_P = 32 or 16)
+BAND_CFG_P32 = {32: (32, (32,)), 64: (32, (32, 2)), 128: (32, (32, 4)),
+                256: (32, (32, 8)), 512: (32, (32, 16)), 1024: (32, (32, 32)),
+                2048: (32, (32, 32, 2))}
+BAND_CFG_P16 = {32: (16, (16, 2)), 64: (16, (16, 4)), 128: (16, (16, 8)),
+                256: (16, (16, 16)), 512: (16, (16, 16, 2)),
+                1024: (16, (16, 16, 4)), 2048: (16, (16, 16, 8))}
+BAND_CFG = BAND_CFG_P32
 
 
 def bands_fwd(X, tab, bands):

@@ -62,3 +62,23 @@ def test_engine_refuses_cpu():
         cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=65536)
         with pytest.raises(RuntimeError):
             cqt.fwd(torch.zeros(1, 65536))
+
+
+def test_valid_tables_pass_host_validation():
+    """Without a GPU the upload gets past every host-side check and fails only
+    at the first CUDA call, so the product tables satisfy the ABI contract
+    (closed-form octave geometry == per-tap tables, every index in range)."""
+    if torch.cuda.is_available():
+        pytest.skip("covered by the GPU tests when a device is present")
+    tabs = build_tables(HeapLayout(Filterbank([3, 4, 2], [8, 16, 32], 44100, 65536)))
+    with pytest.raises(RuntimeError, match=r"cqt_tables_upload failed \(-2\)"):
+        _native.DeviceTables(tabs, 0)
+
+
+def test_inconsistent_geometry_rejected():
+    tabs = build_tables(HeapLayout(Filterbank([3, 4, 2], [8, 16, 32], 44100, 65536)))
+    g = tabs["band_geom"].copy()
+    g[40, 1] += 1          # shift one octave band's window phase
+    tabs["band_geom"] = g
+    with pytest.raises(RuntimeError, match="disagrees with geometry"):
+        _native.DeviceTables(tabs, 0)

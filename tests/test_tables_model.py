@@ -59,11 +59,12 @@ def test_plane_assignment(tabs):
 
 def test_stockham_schedules_match_fft():
     rng = np.random.default_rng(3)
-    for M, (P, rad) in km.BAND_CFG.items():
-        assert np.prod(rad) == M and max(rad) <= P
-        v = rng.standard_normal((2, M)) + 1j * rng.standard_normal((2, M))
-        assert snr_db(np.fft.fft(v), km.stockham(v, rad, -1)) > 250
-        assert snr_db(np.fft.ifft(v) * M, km.stockham(v, rad, +1)) > 250
+    for cfg in (km.BAND_CFG_P16, km.BAND_CFG_P32):
+        for M, (P, rad) in cfg.items():
+            assert np.prod(rad) == M and max(rad) <= P and all(P % r == 0 for r in rad)
+            v = rng.standard_normal((2, M)) + 1j * rng.standard_normal((2, M))
+            assert snr_db(np.fft.fft(v), km.stockham(v, rad, -1)) > 250
+            assert snr_db(np.fft.ifft(v) * M, km.stockham(v, rad, +1)) > 250
 
 
 def test_packed_spectrum_model():
