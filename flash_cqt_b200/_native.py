@@ -1,17 +1,21 @@
 """ctypes binding of ``libflashcqt_b200.so`` (C ABI in include/flash_cqt_b200.h).
 
 The shared library is built in-tree by ``flash_cqt_b200.build`` (or by
-``__graft_entry__.build()``).  There is no fallback: if the library is missing
+``__graft_entry__.build()``); ``FLASH_CQT_B200_LIB`` may point at another
+build of the same ABI.  There is no fallback: if the library is missing
 or a call fails, a ``RuntimeError`` carrying the library's own message is
 raised.
 """
 import ctypes
+import os
 import pathlib
 import threading
 
 import numpy as np
 
-LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libflashcqt_b200.so"
+LIB_PATH = pathlib.Path(os.environ.get(
+    "FLASH_CQT_B200_LIB",
+    pathlib.Path(__file__).resolve().parent / "_lib" / "libflashcqt_b200.so"))
 
 CQT_LAYOUT_PLANAR = 0
 CQT_LAYOUT_COMPLEX = 1

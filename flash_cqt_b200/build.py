@@ -38,9 +38,16 @@ def _deps():
                   + list(INCLUDE.glob("*.h")))
 
 
-def build(force=False, verbose=False, ptxas_info=False):
-    BUILD.mkdir(exist_ok=True)
-    LIB.parent.mkdir(exist_ok=True)
+def build(force=False, verbose=False, ptxas_info=False, defines=(), lib=None,
+          build_dir=None):
+    """Compile and link; `defines` (e.g. ["FCQT_BAND_P=16"]) and an alternative
+    `lib` / `build_dir` produce variant builds of the same ABI."""
+    global BUILD, LIB
+    if lib is not None:
+        LIB = pathlib.Path(lib)
+        BUILD = pathlib.Path(build_dir) if build_dir else LIB.parent / "_build"
+    BUILD.mkdir(parents=True, exist_ok=True)
+    LIB.parent.mkdir(parents=True, exist_ok=True)
     cc = nvcc()
     hdr_time = max(p.stat().st_mtime for p in _deps())
     objs = []
@@ -51,7 +58,7 @@ def build(force=False, verbose=False, ptxas_info=False):
         if (not force and o.exists()
                 and o.stat().st_mtime >= max(s.stat().st_mtime, hdr_time)):
             continue
-        cmd = [cc, *ARCH, *FLAGS, "-c", str(s), "-o", str(o)]
+        cmd = [cc, *ARCH, *FLAGS, *["-D" + d for d in defines], "-c", str(s), "-o", str(o)]
         if ptxas_info:
             cmd += ["-Xptxas", "-v"]
         if verbose:
@@ -71,8 +78,10 @@ def main(argv=None):
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-info", action="store_true")
+    ap.add_argument("-D", dest="defines", action="append", default=[])
+    ap.add_argument("--lib", default=None)
     a = ap.parse_args(argv)
-    print(build(a.force, a.verbose, a.ptxas_info))
+    print(build(a.force, a.verbose, a.ptxas_info, a.defines, a.lib))
 
 
 if __name__ == "__main__":

@@ -35,7 +35,13 @@ namespace {
 
 constexpr int kP = kBandP;
 constexpr int kBandData = padded(kBandCap);              // float2 per CTA
-constexpr int kBandTw = 2048;                            // >= largest twiddle set
+// stage-3 twiddles (only M = 2048 has a third radix-2 stage with P = 32) come
+// from the global W_2048 table when FCQT_TW3_SMEM is 0, which keeps a CTA at
+// 75 KB of shared memory so two CTAs fit the 168 KB carveout
+#ifndef FCQT_TW3_SMEM
+#define FCQT_TW3_SMEM 0
+#endif
+constexpr int kBandTw = FCQT_TW3_SMEM ? 2048 : 1024;     // >= largest twiddle set
 constexpr int kBandSmem = (kBandData + kBandTw) * 8;
 constexpr int kBandMinBlocks = kP == 32 ? 2 : 4;        // 128 / 64 registers a thread
 
@@ -61,7 +67,7 @@ template <int M>
 struct TwLayout {
     static constexpr int R1 = Sched<M>::R1, R2 = Sched<M>::R2, R3 = Sched<M>::R3;
     static constexpr int n2 = (R2 - 1) * R1;
-    static constexpr int n3 = (R3 - 1) * R1 * R2;
+    static constexpr int n3 = FCQT_TW3_SMEM ? (R3 - 1) * R1 * R2 : 0;
     static_assert(n2 + n3 <= kBandTw, "twiddle rows exceed their shared slot");
 };
 
@@ -130,9 +136,14 @@ __device__ __forceinline__ Inst locate(const BandParams& bp, int c) {
 
 // stages 2 and 3 after stage 1's DFT; the last stage's outputs (index
 // n = j + r M / R_last, j = t + T b) go to `emit`
+struct Tw2048 {
+    const float2* w;
+    __device__ __forceinline__ float2 operator()(int e) const { return __ldg(w + (e & 2047)); }
+};
+
 template <int M, int S, class Emit>
 __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const float2* tws,
-                                          int t, Emit emit) {
+                                          const float2* bp_tw, int t, Emit emit) {
     constexpr int T = M / kP;
     using L = TwLayout<M>;
     constexpr int R1 = L::R1, R2 = L::R2, R3 = L::R3;
@@ -152,7 +163,11 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const fl
             __syncthreads();
             stage_load<M, T, R3>(v, buf, t);
             __syncthreads();
-            stage_compute_rows<M, T, R3, R1 * R2, S>(v, t, tws + L::n2);
+            if constexpr (FCQT_TW3_SMEM) {
+                stage_compute_rows<M, T, R3, R1 * R2, S>(v, t, tws + L::n2);
+            } else {
+                stage_compute<M, T, R3, R1 * R2, S, 2048>(v, t, Tw2048{bp_tw});
+            }
             emit(v, integral_constant<int, R3>{}, integral_constant<int, R1 * R2>{});
         }
     }
@@ -161,6 +176,11 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const fl
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
     const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(sa), "l"(gmem));
+}
+
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem) {
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(gmem));
 }
 
 __device__ __forceinline__ void cp_async_wait_all() {
@@ -239,7 +259,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     __syncthreads();   // the staged segment is dead; stage 1 reuses the buffer
 
     const long hb = (long)in.slice * bp.ncoef + off;
-    band_rest<M, +1>(v, buf, tws, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
+    band_rest<M, +1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
 #pragma unroll
@@ -269,33 +289,38 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     const int off = in.d.x;
     const long hb = (long)in.slice * bp.ncoef + off;
 
-    float2 v[kP];
-#pragma unroll
-    for (int b = 0; b < kP / R1; ++b)
-#pragma unroll
-        for (int r = 0; r < R1; ++r) {
-            const int nn = t + T * b + r * (M / R1);
-            float2 val = make_float2(0.f, 0.f);
-            if (in.valid) {
-                if (in_c.interleaved) {
-                    val = __ldg(reinterpret_cast<const float2*>(in_c.re) + hb + nn);
-                } else {
-                    val.x = __ldg(in_c.re + hb + nn);
-                    val.y = __ldg(in_c.im + hb + nn);
-                }
+    // stage the instance's M coefficients into shared memory with
+    // asynchronous copies (coalesced, no registers held while in flight)
+    if (in.valid) {
+        if (in_c.interleaved) {
+            const float2* src = reinterpret_cast<const float2*>(in_c.re) + hb;
+            for (int i = t; i < M; i += T) cp_async8(buf + PADI(i), src + i);
+        } else {
+            for (int i = t; i < M; i += T) {
+                cp_async4(reinterpret_cast<float*>(buf + PADI(i)), in_c.re + hb + i);
+                cp_async4(reinterpret_cast<float*>(buf + PADI(i)) + 1, in_c.im + hb + i);
             }
-            v[b * R1 + r] = val;
         }
+    }
     fill_twiddles<M>(tws, bp.tw2048);
+    cp_async_wait_all();
+    __syncthreads();
+    float2 v[kP];
+    stage_load<M, T, R1>(v, buf, t);
+    if (!in.valid) {
+#pragma unroll
+        for (int i = 0; i < kP; ++i) v[i] = make_float2(0.f, 0.f);
+    }
     static_for<0, kP / R1>([&](auto Bb) {
         dft<R1, -1, decltype(Bb)::value * R1, 1>(v);
     });
+    __syncthreads();   // stage 1 reads done; the exchange reuses the buffer
 
     float2* Es = E + (long)in.slice * tab.nplanes * kPlaneStride;
     const bool side = d_side(in.d);
     const int lo = in.d.y, l = d_l(in.d), lg = d_lg(in.d);
     const int pbase = d_plane(in.d, which) * kPlaneStride + lo;
-    band_rest<M, -1>(v, buf, tws, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
+    band_rest<M, -1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
 #pragma unroll

@@ -53,7 +53,7 @@ struct CoefPtr {           // coefficient heap addressing
 // points held in registers per band-kernel thread (16 or 32); the band
 // schedules in bands.cu follow it
 #ifndef FCQT_BAND_P
-#define FCQT_BAND_P 32
+#define FCQT_BAND_P 16
 #endif
 constexpr int kBandP = FCQT_BAND_P;
 constexpr int kBandThreads = 256;

@@ -111,7 +111,7 @@ BAND_CFG_P32 = {32: (32, (32,)), 64: (32, (32, 2)), 128: (32, (32, 4)),
 BAND_CFG_P16 = {32: (16, (16, 2)), 64: (16, (16, 4)), 128: (16, (16, 8)),
                 256: (16, (16, 16)), 512: (16, (16, 16, 2)),
                 1024: (16, (16, 16, 4)), 2048: (16, (16, 16, 8))}
-BAND_CFG = BAND_CFG_P32
+BAND_CFG = BAND_CFG_P16
 
 
 def bands_fwd(X, tab, bands):
