@@ -28,8 +28,7 @@ struct cqt_tables {
     InvTab inv[2];   // 0 synthesis, 1 transpose of analysis
     const float2* tw2048;
     int4 desc[kMaxBands];   // class order, see BandParams
-    const float2* tw_hi;
-    const float2* tw_lo;
+    SpecTables spec;
     int max_planes;
     void* blob;
 };
@@ -105,7 +104,7 @@ int run_fwd_engine(const cqt_tables* t, int which, const float* sig, CoefPtr out
                    int batch, void* ws, cudaStream_t s) {
     if (batch == 0) return CQT_OK;
     float2* X = static_cast<float2*>(ws);
-    cudaError_t e = launch_spectrum_fwd(sig, X, t->tw_hi, t->tw_lo, batch, s);
+    cudaError_t e = launch_spectrum_fwd(sig, X, t->spec, batch, s);
     if (e != cudaSuccess) return cuda_fail(e, "spectrum_fwd launch");
     e = launch_bands_fwd(X, t->fwd[which], band_params(t, batch), out, s);
     if (e != cudaSuccess) return cuda_fail(e, "bands_fwd launch");
@@ -119,7 +118,7 @@ int run_inv_engine(const cqt_tables* t, int which, CoefPtr in, float* sig, int b
     float2* E = static_cast<float2*>(ws);
     cudaError_t e = launch_bands_inv(in, t->inv[which], which, band_params(t, batch), E, s);
     if (e != cudaSuccess) return cuda_fail(e, "bands_inv launch");
-    e = launch_spectrum_inv(E, t->inv[which], sig, t->tw_hi, t->tw_lo, batch, s);
+    e = launch_spectrum_inv(E, t->inv[which], sig, t->spec, batch, s);
     if (e != cudaSuccess) return cuda_fail(e, "spectrum_inv launch");
     return CQT_OK;
 }
@@ -277,6 +276,9 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     size_t i_aad = add(h->aa_dest, nI), i_aar = add(h->aa_gre, nI), i_aai = add(h->aa_gim, nI);
     size_t i_aam = add(h->aa_mask, maskB);
     size_t i_tw = add(h->tw2048, 2048 * 8), i_hi = add(h->tw_hi, 256 * 8), i_lo = add(h->tw_lo, 256 * 8);
+    std::vector<float2> rows(spectrum_twiddle_count());
+    spectrum_twiddle_rows(rows.data());
+    size_t i_rows = add(rows.data(), rows.size() * sizeof(float2));
 
     void* blob = nullptr;
     e = cudaMalloc(&blob, total);
@@ -324,8 +326,7 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
         const bool side = g[3] & 1;
         t->desc[i] = make_int4(h->band_off[b], side ? b : g[0], g[1] | (g[2] << 16), g[3]);
     }
-    t->tw_hi = (const float2*)P(i_hi);
-    t->tw_lo = (const float2*)P(i_lo);
+    t->spec = SpecTables{(const float2*)P(i_hi), (const float2*)P(i_lo), (const float2*)P(i_rows)};
     t->max_planes = h->sy_nplanes > h->aa_nplanes ? h->sy_nplanes : h->aa_nplanes;
     t->blob = blob;
     *out = t;
@@ -396,7 +397,7 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
     switch (stage) {
     case 0:
         if (!sig_in) return fail(CQT_ERR_ARG, "null input");
-        e = launch_spectrum_fwd(sig_in, static_cast<float2*>(ws), t->tw_hi, t->tw_lo, batch, s);
+        e = launch_spectrum_fwd(sig_in, static_cast<float2*>(ws), t->spec, batch, s);
         break;
     case 1:
         if ((rc = coef_ptr(c_re, c_im, layout, &cp))) return rc;
@@ -410,8 +411,8 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
         break;
     case 3:
         if (!sig_out) return fail(CQT_ERR_ARG, "null output");
-        e = launch_spectrum_inv(static_cast<const float2*>(ws), t->inv[0], sig_out, t->tw_hi,
-                                t->tw_lo, batch, s);
+        e = launch_spectrum_inv(static_cast<const float2*>(ws), t->inv[0], sig_out, t->spec,
+                                batch, s);
         break;
     default:
         return fail(CQT_ERR_ARG, "unknown stage");

@@ -58,16 +58,23 @@ struct CoefPtr {           // coefficient heap addressing
 constexpr int kBandP = FCQT_BAND_P;
 constexpr int kBandThreads = 256;
 constexpr int kBandCap = kBandThreads * kBandP;   // points per band CTA
-constexpr int kSpecThreads = 512;
 
 BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, int batch);
 
 cudaError_t init_kernel_attributes();
-cudaError_t launch_spectrum_fwd(const float* x, float2* X, const float2* tw_hi,
-                                const float2* tw_lo, int batch, cudaStream_t s);
+struct SpecTables {        // packed-spectrum engine twiddles (device)
+    const float2* hi;      // W_65536^(256 e), e < 256
+    const float2* lo;      // W_65536^e, e < 256
+    const float2* rows;    // per-stage twiddle rows (spectrum_twiddle_rows)
+};
+
+int spectrum_twiddle_count();
+void spectrum_twiddle_rows(float2* out);   // host, double precision
+
+cudaError_t launch_spectrum_fwd(const float* x, float2* X, const SpecTables& st, int batch,
+                                cudaStream_t s);
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, float* y,
-                                const float2* tw_hi, const float2* tw_lo,
-                                int batch, cudaStream_t s);
+                                const SpecTables& st, int batch, cudaStream_t s);
 cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParams& bp,
                              CoefPtr out, cudaStream_t s);
 cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const BandParams& bp,

@@ -8,24 +8,59 @@
 //   CTA 0 transforms u0[n] = z[n] + z[n + 16384]               -> Z[2k]
 //   CTA 1 transforms u1[n] = (z[n] - z[n + 16384]) W_32768^n   -> Z[2k + 1]
 // so each CTA holds a 16384-point problem (132 KB with padding) entirely in
-// shared memory, runs it as Stockham stages 32 x 32 x 16 (512 threads, 32
-// points each), and then untangles the (q, L - q) bin pairs of its parity --
-// which are all local -- into the real spectrum X[q] (spectral recovery of
-// fused.py:311-328, done once per bin instead of once per router tap).
+// shared memory and runs it as Stockham stages (16 x 16 x 16 x 4 with 1024
+// threads of 16 points, or 32 x 32 x 16 with 512 threads of 32 points),
+// then untangles the (q, L - q) bin pairs of its parity -- which are all
+// local -- into the real spectrum X[q] (spectral recovery of fused.py:311-328,
+// done once per bin instead of once per router tap).
 // The inverse mirrors it: each CTA rebuilds the packed spectrum from the
 // colour planes on the fly (quads {n, 16384 - n, 16384 + n, 32768 - n} close
 // under both the retangle and the DIF maps), forms its DIF half, runs the
 // inverse Stockham stages and stores z[2m + h] de-interleaved into y.
+//
+// Stage twiddles W_{NS R}^{r k} come from shared rows that every warp reads
+// without bank conflicts: direct rows [r][k] for spans NS <= 32, and for
+// larger spans a split W^{r k} = lo[r][k mod 32] * hi[r][k / 32] (lo rows are
+// read lane-consecutive, hi rows are warp-uniform broadcasts).  The library
+// generates the rows in double precision at table upload.
+#include <cmath>
+
 #include "engine.cuh"
 #include "internal.h"
 
 namespace fcqt {
 
+#ifndef FCQT_SPEC_P
+#define FCQT_SPEC_P 16
+#endif
+
 namespace {
 
-constexpr int kSpecP = 32;
-constexpr int kSpecT = kSpecThreads;
-constexpr int kSpecSmem = padded(kQuarter) * 8 + 2 * 256 * 8;
+template <int P> struct SpecCfg;
+template <> struct SpecCfg<32> {
+    static constexpr int T = 512, NST = 3, R1 = 32, R2 = 32, R3 = 16, R4 = 1;
+};
+template <> struct SpecCfg<16> {
+    static constexpr int T = 1024, NST = 4, R1 = 16, R2 = 16, R3 = 16, R4 = 4;
+};
+constexpr int kSpecP = FCQT_SPEC_P;
+using SC = SpecCfg<kSpecP>;
+constexpr int kSpecT = SC::T;
+
+constexpr int sR(int s) { return s == 1 ? SC::R1 : s == 2 ? SC::R2 : s == 3 ? SC::R3 : SC::R4; }
+constexpr int sNS(int s) { return s <= 1 ? 1 : sNS(s - 1) * sR(s - 1); }
+constexpr bool sSplit(int s) { return sNS(s) > 32; }
+constexpr int sSize(int s) {
+    return (s < 2 || s > SC::NST) ? 0
+           : sSplit(s) ? sR(s) * 32 + sR(s) * (sNS(s) / 32)
+                       : (sR(s) - 1) * sNS(s);
+}
+constexpr int sOff(int s) { return s <= 2 ? 0 : sOff(s - 1) + sSize(s - 1); }
+constexpr int kSpecTwTotal = sOff(SC::NST + 1);
+static_assert(sNS(SC::NST) * sR(SC::NST) == kQuarter, "stage radices must multiply to 16384");
+
+constexpr int kSpecData = padded(kQuarter);
+constexpr int kSpecSmem = (kSpecData + 512 + kSpecTwTotal) * 8;
 
 struct Tw64k {
     const float2* hi;
@@ -33,63 +68,87 @@ struct Tw64k {
     __device__ __forceinline__ float2 operator()(int e) const { return tw64k(hi, lo, e); }
 };
 
-__device__ __forceinline__ void load_twiddles(float2* hi, float2* lo,
-                                              const float2* ghi, const float2* glo) {
-    const int t = threadIdx.x;
-    if (t < 256) hi[t] = ghi[t];
-    else if (t < 512) lo[t - 256] = glo[t - 256];
+__device__ __forceinline__ void load_tables(float2* sm_hilo, float2* sm_tw, const float2* ghi,
+                                            const float2* glo, const float2* gtw) {
+    for (int i = threadIdx.x; i < 512 + kSpecTwTotal; i += kSpecT) {
+        if (i < 256) sm_hilo[i] = __ldg(ghi + i);
+        else if (i < 512) sm_hilo[i] = __ldg(glo + i - 256);
+        else sm_tw[i - 512] = __ldg(gtw + i - 512);
+    }
 }
 
-// the three Stockham stages of the 16384-point sub-transform after stage 1's
-// DFT; S = -1 forward (result left in shared memory, natural order),
-// S = +1 inverse (result handed to the caller's store functor)
-template <int S, class Store>
-__device__ __forceinline__ void quarter_stages_2_3(float2 (&v)[kSpecP], float2* buf,
-                                                   const Tw64k& tw, Store store) {
-    const int t = threadIdx.x;
-    // stage 1 output (R = 32, NS = 1)
-    stage_store<kQuarter, kSpecT, 32, 1>(v, buf, t);
-    __syncthreads();
-    // stage 2: R = 32, NS = 32
-    stage_load<kQuarter, kSpecT, 32>(v, buf, t);
-    __syncthreads();
-    stage_compute<kQuarter, kSpecT, 32, 32, S, 65536>(v, t, tw);
-    stage_store<kQuarter, kSpecT, 32, 32>(v, buf, t);
-    __syncthreads();
-    // stage 3: R = 16, NS = 1024, two butterflies per thread
-    stage_load<kQuarter, kSpecT, 16>(v, buf, t);
-    __syncthreads();
-    stage_compute<kQuarter, kSpecT, 16, 1024, S, 65536>(v, t, tw);
-    store(v);
+// twiddle and DFT of stage s (all butterflies of the thread)
+template <int s, int S>
+__device__ __forceinline__ void spec_compute(float2 (&v)[kSpecP], int t, const float2* tws) {
+    constexpr int R = sR(s), NS = sNS(s), off = sOff(s);
+    static_for<0, kSpecP / R>([&](auto Bb) {
+        constexpr int b = decltype(Bb)::value;
+        if constexpr (s > 1) {
+            const int k = (t + kSpecT * b) % NS;
+#pragma unroll
+            for (int r = 1; r < R; ++r) {
+                float2 w;
+                if constexpr (sSplit(s)) {
+                    w = cmul(tws[off + r * 32 + (k & 31)],
+                             tws[off + R * 32 + r * (NS / 32) + (k >> 5)]);
+                } else {
+                    w = tws[off + (r - 1) * NS + k];
+                }
+                if constexpr (S > 0) w.y = -w.y;
+                v[b * R + r] = cmul(v[b * R + r], w);
+            }
+        }
+        dft<R, S, b * R, 1>(v);
+    });
 }
 
-__global__ void __launch_bounds__(kSpecThreads, 1)
+// stages s..NST (stage s - 1 is computed and held in v); `fin` receives the
+// last stage's outputs, index n = j + r NS_last for j = t + T b
+template <int s, int S, class Fin>
+__device__ __forceinline__ void spec_stages(float2 (&v)[kSpecP], float2* buf, const float2* tws,
+                                            int t, Fin fin) {
+    if constexpr (s > SC::NST) {
+        fin(v);
+    } else {
+        stage_store<kQuarter, kSpecT, sR(s - 1), sNS(s - 1)>(v, buf, t);
+        __syncthreads();
+        stage_load<kQuarter, kSpecT, sR(s)>(v, buf, t);
+        __syncthreads();
+        spec_compute<s, S>(v, t, tws);
+        spec_stages<s + 1, S>(v, buf, tws, t, fin);
+    }
+}
+
+__global__ void __launch_bounds__(kSpecT, 1)
 spectrum_fwd_kernel(const float* __restrict__ x, float2* __restrict__ X,
-                    const float2* __restrict__ ghi, const float2* __restrict__ glo) {
+                    const float2* __restrict__ ghi, const float2* __restrict__ glo,
+                    const float2* __restrict__ gtw) {
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
-    float2* hi = buf + padded(kQuarter);
-    float2* lo = hi + 256;
+    float2* hl = buf + kSpecData;
+    float2* tws = hl + 512;
     const int h = blockIdx.x & 1;
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
-    load_twiddles(hi, lo, ghi, glo);
+    load_tables(hl, tws, ghi, glo, gtw);
     __syncthreads();
-    const Tw64k tw{hi, lo};
+    const Tw64k tw{hl, hl + 256};
 
     // stage 1 inputs straight from global: the radix-2 DIF split of z
     const float2* z = reinterpret_cast<const float2*>(x + slice * kSlice);
     float2 v[kSpecP];
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
-        const int n = t + kSpecT * r;
-        const float2 a = __ldg(z + n);
-        const float2 b = __ldg(z + n + kQuarter);
-        v[r] = h == 0 ? cadd(a, b) : cmul(csub(a, b), tw(2 * n));
-    }
-    dft<32, -1, 0, 1>(v);
-    quarter_stages_2_3<-1>(v, buf, tw, [&](float2 (&w)[kSpecP]) {
-        stage_store<kQuarter, kSpecT, 16, 1024>(w, buf, t);
+    for (int b = 0; b < kSpecP / SC::R1; ++b)
+#pragma unroll
+        for (int r = 0; r < SC::R1; ++r) {
+            const int n = t + kSpecT * b + r * (kQuarter / SC::R1);
+            const float2 a = __ldg(z + n);
+            const float2 c = __ldg(z + n + kQuarter);
+            v[b * SC::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
+        }
+    spec_compute<1, -1>(v, t, tws);
+    spec_stages<2, -1>(v, buf, tws, t, [&](float2 (&w)[kSpecP]) {
+        stage_store<kQuarter, kSpecT, sR(SC::NST), sNS(SC::NST)>(w, buf, t);
     });
     __syncthreads();
 
@@ -102,17 +161,16 @@ spectrum_fwd_kernel(const float* __restrict__ x, float2* __restrict__ X,
         const float2 zb = buf[PADI(kq)];
         const int q = 2 * kp + h;
         const float2 w = tw(q);
-        const float2 sq = cadd(zq, cconj(zb));   // 2 E[q]
-        const float2 dq = csub(zq, cconj(zb));   // 2 i O[q] / ... (before W)
+        const float2 sq = cadd(zq, cconj(zb));
+        const float2 dq = csub(zq, cconj(zb));
         const float2 wd = cmul(w, dq);
-        // X[q] = (sq - i w dq) / 2
+        // X[q] = (sq - i W^q dq) / 2
         Xs[q] = make_float2(0.5f * (sq.x + wd.y), 0.5f * (sq.y - wd.x));
         if (kq != kp || q == 0) {
-            // X[L - q] = (conj(sq) + i conj(w) conj(dq) ... ) / 2, written via
-            // the partner's own sums: sb = zb + conj zq, db = zb - conj zq
+            // X[L - q] = (conj(sq) + i conj(W^q) (-conj(dq))) / 2
             const float2 sb = cconj(sq);
             const float2 db = make_float2(-dq.x, dq.y);
-            const float2 wdb = cmulc(db, w);     // conj(w) * db
+            const float2 wdb = cmulc(db, w);
             Xs[kHalf - q] = make_float2(0.5f * (sb.x - wdb.y), 0.5f * (sb.y + wdb.x));
         }
     }
@@ -139,24 +197,25 @@ __device__ __forceinline__ float2 plane_sum(const float2* __restrict__ Es,
 __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
     const float2 e = make_float2(0.5f * (a.x + b.x), 0.5f * (a.y - b.y));
     const float2 d = make_float2(0.5f * (a.x - b.x), 0.5f * (a.y + b.y));
-    const float2 o = cmulc(d, wq);               // d * conj(W_N^q)
+    const float2 o = cmulc(d, wq);
     return make_float2(e.x - o.y, e.y + o.x);
 }
 
-__global__ void __launch_bounds__(kSpecThreads, 1)
+__global__ void __launch_bounds__(kSpecT, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restrict__ mask,
                     float* __restrict__ y, const float2* __restrict__ ghi,
-                    const float2* __restrict__ glo, int nplanes) {
+                    const float2* __restrict__ glo, const float2* __restrict__ gtw,
+                    int nplanes) {
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
-    float2* hi = buf + padded(kQuarter);
-    float2* lo = hi + 256;
+    float2* hl = buf + kSpecData;
+    float2* tws = hl + 512;
     const int h = blockIdx.x & 1;
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
-    load_twiddles(hi, lo, ghi, glo);
+    load_tables(hl, tws, ghi, glo, gtw);
     __syncthreads();
-    const Tw64k tw{hi, lo};
+    const Tw64k tw{hl, hl + 256};
     const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
 
     // quads {n, L - n, Q + n, Q - n}: four bins in, u_h[n] and u_h[Q - n] out
@@ -172,8 +231,7 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
         }
         const float2 z0 = retangle(fA, fB, tw(n));
         const float2 z1 = retangle(fC, fD, tw(kQuarter + n));
-        float2 un = h == 0 ? cadd(z0, z1) : cmulc(csub(z0, z1), tw(2 * n));
-        buf[PADI(n)] = un;
+        buf[PADI(n)] = h == 0 ? cadd(z0, z1) : cmulc(csub(z0, z1), tw(2 * n));
         if (m != n) {
             const float2 z2 = retangle(fD, fC, tw(m));
             const float2 z3 = retangle(fB, fA, tw(kQuarter + m));
@@ -183,38 +241,62 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
     __syncthreads();
 
     float2 v[kSpecP];
-    stage_load<kQuarter, kSpecT, 32>(v, buf, t);
+    stage_load<kQuarter, kSpecT, SC::R1>(v, buf, t);
     __syncthreads();
-    dft<32, +1, 0, 1>(v);
+    spec_compute<1, +1>(v, t, tws);
     float2* ys = reinterpret_cast<float2*>(y + slice * kSlice);
     const float inv = 1.0f / (float)kHalf;
-    quarter_stages_2_3<+1>(v, buf, tw, [&](float2 (&w)[kSpecP]) {
-        // last stage output index n = j + 1024 r (NS = 1024 = M / R)
+    spec_stages<2, +1>(v, buf, tws, t, [&](float2 (&w)[kSpecP]) {
+        constexpr int R = sR(SC::NST), NS = sNS(SC::NST);
 #pragma unroll
-        for (int b = 0; b < 2; ++b)
+        for (int b = 0; b < kSpecP / R; ++b)
 #pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                const int nn = t + kSpecT * b + 1024 * r;
-                ys[2 * nn + h] = cscale(w[b * 16 + r], inv);
+            for (int r = 0; r < R; ++r) {
+                const int nn = t + kSpecT * b + NS * r;
+                ys[2 * nn + h] = cscale(w[b * R + r], inv);
             }
     });
 }
 
 }  // namespace
 
-cudaError_t launch_spectrum_fwd(const float* x, float2* X, const float2* tw_hi,
-                                const float2* tw_lo, int batch, cudaStream_t s) {
+int spectrum_twiddle_count() { return kSpecTwTotal; }
+
+// stage twiddle rows, forward sign, double precision rounded once
+void spectrum_twiddle_rows(float2* out) {
+    const double two_pi = 6.283185307179586476925286766559;
+    auto w = [&](long e, long base) {
+        const double a = -two_pi * (double)(e % base) / (double)base;
+        return make_float2((float)std::cos(a), (float)std::sin(a));
+    };
+    for (int s = 2; s <= SC::NST; ++s) {
+        const int R = sR(s), NS = sNS(s), off = sOff(s);
+        const long base = (long)NS * R;
+        if (sSplit(s)) {
+            for (int r = 0; r < R; ++r)
+                for (int k = 0; k < 32; ++k) out[off + r * 32 + k] = w((long)r * k, base);
+            for (int r = 0; r < R; ++r)
+                for (int k = 0; k < NS / 32; ++k)
+                    out[off + R * 32 + r * (NS / 32) + k] = w((long)r * 32 * k, base);
+        } else {
+            for (int r = 1; r < R; ++r)
+                for (int k = 0; k < NS; ++k) out[off + (r - 1) * NS + k] = w((long)r * k, base);
+        }
+    }
+}
+
+cudaError_t launch_spectrum_fwd(const float* x, float2* X, const SpecTables& st, int batch,
+                                cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    spectrum_fwd_kernel<<<2 * batch, kSpecThreads, kSpecSmem, s>>>(x, X, tw_hi, tw_lo);
+    spectrum_fwd_kernel<<<2 * batch, kSpecT, kSpecSmem, s>>>(x, X, st.hi, st.lo, st.rows);
     return cudaGetLastError();
 }
 
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, float* y,
-                                const float2* tw_hi, const float2* tw_lo,
-                                int batch, cudaStream_t s) {
+                                const SpecTables& st, int batch, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    spectrum_inv_kernel<<<2 * batch, kSpecThreads, kSpecSmem, s>>>(
-        E, tab.mask, y, tw_hi, tw_lo, tab.nplanes);
+    spectrum_inv_kernel<<<2 * batch, kSpecT, kSpecSmem, s>>>(E, tab.mask, y, st.hi, st.lo,
+                                                             st.rows, tab.nplanes);
     return cudaGetLastError();
 }
 

@@ -43,7 +43,9 @@ def stockham(u, radices, sign):
     return u
 
 
-SPEC_RADICES = (32, 32, 16)
+SPEC_RADICES_P32 = (32, 32, 16)
+SPEC_RADICES_P16 = (16, 16, 16, 4)
+SPEC_RADICES = SPEC_RADICES_P16
 
 
 def spectrum_fwd(x):

@@ -68,6 +68,10 @@ def test_stockham_schedules_match_fft():
 
 
 def test_packed_spectrum_model():
+    v = np.random.default_rng(5).standard_normal((2, 16384)) + 0j
+    for rad in (km.SPEC_RADICES_P16, km.SPEC_RADICES_P32):
+        assert np.prod(rad) == 16384
+        assert snr_db(np.fft.fft(v), km.stockham(v, rad, -1)) > 250
     x = x_noise().astype(np.float64)
     X = km.spectrum_fwd(x)
     assert snr_db(np.fft.rfft(x), X) > 250
