@@ -34,7 +34,8 @@ namespace fcqt {
 namespace {
 
 constexpr int kP = kBandP;
-constexpr int kBandData = padded(kBandCap);              // float2 per CTA
+constexpr int kSH = kP == 32 ? 5 : 4;                    // shared padding shift
+constexpr int kBandData = padded<kSH>(kBandCap);         // float2 per CTA
 // stage-3 twiddles (only M = 2048 has a third radix-2 stage with P = 32) come
 // from the global W_2048 table when FCQT_TW3_SMEM is 0, which keeps a CTA at
 // 75 KB of shared memory so two CTAs fit the 168 KB carveout
@@ -151,17 +152,17 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const fl
     if constexpr (R2 == 1) {
         emit(v, integral_constant<int, R1>{}, integral_constant<int, 1>{});
     } else {
-        stage_store<M, T, R1, 1>(v, buf, t);
+        stage_store<M, T, R1, 1, kSH>(v, buf, t);
         __syncthreads();
-        stage_load<M, T, R2>(v, buf, t);
+        stage_load<M, T, R2, kSH>(v, buf, t);
         __syncthreads();
         stage_compute_rows<M, T, R2, R1, S>(v, t, tws);
         if constexpr (R3 == 1) {
             emit(v, integral_constant<int, R2>{}, integral_constant<int, R1>{});
         } else {
-            stage_store<M, T, R2, R1>(v, buf, t);
+            stage_store<M, T, R2, R1, kSH>(v, buf, t);
             __syncthreads();
-            stage_load<M, T, R3>(v, buf, t);
+            stage_load<M, T, R3, kSH>(v, buf, t);
             __syncthreads();
             if constexpr (FCQT_TW3_SMEM) {
                 stage_compute_rows<M, T, R3, R1 * R2, S>(v, t, tws + L::n2);
@@ -201,7 +202,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     constexpr int R1 = Sched<M>::R1;
     const Inst in = locate<M>(bp, c);
     const int t = in.t;
-    float2* buf = smem + in.il * padded(M);
+    float2* buf = smem + in.il * padded<kSH>(M);
     const float2* Xs = X + (long)in.slice * kPlaneStride;
     const int off = in.d.x;
     const bool side = d_side(in.d);
@@ -218,7 +219,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
             lo = in.d.y;
             n = d_lg(in.d);
         }
-        for (int i = t; i < n; i += T) cp_async8(buf + PADI(i), Xs + lo + i);
+        for (int i = t; i < n; i += T) cp_async8(buf + PADI<kSH>(i), Xs + lo + i);
     }
     fill_twiddles<M>(tws, bp.tw2048);
     // stage 1 taps: element r of butterfly b is tap t + T b + r M / R1
@@ -247,7 +248,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
         const int s = src[i];
         float2 val = make_float2(0.f, 0.f);
         if (s >= 0) {
-            float2 xv = buf[PADI(s & 0xFFFF)];
+            float2 xv = buf[PADI<kSH>(s & 0xFFFF)];
             if (s & 0x10000) xv.y = -xv.y;
             val = cscale(xv, gain[i]);
         }
@@ -285,7 +286,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     constexpr int R1 = Sched<M>::R1;
     const Inst in = locate<M>(bp, c);
     const int t = in.t;
-    float2* buf = smem + in.il * padded(M);
+    float2* buf = smem + in.il * padded<kSH>(M);
     const int off = in.d.x;
     const long hb = (long)in.slice * bp.ncoef + off;
 
@@ -294,11 +295,11 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     if (in.valid) {
         if (in_c.interleaved) {
             const float2* src = reinterpret_cast<const float2*>(in_c.re) + hb;
-            for (int i = t; i < M; i += T) cp_async8(buf + PADI(i), src + i);
+            for (int i = t; i < M; i += T) cp_async8(buf + PADI<kSH>(i), src + i);
         } else {
             for (int i = t; i < M; i += T) {
-                cp_async4(reinterpret_cast<float*>(buf + PADI(i)), in_c.re + hb + i);
-                cp_async4(reinterpret_cast<float*>(buf + PADI(i)) + 1, in_c.im + hb + i);
+                cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)), in_c.re + hb + i);
+                cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)) + 1, in_c.im + hb + i);
             }
         }
     }
@@ -306,7 +307,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     cp_async_wait_all();
     __syncthreads();
     float2 v[kP];
-    stage_load<M, T, R1>(v, buf, t);
+    stage_load<M, T, R1, kSH>(v, buf, t);
     if (!in.valid) {
 #pragma unroll
         for (int i = 0; i < kP; ++i) v[i] = make_float2(0.f, 0.f);

@@ -9,8 +9,11 @@
 // After the last stage the result is in natural order, so the first stage can
 // read straight from global memory and the last stage can write straight to
 // global memory, both coalesced across consecutive j.  Between stages the
-// data goes through shared memory with one float2 of padding every 32 (PADI),
-// which makes every stage's read and write pattern free of bank conflicts.
+// data goes through shared memory with one float2 of padding every 2^SH
+// elements (PADI<SH>); with SH = log2(points per thread) every stage's read
+// and write pattern is free of bank conflicts (64-bit accesses are served
+// per half warp, so the stride-R stores of a radix-R first stage need R
+// distinct bank pairs within 16 lanes).
 #pragma once
 #include "fft_core.cuh"
 
@@ -22,8 +25,10 @@ constexpr int kQuarter = kHalf / 2;      // per-CTA sub-transform length
 constexpr int kPlaneStride = kHalf + 8;  // complex elements per spectrum row / colour plane
 constexpr int kMaxPlanes = 4;
 
-__host__ __device__ constexpr int padded(int n) { return n + (n >> 5); }
-__device__ __forceinline__ int PADI(int i) { return i + (i >> 5); }
+template <int SH = 5>
+__host__ __device__ constexpr int padded(int n) { return n + (n >> SH); }
+template <int SH = 5>
+__device__ __forceinline__ int PADI(int i) { return i + (i >> SH); }
 
 // W_65536^e from two 256-entry tables in shared memory: hi[e >> 8] * lo[e & 255]
 __device__ __forceinline__ float2 tw64k(const float2* hi, const float2* lo, int e) {
@@ -33,24 +38,24 @@ __device__ __forceinline__ float2 tw64k(const float2* hi, const float2* lo, int 
 // ---------------------------------------------------------------- stages
 // Read the inputs of a radix-R stage of length M for butterflies
 // j = t + T * b (b < P / R) from a padded shared buffer.
-template <int M, int T, int R, int P>
+template <int M, int T, int R, int SH, int P>
 __device__ __forceinline__ void stage_load(float2 (&v)[P], const float2* buf, int t) {
 #pragma unroll
     for (int b = 0; b < P / R; ++b)
 #pragma unroll
         for (int r = 0; r < R; ++r)
-            v[b * R + r] = buf[PADI(t + T * b + r * (M / R))];
+            v[b * R + r] = buf[PADI<SH>(t + T * b + r * (M / R))];
 }
 
 // Write the outputs of a radix-R stage with span NS to a padded shared buffer.
-template <int M, int T, int R, int NS, int P>
+template <int M, int T, int R, int NS, int SH, int P>
 __device__ __forceinline__ void stage_store(const float2 (&v)[P], float2* buf, int t) {
 #pragma unroll
     for (int b = 0; b < P / R; ++b) {
         const int j = t + T * b;
         const int base = (j / NS) * NS * R + (j % NS);
 #pragma unroll
-        for (int r = 0; r < R; ++r) buf[PADI(base + r * NS)] = v[b * R + r];
+        for (int r = 0; r < R; ++r) buf[PADI<SH>(base + r * NS)] = v[b * R + r];
     }
 }
 

@@ -59,7 +59,8 @@ constexpr int sOff(int s) { return s <= 2 ? 0 : sOff(s - 1) + sSize(s - 1); }
 constexpr int kSpecTwTotal = sOff(SC::NST + 1);
 static_assert(sNS(SC::NST) * sR(SC::NST) == kQuarter, "stage radices must multiply to 16384");
 
-constexpr int kSpecData = padded(kQuarter);
+constexpr int kSH = kSpecP == 32 ? 5 : 4;    // shared padding shift
+constexpr int kSpecData = padded<kSH>(kQuarter);
 constexpr int kSpecSmem = (kSpecData + 512 + kSpecTwTotal) * 8;
 
 struct Tw64k {
@@ -110,9 +111,9 @@ __device__ __forceinline__ void spec_stages(float2 (&v)[kSpecP], float2* buf, co
     if constexpr (s > SC::NST) {
         fin(v);
     } else {
-        stage_store<kQuarter, kSpecT, sR(s - 1), sNS(s - 1)>(v, buf, t);
+        stage_store<kQuarter, kSpecT, sR(s - 1), sNS(s - 1), kSH>(v, buf, t);
         __syncthreads();
-        stage_load<kQuarter, kSpecT, sR(s)>(v, buf, t);
+        stage_load<kQuarter, kSpecT, sR(s), kSH>(v, buf, t);
         __syncthreads();
         spec_compute<s, S>(v, t, tws);
         spec_stages<s + 1, S>(v, buf, tws, t, fin);
@@ -148,7 +149,7 @@ spectrum_fwd_kernel(const float* __restrict__ x, float2* __restrict__ X,
         }
     spec_compute<1, -1>(v, t, tws);
     spec_stages<2, -1>(v, buf, tws, t, [&](float2 (&w)[kSpecP]) {
-        stage_store<kQuarter, kSpecT, sR(SC::NST), sNS(SC::NST)>(w, buf, t);
+        stage_store<kQuarter, kSpecT, sR(SC::NST), sNS(SC::NST), kSH>(w, buf, t);
     });
     __syncthreads();
 
@@ -157,8 +158,8 @@ spectrum_fwd_kernel(const float* __restrict__ x, float2* __restrict__ X,
     const int npairs = h == 0 ? kQuarter / 2 + 1 : kQuarter / 2;
     for (int kp = t; kp < npairs; kp += kSpecT) {
         const int kq = h == 0 ? ((kQuarter - kp) & (kQuarter - 1)) : (kQuarter - 1 - kp);
-        const float2 zq = buf[PADI(kp)];
-        const float2 zb = buf[PADI(kq)];
+        const float2 zq = buf[PADI<kSH>(kp)];
+        const float2 zb = buf[PADI<kSH>(kq)];
         const int q = 2 * kp + h;
         const float2 w = tw(q);
         const float2 sq = cadd(zq, cconj(zb));
@@ -231,17 +232,17 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
         }
         const float2 z0 = retangle(fA, fB, tw(n));
         const float2 z1 = retangle(fC, fD, tw(kQuarter + n));
-        buf[PADI(n)] = h == 0 ? cadd(z0, z1) : cmulc(csub(z0, z1), tw(2 * n));
+        buf[PADI<kSH>(n)] = h == 0 ? cadd(z0, z1) : cmulc(csub(z0, z1), tw(2 * n));
         if (m != n) {
             const float2 z2 = retangle(fD, fC, tw(m));
             const float2 z3 = retangle(fB, fA, tw(kQuarter + m));
-            buf[PADI(m)] = h == 0 ? cadd(z2, z3) : cmulc(csub(z2, z3), tw(2 * m));
+            buf[PADI<kSH>(m)] = h == 0 ? cadd(z2, z3) : cmulc(csub(z2, z3), tw(2 * m));
         }
     }
     __syncthreads();
 
     float2 v[kSpecP];
-    stage_load<kQuarter, kSpecT, SC::R1>(v, buf, t);
+    stage_load<kQuarter, kSpecT, SC::R1, kSH>(v, buf, t);
     __syncthreads();
     spec_compute<1, +1>(v, t, tws);
     float2* ys = reinterpret_cast<float2*>(y + slice * kSlice);
