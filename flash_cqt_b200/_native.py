@@ -78,6 +78,8 @@ def lib():
                 fn.restype = ci
             L.cqt_launch_stage.argtypes = [vp, ci, vp, vp, vp, vp, ci, ci, vp, sz, vp]
             L.cqt_launch_stage.restype = ci
+            L.cqt_analysis_noalloc.argtypes = [vp, vp, vp, vp, ci, ci, vp]
+            L.cqt_analysis_noalloc.restype = ci
             _lib = L
     return _lib
 
@@ -87,7 +89,7 @@ def exported_symbols():
     return ["cqt_tables_upload", "cqt_tables_free", "cqt_ncoef",
             "cqt_workspace_bytes", "cqt_analysis", "cqt_synthesis",
             "cqt_adj_analysis", "cqt_adj_synthesis", "cqt_launch_stage",
-            "cqt_last_error", "cqt_version"]
+            "cqt_analysis_noalloc", "cqt_last_error", "cqt_version"]
 
 
 def _check(rc, what):

@@ -4,6 +4,7 @@
 // or synchronises.
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -421,3 +422,66 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------
+// Allocation-free analysis.
+//
+// Some callers cannot allocate device memory at all: a real-time audio
+// callback (a plugin's process() on the host's audio thread) must not call
+// cudaMalloc, which can block and synchronise the device and so cause audio
+// dropouts, and a host with a fixed, pre-planned memory budget may forbid
+// allocations after start-up.  cqt_analysis_noalloc serves them: it is
+// cqt_analysis with its scratch (the half-spectrum rows of the slices) taken
+// from the file-scope array below instead of a caller-allocated workspace.
+//
+// * The array holds at most kNoAllocMaxBatch = 8 slices (2,097,664 bytes);
+//   every GPU that loads this library keeps it until the process exits.
+// * The first call on a device, with that device current, looks up the
+//   array's device address with cudaGetSymbolAddress and caches it; make that
+//   first call before any stream capture.
+// * All calls on a device share the array and it keeps the last call's
+//   contents.  Nothing in it needs clearing (the spectrum kernel writes every
+//   bin the band kernel later reads), but calls that overlap on the GPU --
+//   e.g. on two streams without ordering between them -- race on it.
+namespace {
+
+constexpr int kNoAllocMaxBatch = 8;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float2 g_noalloc_scratch[kNoAllocMaxBatch * kPlaneStride];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices];
+
+}  // namespace
+
+extern "C" int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* c_re,
+                                    float* c_im, int layout, int batch, void* stream) {
+    if (!t) return fail(CQT_ERR_ARG, "null tables");
+    if (batch < 0) return fail(CQT_ERR_ARG, "negative batch");
+    if (batch > kNoAllocMaxBatch)
+        return fail(CQT_ERR_ARG,
+                    "cqt_analysis_noalloc takes at most 8 slices per call (its static "
+                    "scratch holds 8); split the batch or use cqt_analysis");
+    if (layout != CQT_LAYOUT_PLANAR && layout != CQT_LAYOUT_COMPLEX)
+        return fail(CQT_ERR_ARG, "unknown coefficient layout");
+    int rc = check_device(t);
+    if (rc) return rc;
+    if (t->device < 0 || t->device >= kNoAllocMaxDevices)
+        return fail(CQT_ERR_DEVICE, "device index beyond the no-allocation address cache");
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        scratch = g_noalloc_ptr[t->device];
+        if (!scratch) {
+            cudaError_t e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+            g_noalloc_ptr[t->device] = scratch;
+        }
+    }
+    if (batch == 0) return CQT_OK;
+    if (!x) return fail(CQT_ERR_ARG, "null input");
+    CoefPtr out;
+    if ((rc = coef_ptr(c_re, c_im, layout, &out))) return rc;
+    return run_fwd_engine(t, 0, x, out, batch, scratch, static_cast<cudaStream_t>(stream));
+}

@@ -137,6 +137,18 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in,
                      int batch, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* cqt_analysis without a workspace argument, for callers that cannot
+ * allocate device memory (e.g. a real-time audio callback, where cudaMalloc
+ * may block and synchronise the device).  No counterpart in the reference.
+ * Scratch comes from a static device array inside this library sized for at
+ * most 8 slices (batch > 8 returns CQT_ERR_ARG); every GPU that loads the
+ * library holds those 2 MiB until exit.  The first call on a device (that
+ * device current) looks the array up with cudaGetSymbolAddress: make it
+ * before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU race.  Allocates nothing, never synchronises. */
+int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* c_re,
+                         float* c_im, int layout, int batch, void* stream);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* cqt_last_error(void);
 
