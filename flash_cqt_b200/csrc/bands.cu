@@ -222,7 +222,11 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
         for (int i = t; i < n; i += T) cp_async8(buf + PADI<kSH>(i), Xs + lo + i);
     }
     fill_twiddles<M>(tws, bp.tw2048);
-    // stage 1 taps: element r of butterfly b is tap t + T b + r M / R1
+    // stage 1 taps: element r of butterfly b is tap t + T b + r M / R1.
+    // Octave bands read segment entry (m + l) mod M inside the window
+    // support; side bands go through the per-tap gather table (conjugated
+    // mirror taps).  The barrier below is outside both branches: one CTA may
+    // hold instances of both kinds.
     float gain[kP];
     int src[kP];
     const int l = d_l(in.d);
@@ -233,26 +237,34 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
             const int m = t + T * b + r * (M / R1);
             gain[b * R1 + r] = in.valid ? __ldg(tab.gain + off + m) : 0.f;
             if (side) {
-                const int s = in.valid ? __ldg(tab.src + off + m) : -1;
-                src[b * R1 + r] = s < 0 ? -1 : (((s & 0xFFFF) - lo) | (s & 0x10000));
-            } else {
-                const int i = (m + l) & (M - 1);
-                src[b * R1 + r] = i < n ? i : -1;
+                const int sv = in.valid ? __ldg(tab.src + off + m) : -1;
+                src[b * R1 + r] = sv < 0 ? -1 : (((sv & 0xFFFF) - lo) | (sv & 0x10000));
             }
         }
     cp_async_wait_all();
     __syncthreads();
     float2 v[kP];
+    if (!side) {
 #pragma unroll
-    for (int i = 0; i < kP; ++i) {
-        const int s = src[i];
-        float2 val = make_float2(0.f, 0.f);
-        if (s >= 0) {
-            float2 xv = buf[PADI<kSH>(s & 0xFFFF)];
-            if (s & 0x10000) xv.y = -xv.y;
-            val = cscale(xv, gain[i]);
+        for (int b = 0; b < kP / R1; ++b)
+#pragma unroll
+            for (int r = 0; r < R1; ++r) {
+                const int i = (t + T * b + r * (M / R1) + l) & (M - 1);
+                v[b * R1 + r] = i < n ? cscale(buf[PADI<kSH>(i)], gain[b * R1 + r])
+                                      : make_float2(0.f, 0.f);
+            }
+    } else {
+#pragma unroll
+        for (int i = 0; i < kP; ++i) {
+            const int sv = src[i];
+            float2 val = make_float2(0.f, 0.f);
+            if (sv >= 0) {
+                float2 xv = buf[PADI<kSH>(sv & 0xFFFF)];
+                if (sv & 0x10000) xv.y = -xv.y;
+                val = cscale(xv, gain[i]);
+            }
+            v[i] = val;
         }
-        v[i] = val;
     }
     static_for<0, kP / R1>([&](auto Bb) {
         dft<R1, +1, decltype(Bb)::value * R1, 1>(v);

@@ -8,8 +8,9 @@
 //   CTA 0 transforms u0[n] = z[n] + z[n + 16384]               -> Z[2k]
 //   CTA 1 transforms u1[n] = (z[n] - z[n + 16384]) W_32768^n   -> Z[2k + 1]
 // so each CTA holds a 16384-point problem (132 KB with padding) entirely in
-// shared memory and runs it as Stockham stages (16 x 16 x 16 x 4 with 1024
-// threads of 16 points, or 32 x 32 x 16 with 512 threads of 32 points),
+// shared memory and runs it as Stockham stages (32 x 32 x 16 with 512
+// threads of 32 points for the forward, 16 x 16 x 16 x 4 with 1024 threads of
+// 16 points for the inverse -- the faster schedule of each on B200),
 // then untangles the (q, L - q) bin pairs of its parity -- which are all
 // local -- into the real spectrum X[q] (spectral recovery of fused.py:311-328,
 // done once per bin instead of once per router tap).
@@ -30,8 +31,13 @@
 
 namespace fcqt {
 
-#ifndef FCQT_SPEC_P
-#define FCQT_SPEC_P 16
+// points per thread of the forward and inverse kernels (16 -> 1024 threads,
+// stages 16 x 16 x 16 x 4; 32 -> 512 threads, stages 32 x 32 x 16)
+#ifndef FCQT_SPEC_P_FWD
+#define FCQT_SPEC_P_FWD 32
+#endif
+#ifndef FCQT_SPEC_P_INV
+#define FCQT_SPEC_P_INV 16
 #endif
 
 namespace {
@@ -43,25 +49,39 @@ template <> struct SpecCfg<32> {
 template <> struct SpecCfg<16> {
     static constexpr int T = 1024, NST = 4, R1 = 16, R2 = 16, R3 = 16, R4 = 4;
 };
-constexpr int kSpecP = FCQT_SPEC_P;
-using SC = SpecCfg<kSpecP>;
-constexpr int kSpecT = SC::T;
 
-constexpr int sR(int s) { return s == 1 ? SC::R1 : s == 2 ? SC::R2 : s == 3 ? SC::R3 : SC::R4; }
-constexpr int sNS(int s) { return s <= 1 ? 1 : sNS(s - 1) * sR(s - 1); }
-constexpr bool sSplit(int s) { return sNS(s) > 32; }
-constexpr int sSize(int s) {
-    return (s < 2 || s > SC::NST) ? 0
-           : sSplit(s) ? sR(s) * 32 + sR(s) * (sNS(s) / 32)
-                       : (sR(s) - 1) * sNS(s);
+template <int P>
+constexpr int sR(int s) {
+    using C = SpecCfg<P>;
+    return s == 1 ? C::R1 : s == 2 ? C::R2 : s == 3 ? C::R3 : C::R4;
 }
-constexpr int sOff(int s) { return s <= 2 ? 0 : sOff(s - 1) + sSize(s - 1); }
-constexpr int kSpecTwTotal = sOff(SC::NST + 1);
-static_assert(sNS(SC::NST) * sR(SC::NST) == kQuarter, "stage radices must multiply to 16384");
+template <int P>
+constexpr int sNS(int s) { return s <= 1 ? 1 : sNS<P>(s - 1) * sR<P>(s - 1); }
+template <int P>
+constexpr bool sSplit(int s) { return sNS<P>(s) > 32; }
+template <int P>
+constexpr int sSize(int s) {
+    return (s < 2 || s > SpecCfg<P>::NST) ? 0
+           : sSplit<P>(s) ? sR<P>(s) * 32 + sR<P>(s) * (sNS<P>(s) / 32)
+                          : (sR<P>(s) - 1) * sNS<P>(s);
+}
+template <int P>
+constexpr int sOff(int s) { return s <= 2 ? 0 : sOff<P>(s - 1) + sSize<P>(s - 1); }
+template <int P>
+constexpr int twTotal() { return sOff<P>(SpecCfg<P>::NST + 1); }
+template <int P>
+constexpr int shiftOf() { return P == 32 ? 5 : 4; }   // shared padding shift
+template <int P>
+constexpr int smemOf() { return (padded<shiftOf<P>()>(kQuarter) + 512 + twTotal<P>()) * 8; }
 
-constexpr int kSH = kSpecP == 32 ? 5 : 4;    // shared padding shift
-constexpr int kSpecData = padded<kSH>(kQuarter);
-constexpr int kSpecSmem = (kSpecData + 512 + kSpecTwTotal) * 8;
+static_assert(sNS<16>(4) * sR<16>(4) == kQuarter && sNS<32>(3) * sR<32>(3) == kQuarter,
+              "stage radices must multiply to 16384");
+
+constexpr int kPF = FCQT_SPEC_P_FWD;
+constexpr int kPI = FCQT_SPEC_P_INV;
+// the twiddle-row blob holds the P = 32 rows, then the P = 16 rows
+constexpr int rowsOff(int P) { return P == 32 ? 0 : twTotal<32>(); }
+constexpr int kSpecRowsTotal = twTotal<32>() + twTotal<16>();
 
 struct Tw64k {
     const float2* hi;
@@ -69,9 +89,11 @@ struct Tw64k {
     __device__ __forceinline__ float2 operator()(int e) const { return tw64k(hi, lo, e); }
 };
 
+template <int P>
 __device__ __forceinline__ void load_tables(float2* sm_hilo, float2* sm_tw, const float2* ghi,
                                             const float2* glo, const float2* gtw) {
-    for (int i = threadIdx.x; i < 512 + kSpecTwTotal; i += kSpecT) {
+    gtw += rowsOff(P);
+    for (int i = threadIdx.x; i < 512 + twTotal<P>(); i += SpecCfg<P>::T) {
         if (i < 256) sm_hilo[i] = __ldg(ghi + i);
         else if (i < 512) sm_hilo[i] = __ldg(glo + i - 256);
         else sm_tw[i - 512] = __ldg(gtw + i - 512);
@@ -79,17 +101,18 @@ __device__ __forceinline__ void load_tables(float2* sm_hilo, float2* sm_tw, cons
 }
 
 // twiddle and DFT of stage s (all butterflies of the thread)
-template <int s, int S>
-__device__ __forceinline__ void spec_compute(float2 (&v)[kSpecP], int t, const float2* tws) {
-    constexpr int R = sR(s), NS = sNS(s), off = sOff(s);
-    static_for<0, kSpecP / R>([&](auto Bb) {
+template <int P, int s, int S>
+__device__ __forceinline__ void spec_compute(float2 (&v)[P], int t, const float2* tws) {
+    constexpr int R = sR<P>(s), NS = sNS<P>(s), off = sOff<P>(s);
+    constexpr int T = SpecCfg<P>::T;
+    static_for<0, P / R>([&](auto Bb) {
         constexpr int b = decltype(Bb)::value;
         if constexpr (s > 1) {
-            const int k = (t + kSpecT * b) % NS;
+            const int k = (t + T * b) % NS;
 #pragma unroll
             for (int r = 1; r < R; ++r) {
                 float2 w;
-                if constexpr (sSplit(s)) {
+                if constexpr (sSplit<P>(s)) {
                     w = cmul(tws[off + r * 32 + (k & 31)],
                              tws[off + R * 32 + r * (NS / 32) + (k >> 5)]);
                 } else {
@@ -105,61 +128,64 @@ __device__ __forceinline__ void spec_compute(float2 (&v)[kSpecP], int t, const f
 
 // stages s..NST (stage s - 1 is computed and held in v); `fin` receives the
 // last stage's outputs, index n = j + r NS_last for j = t + T b
-template <int s, int S, class Fin>
-__device__ __forceinline__ void spec_stages(float2 (&v)[kSpecP], float2* buf, const float2* tws,
+template <int P, int s, int S, class Fin>
+__device__ __forceinline__ void spec_stages(float2 (&v)[P], float2* buf, const float2* tws,
                                             int t, Fin fin) {
-    if constexpr (s > SC::NST) {
+    constexpr int T = SpecCfg<P>::T, SH = shiftOf<P>();
+    if constexpr (s > SpecCfg<P>::NST) {
         fin(v);
     } else {
-        stage_store<kQuarter, kSpecT, sR(s - 1), sNS(s - 1), kSH>(v, buf, t);
+        stage_store<kQuarter, T, sR<P>(s - 1), sNS<P>(s - 1), SH>(v, buf, t);
         __syncthreads();
-        stage_load<kQuarter, kSpecT, sR(s), kSH>(v, buf, t);
+        stage_load<kQuarter, T, sR<P>(s), SH>(v, buf, t);
         __syncthreads();
-        spec_compute<s, S>(v, t, tws);
-        spec_stages<s + 1, S>(v, buf, tws, t, fin);
+        spec_compute<P, s, S>(v, t, tws);
+        spec_stages<P, s + 1, S>(v, buf, tws, t, fin);
     }
 }
 
-__global__ void __launch_bounds__(kSpecT, 1)
+__global__ void __launch_bounds__(SpecCfg<kPF>::T, 1)
 spectrum_fwd_kernel(const float* __restrict__ x, float2* __restrict__ X,
                     const float2* __restrict__ ghi, const float2* __restrict__ glo,
                     const float2* __restrict__ gtw) {
+    constexpr int P = kPF, T = SpecCfg<P>::T, SH = shiftOf<P>();
+    using C = SpecCfg<P>;
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
-    float2* hl = buf + kSpecData;
+    float2* hl = buf + padded<SH>(kQuarter);
     float2* tws = hl + 512;
     const int h = blockIdx.x & 1;
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
-    load_tables(hl, tws, ghi, glo, gtw);
+    load_tables<P>(hl, tws, ghi, glo, gtw);
     __syncthreads();
     const Tw64k tw{hl, hl + 256};
 
     // stage 1 inputs straight from global: the radix-2 DIF split of z
     const float2* z = reinterpret_cast<const float2*>(x + slice * kSlice);
-    float2 v[kSpecP];
+    float2 v[P];
 #pragma unroll
-    for (int b = 0; b < kSpecP / SC::R1; ++b)
+    for (int b = 0; b < P / C::R1; ++b)
 #pragma unroll
-        for (int r = 0; r < SC::R1; ++r) {
-            const int n = t + kSpecT * b + r * (kQuarter / SC::R1);
+        for (int r = 0; r < C::R1; ++r) {
+            const int n = t + T * b + r * (kQuarter / C::R1);
             const float2 a = __ldg(z + n);
             const float2 c = __ldg(z + n + kQuarter);
-            v[b * SC::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
+            v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
         }
-    spec_compute<1, -1>(v, t, tws);
-    spec_stages<2, -1>(v, buf, tws, t, [&](float2 (&w)[kSpecP]) {
-        stage_store<kQuarter, kSpecT, sR(SC::NST), sNS(SC::NST), kSH>(w, buf, t);
+    spec_compute<P, 1, -1>(v, t, tws);
+    spec_stages<P, 2, -1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+        stage_store<kQuarter, T, sR<P>(C::NST), sNS<P>(C::NST), SH>(w, buf, t);
     });
     __syncthreads();
 
     // untangle the (q, L - q) pairs of this parity: X[q] = E + W_N^q O
     float2* Xs = X + slice * kPlaneStride;
     const int npairs = h == 0 ? kQuarter / 2 + 1 : kQuarter / 2;
-    for (int kp = t; kp < npairs; kp += kSpecT) {
+    for (int kp = t; kp < npairs; kp += T) {
         const int kq = h == 0 ? ((kQuarter - kp) & (kQuarter - 1)) : (kQuarter - 1 - kp);
-        const float2 zq = buf[PADI<kSH>(kp)];
-        const float2 zb = buf[PADI<kSH>(kq)];
+        const float2 zq = buf[PADI<SH>(kp)];
+        const float2 zb = buf[PADI<SH>(kq)];
         const int q = 2 * kp + h;
         const float2 w = tw(q);
         const float2 sq = cadd(zq, cconj(zb));
@@ -202,25 +228,27 @@ __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
     return make_float2(e.x - o.y, e.y + o.x);
 }
 
-__global__ void __launch_bounds__(kSpecT, 1)
+__global__ void __launch_bounds__(SpecCfg<kPI>::T, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restrict__ mask,
                     float* __restrict__ y, const float2* __restrict__ ghi,
                     const float2* __restrict__ glo, const float2* __restrict__ gtw,
                     int nplanes) {
+    constexpr int P = kPI, T = SpecCfg<P>::T, SH = shiftOf<P>();
+    using C = SpecCfg<P>;
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
-    float2* hl = buf + kSpecData;
+    float2* hl = buf + padded<SH>(kQuarter);
     float2* tws = hl + 512;
     const int h = blockIdx.x & 1;
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
-    load_tables(hl, tws, ghi, glo, gtw);
+    load_tables<P>(hl, tws, ghi, glo, gtw);
     __syncthreads();
     const Tw64k tw{hl, hl + 256};
     const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
 
     // quads {n, L - n, Q + n, Q - n}: four bins in, u_h[n] and u_h[Q - n] out
-    for (int n = t; n <= kQuarter / 2; n += kSpecT) {
+    for (int n = t; n <= kQuarter / 2; n += T) {
         const int m = (kQuarter - n) & (kQuarter - 1);
         float2 fA = plane_sum(Es, mask, n, nplanes);
         float2 fB = plane_sum(Es, mask, kHalf - n, nplanes);
@@ -230,30 +258,36 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
             fA.y = 0.f;
             fB.y = 0.f;
         }
-        const float2 z0 = retangle(fA, fB, tw(n));
-        const float2 z1 = retangle(fC, fD, tw(kQuarter + n));
-        buf[PADI<kSH>(n)] = h == 0 ? cadd(z0, z1) : cmulc(csub(z0, z1), tw(2 * n));
+        // every twiddle of the quad follows from W^n and W^2n exactly
+        // (W = W_65536, W^Q = -i): W^{Q+n} = -i W^n, W^{Q-n} = -i conj(W^n),
+        // W^{2Q-n} = -conj(W^n), W^{2Q-2n} = -conj(W^2n)
+        const float2 wn = tw(n);
+        const float2 w2n = h == 0 ? make_float2(1.f, 0.f) : tw(2 * n);
+        const float2 z0 = retangle(fA, fB, wn);
+        const float2 z1 = retangle(fC, fD, make_float2(wn.y, -wn.x));
+        buf[PADI<SH>(n)] = h == 0 ? cadd(z0, z1) : cmulc(csub(z0, z1), w2n);
         if (m != n) {
-            const float2 z2 = retangle(fD, fC, tw(m));
-            const float2 z3 = retangle(fB, fA, tw(kQuarter + m));
-            buf[PADI<kSH>(m)] = h == 0 ? cadd(z2, z3) : cmulc(csub(z2, z3), tw(2 * m));
+            const float2 z2 = retangle(fD, fC, make_float2(-wn.y, -wn.x));
+            const float2 z3 = retangle(fB, fA, make_float2(-wn.x, wn.y));
+            buf[PADI<SH>(m)] =
+                h == 0 ? cadd(z2, z3) : cmulc(csub(z2, z3), make_float2(-w2n.x, w2n.y));
         }
     }
     __syncthreads();
 
-    float2 v[kSpecP];
-    stage_load<kQuarter, kSpecT, SC::R1, kSH>(v, buf, t);
+    float2 v[P];
+    stage_load<kQuarter, T, C::R1, SH>(v, buf, t);
     __syncthreads();
-    spec_compute<1, +1>(v, t, tws);
+    spec_compute<P, 1, +1>(v, t, tws);
     float2* ys = reinterpret_cast<float2*>(y + slice * kSlice);
     const float inv = 1.0f / (float)kHalf;
-    spec_stages<2, +1>(v, buf, tws, t, [&](float2 (&w)[kSpecP]) {
-        constexpr int R = sR(SC::NST), NS = sNS(SC::NST);
+    spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+        constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
 #pragma unroll
-        for (int b = 0; b < kSpecP / R; ++b)
+        for (int b = 0; b < P / R; ++b)
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                const int nn = t + kSpecT * b + NS * r;
+                const int nn = t + T * b + NS * r;
                 ys[2 * nn + h] = cscale(w[b * R + r], inv);
             }
     });
@@ -261,19 +295,20 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
 
 }  // namespace
 
-int spectrum_twiddle_count() { return kSpecTwTotal; }
+int spectrum_twiddle_count() { return kSpecRowsTotal; }
 
-// stage twiddle rows, forward sign, double precision rounded once
-void spectrum_twiddle_rows(float2* out) {
+namespace {
+template <int P>
+void rows_for(float2* out) {
     const double two_pi = 6.283185307179586476925286766559;
     auto w = [&](long e, long base) {
         const double a = -two_pi * (double)(e % base) / (double)base;
         return make_float2((float)std::cos(a), (float)std::sin(a));
     };
-    for (int s = 2; s <= SC::NST; ++s) {
-        const int R = sR(s), NS = sNS(s), off = sOff(s);
+    for (int s = 2; s <= SpecCfg<P>::NST; ++s) {
+        const int R = sR<P>(s), NS = sNS<P>(s), off = sOff<P>(s);
         const long base = (long)NS * R;
-        if (sSplit(s)) {
+        if (sSplit<P>(s)) {
             for (int r = 0; r < R; ++r)
                 for (int k = 0; k < 32; ++k) out[off + r * 32 + k] = w((long)r * k, base);
             for (int r = 0; r < R; ++r)
@@ -285,28 +320,38 @@ void spectrum_twiddle_rows(float2* out) {
         }
     }
 }
+}  // namespace
+
+// stage twiddle rows of both schedules, forward sign, double precision
+// rounded once
+void spectrum_twiddle_rows(float2* out) {
+    rows_for<32>(out + rowsOff(32));
+    rows_for<16>(out + rowsOff(16));
+}
 
 cudaError_t launch_spectrum_fwd(const float* x, float2* X, const SpecTables& st, int batch,
                                 cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    spectrum_fwd_kernel<<<2 * batch, kSpecT, kSpecSmem, s>>>(x, X, st.hi, st.lo, st.rows);
+    spectrum_fwd_kernel<<<2 * batch, SpecCfg<kPF>::T, smemOf<kPF>(), s>>>(x, X, st.hi, st.lo,
+                                                                       st.rows);
     return cudaGetLastError();
 }
 
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, float* y,
                                 const SpecTables& st, int batch, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    spectrum_inv_kernel<<<2 * batch, kSpecT, kSpecSmem, s>>>(E, tab.mask, y, st.hi, st.lo,
-                                                             st.rows, tab.nplanes);
+    spectrum_inv_kernel<<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
+        E, tab.mask, y, st.hi, st.lo, st.rows, tab.nplanes);
     return cudaGetLastError();
 }
 
 cudaError_t init_spectrum_attributes() {
     cudaError_t e = cudaFuncSetAttribute(spectrum_fwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSpecSmem);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         smemOf<kPF>());
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(spectrum_inv_kernel,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSpecSmem);
+    return cudaFuncSetAttribute(spectrum_inv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smemOf<kPI>());
 }
 
 }  // namespace fcqt
