@@ -33,6 +33,10 @@ namespace fcqt {
 
 namespace {
 
+#ifndef FCQT_PREFETCH_GAINS
+#define FCQT_PREFETCH_GAINS 1
+#endif
+
 constexpr int kP = kBandP;
 constexpr int kSH = kP == 32 ? 5 : 4;                    // shared padding shift
 constexpr int kBandData = padded<kSH>(kBandCap);         // float2 per CTA
@@ -333,6 +337,19 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     const bool side = d_side(in.d);
     const int lo = in.d.y, l = d_l(in.d), lg = d_lg(in.d);
     const int pbase = d_plane(in.d, which) * kPlaneStride + lo;
+#if FCQT_PREFETCH_GAINS
+    // the gains of this thread's final-stage outputs, loaded before the
+    // stages so the scatter does not wait on them
+    constexpr int RL = TwLayout<M>::R3 > 1 ? TwLayout<M>::R3
+                       : TwLayout<M>::R2 > 1 ? TwLayout<M>::R2 : TwLayout<M>::R1;
+    constexpr int NSL = M / RL;
+    float gpre[kP];
+#pragma unroll
+    for (int b = 0; b < kP / RL; ++b)
+#pragma unroll
+        for (int r = 0; r < RL; ++r)
+            gpre[b * RL + r] = in.valid ? __ldg(tab.gre + off + t + T * b + r * NSL) : 0.f;
+#endif
     band_rest<M, -1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
@@ -349,7 +366,11 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
                                             val.y * __ldg(tab.gim + off + m));
                 } else {
                     const int i = (m + l) & (M - 1);
+#if FCQT_PREFETCH_GAINS
+                    const float g = gpre[b * R + r];
+#else
                     const float g = __ldg(tab.gre + off + m);
+#endif
                     if (i < lg && g != 0.f) Es[pbase + i] = cscale(val, g);
                 }
             }

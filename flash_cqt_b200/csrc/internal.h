@@ -56,7 +56,10 @@ struct CoefPtr {           // coefficient heap addressing
 #define FCQT_BAND_P 16
 #endif
 constexpr int kBandP = FCQT_BAND_P;
-constexpr int kBandThreads = 256;
+#ifndef FCQT_BAND_THREADS
+#define FCQT_BAND_THREADS 256
+#endif
+constexpr int kBandThreads = FCQT_BAND_THREADS;
 constexpr int kBandCap = kBandThreads * kBandP;   // points per band CTA
 
 BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, int batch);
