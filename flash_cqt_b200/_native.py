@@ -29,6 +29,7 @@ class HostTables(ctypes.Structure):
     _fields_ = [
         ("nbands", ctypes.c_int32), ("ncoef", ctypes.c_int32),
         ("band_off", _i32p), ("band_list", _i32p), ("band_geom", _i32p),
+        ("ngroups", ctypes.c_int32), ("group_count", _i32p), ("group_roll", _i32p),
         ("nclasses", ctypes.c_int32),
         ("class_len", _i32p), ("class_count", _i32p), ("class_first", _i32p),
         ("an_src", _i32p), ("an_gain", _f32p), ("an_seg", _i32p),
@@ -80,6 +81,16 @@ def lib():
             L.cqt_launch_stage.restype = ci
             L.cqt_analysis_noalloc.argtypes = [vp, vp, vp, vp, ci, ci, vp]
             L.cqt_analysis_noalloc.restype = ci
+            i64 = ctypes.c_int64
+            L.cqt_sliced_count.argtypes = [i64]
+            L.cqt_sliced_count.restype = ci
+            L.cqt_sliced_analysis.argtypes = [vp, vp, i64, ci, i64, ci, vp, vp, vp, sz, vp]
+            L.cqt_sliced_adj_synthesis.argtypes = [vp, vp, i64, ci, i64, ci, vp, vp, sz, vp]
+            L.cqt_sliced_synthesis.argtypes = [vp, vp, ci, ci, vp, i64, i64, vp, sz, vp]
+            L.cqt_sliced_adj_analysis.argtypes = [vp, vp, ci, ci, vp, vp, i64, i64, vp, sz, vp]
+            for nm in ("cqt_sliced_analysis", "cqt_sliced_adj_synthesis",
+                       "cqt_sliced_synthesis", "cqt_sliced_adj_analysis"):
+                getattr(L, nm).restype = ci
             _lib = L
     return _lib
 
@@ -89,7 +100,9 @@ def exported_symbols():
     return ["cqt_tables_upload", "cqt_tables_free", "cqt_ncoef",
             "cqt_workspace_bytes", "cqt_analysis", "cqt_synthesis",
             "cqt_adj_analysis", "cqt_adj_synthesis", "cqt_launch_stage",
-            "cqt_analysis_noalloc", "cqt_last_error", "cqt_version"]
+            "cqt_analysis_noalloc", "cqt_sliced_count", "cqt_sliced_analysis",
+            "cqt_sliced_synthesis", "cqt_sliced_adj_analysis",
+            "cqt_sliced_adj_synthesis", "cqt_last_error", "cqt_version"]
 
 
 def _check(rc, what):
@@ -121,6 +134,9 @@ class DeviceTables:
         h.band_off = arr(tabs["band_off"], np.int32, ctypes.c_int32)
         h.band_list = arr(tabs["band_list"], np.int32, ctypes.c_int32)
         h.band_geom = arr(tabs["band_geom"], np.int32, ctypes.c_int32)
+        h.ngroups = len(tabs["group_count"])
+        h.group_count = arr(tabs["group_count"], np.int32, ctypes.c_int32)
+        h.group_roll = arr(tabs["group_roll"], np.int32, ctypes.c_int32)
         h.nclasses = len(cls)
         h.class_len = arr([c[0] for c in cls], np.int32, ctypes.c_int32)
         h.class_count = arr([c[1] for c in cls], np.int32, ctypes.c_int32)
@@ -171,6 +187,9 @@ class DeviceTables:
         _check(lib().cqt_launch_stage(self.handle, int(stage), sig_in, sig_out,
                                       c_re, c_im, layout, int(batch), ws,
                                       ws_bytes, stream), "cqt_launch_stage")
+
+    def sliced(self, name, *args):
+        _check(getattr(lib(), name)(self.handle, *args), name)
 
     def __del__(self):
         h = getattr(self, "handle", None)

@@ -192,6 +192,31 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
 }
 
+// where an instance's M coefficients live: element n at
+// base + ((n + roll) mod M) -- the per-slice heap (roll 0) or the sliced
+// block layout (SliceLayout, roll +-M/4 on octave groups)
+struct CoefAddr {
+    long long base;
+    int roll;
+};
+
+template <int M, bool SLICED>
+__device__ __forceinline__ CoefAddr coef_addr(const BandParams& bp, int slice, int4 d) {
+    CoefAddr a;
+    if constexpr (!SLICED) {
+        a.base = (long long)slice * bp.ncoef + d.x;
+        a.roll = 0;
+    } else {
+        const int S = bp.sl.S;
+        const long long row = slice / S;
+        const int s = slice % S;
+        const int gi = (d.w >> 12) & 15, r = (d.w >> 16) & 255;
+        a.base = bp.sl.goff[gi] + ((row * bp.sl.grows[gi] + r) * S + s) * (long long)M;
+        a.roll = bp.sl.groll[gi] ? ((s & 1) ? -(M / 4) : M / 4) : 0;
+    }
+    return a;
+}
+
 // descriptor fields: {heap offset, lo (octave) | band id (side), l | Lg << 16,
 // flags: bit 0 side band, bits 4-7 synthesis plane, bits 8-11 adjoint plane}
 __device__ __forceinline__ bool d_side(int4 d) { return d.w & 1; }
@@ -199,7 +224,7 @@ __device__ __forceinline__ int d_l(int4 d) { return d.z & 0xFFFF; }
 __device__ __forceinline__ int d_lg(int4 d) { return d.z >> 16; }
 __device__ __forceinline__ int d_plane(int4 d, int which) { return (d.w >> (4 + 4 * which)) & 15; }
 
-template <int M>
+template <int M, bool SLICED>
 __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const BandParams& bp,
                          int c, CoefPtr out, float2* smem, float2* tws) {
     constexpr int T = M / kP;
@@ -275,7 +300,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     });
     __syncthreads();   // the staged segment is dead; stage 1 reuses the buffer
 
-    const long hb = (long)in.slice * bp.ncoef + off;
+    const CoefAddr ca = coef_addr<M, SLICED>(bp, in.slice, in.d);
     band_rest<M, +1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
@@ -285,17 +310,19 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
             for (int r = 0; r < R; ++r) {
                 const int nn = t + T * b + r * NS;
                 const float2 val = w[b * R + r];
+                const long long ix =
+                    SLICED ? ca.base + ((nn + ca.roll) & (M - 1)) : ca.base + nn;
                 if (out.interleaved) {
-                    reinterpret_cast<float2*>(out.re)[hb + nn] = val;
+                    reinterpret_cast<float2*>(out.re)[ix] = val;
                 } else {
-                    out.re[hb + nn] = val.x;
-                    out.im[hb + nn] = val.y;
+                    out.re[ix] = val.x;
+                    out.im[ix] = val.y;
                 }
             }
     });
 }
 
-template <int M>
+template <int M, bool SLICED>
 __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandParams& bp, int c,
                          float2* __restrict__ E, float2* smem, float2* tws) {
     constexpr int T = M / kP;
@@ -304,18 +331,20 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     const int t = in.t;
     float2* buf = smem + in.il * padded<kSH>(M);
     const int off = in.d.x;
-    const long hb = (long)in.slice * bp.ncoef + off;
+    const CoefAddr ca = coef_addr<M, SLICED>(bp, in.slice, in.d);
 
     // stage the instance's M coefficients into shared memory with
     // asynchronous copies (coalesced, no registers held while in flight)
     if (in.valid) {
         if (in_c.interleaved) {
-            const float2* src = reinterpret_cast<const float2*>(in_c.re) + hb;
-            for (int i = t; i < M; i += T) cp_async8(buf + PADI<kSH>(i), src + i);
+            const float2* src = reinterpret_cast<const float2*>(in_c.re) + ca.base;
+            for (int i = t; i < M; i += T)
+                cp_async8(buf + PADI<kSH>(i), src + (SLICED ? ((i + ca.roll) & (M - 1)) : i));
         } else {
             for (int i = t; i < M; i += T) {
-                cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)), in_c.re + hb + i);
-                cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)) + 1, in_c.im + hb + i);
+                const long long ix = ca.base + (SLICED ? ((i + ca.roll) & (M - 1)) : i);
+                cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)), in_c.re + ix);
+                cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)) + 1, in_c.im + ix);
             }
         }
     }
@@ -383,6 +412,7 @@ __device__ __forceinline__ int find_class(const BandSched& sc) {
     return c;
 }
 
+template <bool SLICED>
 __global__ void __launch_bounds__(kBandThreads, kBandMinBlocks)
 bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant__ BandParams bp,
                  CoefPtr out) {
@@ -391,17 +421,18 @@ bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant
     float2* tws = smem + kBandData;
     const int c = find_class(bp.sc);
     switch (bp.sc.M[c]) {
-    case 2048: band_fwd<2048>(X, tab, bp, c, out, smem, tws); break;
-    case 1024: band_fwd<1024>(X, tab, bp, c, out, smem, tws); break;
-    case 512:  band_fwd<512>(X, tab, bp, c, out, smem, tws); break;
-    case 256:  band_fwd<256>(X, tab, bp, c, out, smem, tws); break;
-    case 128:  band_fwd<128>(X, tab, bp, c, out, smem, tws); break;
-    case 64:   band_fwd<64>(X, tab, bp, c, out, smem, tws); break;
-    case 32:   band_fwd<32>(X, tab, bp, c, out, smem, tws); break;
+    case 2048: band_fwd<2048, SLICED>(X, tab, bp, c, out, smem, tws); break;
+    case 1024: band_fwd<1024, SLICED>(X, tab, bp, c, out, smem, tws); break;
+    case 512:  band_fwd<512, SLICED>(X, tab, bp, c, out, smem, tws); break;
+    case 256:  band_fwd<256, SLICED>(X, tab, bp, c, out, smem, tws); break;
+    case 128:  band_fwd<128, SLICED>(X, tab, bp, c, out, smem, tws); break;
+    case 64:   band_fwd<64, SLICED>(X, tab, bp, c, out, smem, tws); break;
+    case 32:   band_fwd<32, SLICED>(X, tab, bp, c, out, smem, tws); break;
     default: break;
     }
 }
 
+template <bool SLICED>
 __global__ void __launch_bounds__(kBandThreads, kBandMinBlocks)
 bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ BandParams bp,
                  float2* __restrict__ E) {
@@ -410,13 +441,13 @@ bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ Band
     float2* tws = smem + kBandData;
     const int c = find_class(bp.sc);
     switch (bp.sc.M[c]) {
-    case 2048: band_inv<2048>(in, tab, which, bp, c, E, smem, tws); break;
-    case 1024: band_inv<1024>(in, tab, which, bp, c, E, smem, tws); break;
-    case 512:  band_inv<512>(in, tab, which, bp, c, E, smem, tws); break;
-    case 256:  band_inv<256>(in, tab, which, bp, c, E, smem, tws); break;
-    case 128:  band_inv<128>(in, tab, which, bp, c, E, smem, tws); break;
-    case 64:   band_inv<64>(in, tab, which, bp, c, E, smem, tws); break;
-    case 32:   band_inv<32>(in, tab, which, bp, c, E, smem, tws); break;
+    case 2048: band_inv<2048, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
+    case 1024: band_inv<1024, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
+    case 512:  band_inv<512, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
+    case 256:  band_inv<256, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
+    case 128:  band_inv<128, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
+    case 64:   band_inv<64, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
+    case 32:   band_inv<32, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
     default: break;
     }
 }
@@ -445,7 +476,10 @@ cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParam
                              CoefPtr out, cudaStream_t s) {
     const int grid = bp.sc.cta0[bp.sc.ncls];
     if (grid <= 0) return cudaSuccess;
-    bands_fwd_kernel<<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bp, out);
+    if (bp.sl.S > 0)
+        bands_fwd_kernel<true><<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bp, out);
+    else
+        bands_fwd_kernel<false><<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bp, out);
     return cudaGetLastError();
 }
 
@@ -453,16 +487,22 @@ cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const Ban
                              float2* E, cudaStream_t s) {
     const int grid = bp.sc.cta0[bp.sc.ncls];
     if (grid <= 0) return cudaSuccess;
-    bands_inv_kernel<<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E);
+    if (bp.sl.S > 0)
+        bands_inv_kernel<true><<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E);
+    else
+        bands_inv_kernel<false><<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E);
     return cudaGetLastError();
 }
 
 cudaError_t init_band_attributes() {
-    cudaError_t e = cudaFuncSetAttribute(bands_fwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kBandSmem);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(bands_inv_kernel,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, kBandSmem);
+    const void* fns[] = {(const void*)bands_fwd_kernel<false>, (const void*)bands_fwd_kernel<true>,
+                         (const void*)bands_inv_kernel<false>, (const void*)bands_inv_kernel<true>};
+    for (const void* f : fns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kBandSmem);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace fcqt

@@ -29,6 +29,8 @@ struct cqt_tables {
     InvTab inv[2];   // 0 synthesis, 1 transpose of analysis
     const float2* tw2048;
     int4 desc[kMaxBands];   // class order, see BandParams
+    int ngroups;
+    int group_count[kMaxGroups], group_len[kMaxGroups], group_roll[kMaxGroups];
     SpecTables spec;
     int max_planes;
     void* blob;
@@ -97,31 +99,78 @@ BandParams band_params(const cqt_tables* t, int batch) {
     bp.tw2048 = t->tw2048;
     bp.ncoef = t->ncoef;
     std::memcpy(bp.desc, t->desc, sizeof bp.desc);
+    bp.sl = SliceLayout{};
     return bp;
 }
 
+BandParams band_params_sliced(const cqt_tables* t, int rows, int slices) {
+    BandParams bp = band_params(t, rows * slices);
+    bp.sl.S = slices;
+    long long off = 0;
+    for (int g = 0; g < t->ngroups; ++g) {
+        bp.sl.goff[g] = off;
+        bp.sl.grows[g] = t->group_count[g];
+        bp.sl.groll[g] = t->group_roll[g];
+        off += (long long)rows * slices * t->group_count[g] * t->group_len[g];
+    }
+    return bp;
+}
+
+SigMap contiguous_in(const float* x) { return SigMap{x, nullptr, 0, 0, 0, nullptr}; }
+SigMap contiguous_out(float* y) { return SigMap{nullptr, y, 0, 0, 0, nullptr}; }
+
 // one analysis-engine pass: real signal -> spectrum -> bands
-int run_fwd_engine(const cqt_tables* t, int which, const float* sig, CoefPtr out,
-                   int batch, void* ws, cudaStream_t s) {
+int run_fwd(const cqt_tables* t, int which, const SigMap& sig, CoefPtr out,
+            const BandParams& bp, int batch, void* ws, cudaStream_t s) {
     if (batch == 0) return CQT_OK;
     float2* X = static_cast<float2*>(ws);
     cudaError_t e = launch_spectrum_fwd(sig, X, t->spec, batch, s);
     if (e != cudaSuccess) return cuda_fail(e, "spectrum_fwd launch");
-    e = launch_bands_fwd(X, t->fwd[which], band_params(t, batch), out, s);
+    e = launch_bands_fwd(X, t->fwd[which], bp, out, s);
     if (e != cudaSuccess) return cuda_fail(e, "bands_fwd launch");
     return CQT_OK;
 }
 
+int run_fwd_engine(const cqt_tables* t, int which, const float* sig, CoefPtr out,
+                   int batch, void* ws, cudaStream_t s) {
+    return run_fwd(t, which, contiguous_in(sig), out, band_params(t, batch), batch, ws, s);
+}
+
 // one synthesis-engine pass: bands -> colour planes -> real signal
-int run_inv_engine(const cqt_tables* t, int which, CoefPtr in, float* sig, int batch,
-                   void* ws, cudaStream_t s) {
+int run_inv(const cqt_tables* t, int which, CoefPtr in, const SigMap& sig,
+            const BandParams& bp, int batch, void* ws, cudaStream_t s) {
     if (batch == 0) return CQT_OK;
     float2* E = static_cast<float2*>(ws);
-    cudaError_t e = launch_bands_inv(in, t->inv[which], which, band_params(t, batch), E, s);
+    cudaError_t e = launch_bands_inv(in, t->inv[which], which, bp, E, s);
     if (e != cudaSuccess) return cuda_fail(e, "bands_inv launch");
     e = launch_spectrum_inv(E, t->inv[which], sig, t->spec, batch, s);
     if (e != cudaSuccess) return cuda_fail(e, "spectrum_inv launch");
     return CQT_OK;
+}
+
+int run_inv_engine(const cqt_tables* t, int which, CoefPtr in, float* sig, int batch,
+                   void* ws, cudaStream_t s) {
+    return run_inv(t, which, in, contiguous_out(sig), band_params(t, batch), batch, ws, s);
+}
+
+int sliced_count(long long length) {
+    if (length <= 0) return 1;
+    const long long nb = (length + kQuarter - 1) / kQuarter;
+    return (int)((nb + 1) / 2 + 1);
+}
+
+int check_sliced(const cqt_tables* t, int rows, int slices, long long ld, long long length,
+                 void* ws, size_t ws_bytes) {
+    if (!t) return fail(CQT_ERR_ARG, "null tables");
+    if (rows < 0 || slices < 1 || length < 0 || ld < length)
+        return fail(CQT_ERR_ARG, "bad sliced geometry (rows, slices, ld >= length)");
+    if ((long long)rows * slices > (1LL << 30))
+        return fail(CQT_ERR_ARG, "too many slices in one call");
+    if (t->ngroups < 1) return fail(CQT_ERR_ARG, "tables carry no group layout");
+    if (rows > 0 && (!ws || ws_bytes < ws_need(t, rows * slices)))
+        return fail(CQT_ERR_ARG, "workspace missing or smaller than cqt_workspace_bytes(rows * S)");
+    if (((uintptr_t)ws & 15u) != 0) return fail(CQT_ERR_ARG, "workspace not 16-byte aligned");
+    return check_device(t);
 }
 
 }  // namespace
@@ -196,6 +245,31 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
         }
     }
     if (h->nbands > kMaxBands) return fail(CQT_ERR_ARG, "too many bands");
+    // block length of every band, and the group of every band (heap order)
+    std::vector<int> band_M(h->nbands, 0), band_group(h->nbands, -1), band_row(h->nbands, 0);
+    std::vector<int> group_first(kMaxGroups, 0);
+    for (int c = 0; c < h->nclasses; ++c)
+        for (int i = 0; i < h->class_count[c]; ++i)
+            band_M[h->band_list[h->class_first[c] + i]] = h->class_len[c];
+    if (h->ngroups < 1 || h->ngroups > kMaxGroups || !h->group_count || !h->group_roll)
+        return fail(CQT_ERR_ARG, "group table missing or too large");
+    {
+        int b = 0;
+        for (int g = 0; g < h->ngroups; ++g) {
+            const int n = h->group_count[g];
+            if (n < 1 || n > 255 || b + n > h->nbands)
+                return fail(CQT_ERR_ARG, "group counts do not partition the bands");
+            group_first[g] = b;
+            for (int i = 0; i < n; ++i, ++b) {
+                band_group[b] = g;
+                band_row[b] = i;
+                if (band_M[b] != band_M[group_first[g]] ||
+                    h->band_off[b] != h->band_off[group_first[g]] + i * band_M[b])
+                    return fail(CQT_ERR_ARG, "group bands are not consecutive equal-length rows");
+            }
+        }
+        if (b != h->nbands) return fail(CQT_ERR_ARG, "group counts do not partition the bands");
+    }
     // the closed-form octave path must compute exactly what the tables say
     for (int c = 0; c < h->nclasses; ++c) {
         const int M = h->class_len[c];
@@ -321,11 +395,18 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     t->inv[1] = InvTab{(const int*)P(i_aad), (const float*)P(i_aar), (const float*)P(i_aai),
                        (const unsigned char*)P(i_aam), h->aa_nplanes};
     t->tw2048 = (const float2*)P(i_tw);
+    t->ngroups = h->ngroups;
+    for (int g = 0; g < h->ngroups; ++g) {
+        t->group_count[g] = h->group_count[g];
+        t->group_roll[g] = h->group_roll[g] ? 1 : 0;
+        t->group_len[g] = band_M[group_first[g]];
+    }
     for (int i = 0; i < h->nbands; ++i) {
         const int b = h->band_list[i];
         const int32_t* g = h->band_geom + 4 * b;
         const bool side = g[3] & 1;
-        t->desc[i] = make_int4(h->band_off[b], side ? b : g[0], g[1] | (g[2] << 16), g[3]);
+        t->desc[i] = make_int4(h->band_off[b], side ? b : g[0], g[1] | (g[2] << 16),
+                               (g[3] & 0xFFF) | (band_group[b] << 12) | (band_row[b] << 16));
     }
     t->spec = SpecTables{(const float2*)P(i_hi), (const float2*)P(i_lo), (const float2*)P(i_rows)};
     t->max_planes = h->sy_nplanes > h->aa_nplanes ? h->sy_nplanes : h->aa_nplanes;
@@ -398,7 +479,8 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
     switch (stage) {
     case 0:
         if (!sig_in) return fail(CQT_ERR_ARG, "null input");
-        e = launch_spectrum_fwd(sig_in, static_cast<float2*>(ws), t->spec, batch, s);
+        e = launch_spectrum_fwd(contiguous_in(sig_in), static_cast<float2*>(ws), t->spec, batch,
+                                s);
         break;
     case 1:
         if ((rc = coef_ptr(c_re, c_im, layout, &cp))) return rc;
@@ -412,8 +494,8 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
         break;
     case 3:
         if (!sig_out) return fail(CQT_ERR_ARG, "null output");
-        e = launch_spectrum_inv(static_cast<const float2*>(ws), t->inv[0], sig_out, t->spec,
-                                batch, s);
+        e = launch_spectrum_inv(static_cast<const float2*>(ws), t->inv[0],
+                                contiguous_out(sig_out), t->spec, batch, s);
         break;
     default:
         return fail(CQT_ERR_ARG, "unknown stage");
@@ -485,3 +567,71 @@ extern "C" int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* 
     if ((rc = coef_ptr(c_re, c_im, layout, &out))) return rc;
     return run_fwd_engine(t, 0, x, out, batch, scratch, static_cast<cudaStream_t>(stream));
 }
+
+// ------------------------------------------------------------------------
+// Sliced streaming transform (include/flash_cqt_b200.h): the SlicedCQT
+// slicing, rolls and overlap-add folded into the same four kernels.
+extern "C" {
+
+int cqt_sliced_count(int64_t length) { return sliced_count(length); }
+
+int cqt_sliced_analysis(const cqt_tables* t, const float* x, int64_t ld, int rows,
+                        int64_t length, int slices, const float* window, float* coef,
+                        void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_sliced(t, rows, slices, ld, length, ws, ws_bytes);
+    if (rc) return rc;
+    if (rows == 0) return CQT_OK;
+    if (!x || !coef || !window) return fail(CQT_ERR_ARG, "null signal, coefficients or window");
+    if ((uintptr_t)coef & 7u) return fail(CQT_ERR_ARG, "coefficient buffer not 8-byte aligned");
+    const SigMap in{x, nullptr, ld, length, slices, window};
+    const CoefPtr out{coef, nullptr, 1};
+    return run_fwd(t, 0, in, out, band_params_sliced(t, rows, slices), rows * slices, ws,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int cqt_sliced_adj_synthesis(const cqt_tables* t, const float* gy, int64_t ld, int rows,
+                             int64_t length, int slices, float* gcoef, void* ws,
+                             size_t ws_bytes, void* stream) {
+    int rc = check_sliced(t, rows, slices, ld, length, ws, ws_bytes);
+    if (rc) return rc;
+    if (rows == 0) return CQT_OK;
+    if (!gy || !gcoef) return fail(CQT_ERR_ARG, "null gradient buffers");
+    if ((uintptr_t)gcoef & 7u) return fail(CQT_ERR_ARG, "coefficient buffer not 8-byte aligned");
+    const SigMap in{gy, nullptr, ld, length, slices, nullptr};
+    const CoefPtr out{gcoef, nullptr, 1};
+    return run_fwd(t, 1, in, out, band_params_sliced(t, rows, slices), rows * slices, ws,
+                   static_cast<cudaStream_t>(stream));
+}
+
+static int sliced_inv(const cqt_tables* t, int which, const float* coef, int rows, int slices,
+                      const float* window, float* y, int64_t ld, int64_t length, void* ws,
+                      size_t ws_bytes, void* stream) {
+    int rc = check_sliced(t, rows, slices, ld, length, ws, ws_bytes);
+    if (rc) return rc;
+    if (rows == 0) return CQT_OK;
+    if (!coef || !y) return fail(CQT_ERR_ARG, "null coefficients or output");
+    if ((uintptr_t)coef & 7u) return fail(CQT_ERR_ARG, "coefficient buffer not 8-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // overlap-add target: zero the rows first (stream-ordered, capturable)
+    cudaError_t e = cudaMemset2DAsync(y, (size_t)ld * sizeof(float), 0,
+                                      (size_t)length * sizeof(float), rows, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync(overlap-add target)");
+    const SigMap out{nullptr, y, ld, length, slices, window};
+    const CoefPtr in{const_cast<float*>(coef), nullptr, 1};
+    return run_inv(t, which, in, out, band_params_sliced(t, rows, slices), rows * slices, ws, s);
+}
+
+int cqt_sliced_synthesis(const cqt_tables* t, const float* coef, int rows, int slices,
+                         float* y, int64_t ld, int64_t length, void* ws, size_t ws_bytes,
+                         void* stream) {
+    return sliced_inv(t, 0, coef, rows, slices, nullptr, y, ld, length, ws, ws_bytes, stream);
+}
+
+int cqt_sliced_adj_analysis(const cqt_tables* t, const float* gcoef, int rows, int slices,
+                            const float* window, float* gx, int64_t ld, int64_t length,
+                            void* ws, size_t ws_bytes, void* stream) {
+    if (!window) return fail(CQT_ERR_ARG, "the transpose of the sliced analysis needs the window");
+    return sliced_inv(t, 1, gcoef, rows, slices, window, gx, ld, length, ws, ws_bytes, stream);
+}
+
+}  // extern "C"

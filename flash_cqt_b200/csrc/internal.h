@@ -31,7 +31,36 @@ struct BandSched {         // CTA ranges of the block-length classes for one lau
 };
 
 constexpr int kMaxBands = 160;
+constexpr int kMaxGroups = 16;
 
+// Coefficient layout of the sliced transform: one interleaved complex buffer
+// holding, group after group, blocks [rows][b][S * M] (octave groups: slice
+// coefficients in time order, each slice's block rolled by +M/4 (even slice)
+// or -M/4 (odd slice), sliced.py:119-146) and [rows][S][M] (DC and Nyquist
+// side groups, not rolled).  S == 0 selects the per-slice heap layout.
+struct SliceLayout {
+    int S;                          // slices per signal row
+    long long goff[kMaxGroups];     // complex offset of each group block
+    int grows[kMaxGroups];          // bands in the group
+    int groll[kMaxGroups];          // 1: coefficients rolled by +-M/4
+};
+
+// where a slice's samples come from (analysis front end) or go to
+// (synthesis back end).  S == 0: contiguous [B][65536] slices.  S > 0:
+// slice s of row r covers samples 2H (s - 1) + j, j < 4H (H = 16384) of a
+// [rows][ld] signal of `length` samples, in the quarter-rolled order of
+// sliced.py:106-117 (sample n of the slice is j = (n +- H) mod 4H, + for even
+// s); the window (if not null) multiplies sample j; outside [0, length) the
+// input reads zero and the output drops the sample.  Outputs overlap-add
+// (two slices per sample) into a zeroed signal.
+struct SigMap {
+    const float* x;        // input signal (analysis engine)
+    float* y;              // output signal (synthesis engine)
+    long long ld;          // row stride in floats
+    long long length;
+    int S;
+    const float* window;   // [65536] or null
+};
 // everything a band kernel needs besides the per-tap tables, passed by value
 // (kernel parameters live in the constant bank: no dependent global loads)
 struct BandParams {
@@ -40,8 +69,9 @@ struct BandParams {
     int ncoef;
     // per band in class order: {heap offset, lo (octave) | band id (side),
     // l | Lg << 16, flags: bit 0 side band, bits 4-7 synthesis plane,
-    // bits 8-11 adjoint plane}
+    // bits 8-11 adjoint plane, bits 12-15 group, bits 16-23 row in group}
     int4 desc[kMaxBands];
+    SliceLayout sl;
 };
 
 struct CoefPtr {           // coefficient heap addressing
@@ -74,9 +104,9 @@ struct SpecTables {        // packed-spectrum engine twiddles (device)
 int spectrum_twiddle_count();
 void spectrum_twiddle_rows(float2* out);   // host, double precision
 
-cudaError_t launch_spectrum_fwd(const float* x, float2* X, const SpecTables& st, int batch,
+cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& st, int batch,
                                 cudaStream_t s);
-cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, float* y,
+cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
                                 const SpecTables& st, int batch, cudaStream_t s);
 cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParams& bp,
                              CoefPtr out, cudaStream_t s);

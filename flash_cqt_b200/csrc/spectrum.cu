@@ -144,8 +144,52 @@ __device__ __forceinline__ void spec_stages(float2 (&v)[P], float2* buf, const f
     }
 }
 
+// one packed input pair z[n] = (sample 2n, sample 2n + 1) of slice g
+struct SliceReader {
+    const float* row;      // signal row (sliced) or slice base (contiguous)
+    long long p0;          // sample of slice position 0 (sliced)
+    long long length;
+    int shift;             // +-H
+    const float* window;
+    bool sliced;
+    __device__ __forceinline__ float2 operator()(int n) const {
+        if (!sliced) return __ldg(reinterpret_cast<const float2*>(row) + n);
+        const int j = (2 * n + shift) & (kSlice - 1);
+        const long long p = p0 + j;
+        float2 v;
+        v.x = (p >= 0 && p < length) ? __ldg(row + p) : 0.f;
+        v.y = (p + 1 >= 0 && p + 1 < length) ? __ldg(row + p + 1) : 0.f;
+        if (window) {
+            v.x *= __ldg(window + j);
+            v.y *= __ldg(window + j + 1);
+        }
+        return v;
+    }
+};
+
+template <bool SLICED>
+__device__ __forceinline__ SliceReader make_reader(const SigMap& m, long long g) {
+    SliceReader r;
+    r.sliced = SLICED;
+    r.window = m.window;
+    r.length = m.length;
+    if constexpr (!SLICED) {
+        r.row = m.x + g * kSlice;
+        r.p0 = 0;
+        r.shift = 0;
+    } else {
+        const long long row = g / m.S;
+        const int s = (int)(g % m.S);
+        r.row = m.x + row * m.ld;
+        r.p0 = 2LL * kQuarter * (s - 1);
+        r.shift = (s & 1) ? -kQuarter : kQuarter;
+    }
+    return r;
+}
+
+template <bool SLICED>
 __global__ void __launch_bounds__(SpecCfg<kPF>::T, 1)
-spectrum_fwd_kernel(const float* __restrict__ x, float2* __restrict__ X,
+spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                     const float2* __restrict__ ghi, const float2* __restrict__ glo,
                     const float2* __restrict__ gtw) {
     constexpr int P = kPF, T = SpecCfg<P>::T, SH = shiftOf<P>();
@@ -162,15 +206,15 @@ spectrum_fwd_kernel(const float* __restrict__ x, float2* __restrict__ X,
     const Tw64k tw{hl, hl + 256};
 
     // stage 1 inputs straight from global: the radix-2 DIF split of z
-    const float2* z = reinterpret_cast<const float2*>(x + slice * kSlice);
+    const SliceReader z = make_reader<SLICED>(in, slice);
     float2 v[P];
 #pragma unroll
     for (int b = 0; b < P / C::R1; ++b)
 #pragma unroll
         for (int r = 0; r < C::R1; ++r) {
             const int n = t + T * b + r * (kQuarter / C::R1);
-            const float2 a = __ldg(z + n);
-            const float2 c = __ldg(z + n + kQuarter);
+            const float2 a = z(n);
+            const float2 c = z(n + kQuarter);
             v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
         }
     spec_compute<P, 1, -1>(v, t, tws);
@@ -228,9 +272,10 @@ __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
     return make_float2(e.x - o.y, e.y + o.x);
 }
 
+template <bool SLICED>
 __global__ void __launch_bounds__(SpecCfg<kPI>::T, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restrict__ mask,
-                    float* __restrict__ y, const float2* __restrict__ ghi,
+                    const SigMap out, const float2* __restrict__ ghi,
                     const float2* __restrict__ glo, const float2* __restrict__ gtw,
                     int nplanes) {
     constexpr int P = kPI, T = SpecCfg<P>::T, SH = shiftOf<P>();
@@ -279,18 +324,49 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
     stage_load<kQuarter, T, C::R1, SH>(v, buf, t);
     __syncthreads();
     spec_compute<P, 1, +1>(v, t, tws);
-    float2* ys = reinterpret_cast<float2*>(y + slice * kSlice);
     const float inv = 1.0f / (float)kHalf;
-    spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-        constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
+    if constexpr (!SLICED) {
+        float2* ys = reinterpret_cast<float2*>(out.y + slice * kSlice);
+        spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+            constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
 #pragma unroll
-        for (int b = 0; b < P / R; ++b)
+            for (int b = 0; b < P / R; ++b)
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int nn = t + T * b + NS * r;
-                ys[2 * nn + h] = cscale(w[b * R + r], inv);
-            }
-    });
+                for (int r = 0; r < R; ++r) {
+                    const int nn = t + T * b + NS * r;
+                    ys[2 * nn + h] = cscale(w[b * R + r], inv);
+                }
+        });
+    } else {
+        // un-roll by +-H and overlap-add into the zeroed output: every output
+        // sample receives exactly two terms, and a + b == b + a, so the
+        // result does not depend on the order of the two atomic adds
+        const long long row = slice / out.S;
+        const int s = (int)(slice % out.S);
+        float* yr = out.y + row * out.ld;
+        const long long p0 = 2LL * kQuarter * (s - 1);
+        const int shift = (s & 1) ? -kQuarter : kQuarter;
+        const float* wnd = out.window;
+        const long long len = out.length;
+        spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+            constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
+#pragma unroll
+            for (int b = 0; b < P / R; ++b)
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int nn = t + T * b + NS * r;
+                    float2 val = cscale(w[b * R + r], inv);
+                    const int j = (2 * (2 * nn + h) + shift) & (kSlice - 1);
+                    if (wnd) {
+                        val.x *= __ldg(wnd + j);
+                        val.y *= __ldg(wnd + j + 1);
+                    }
+                    const long long p = p0 + j;
+                    if (p >= 0 && p < len) atomicAdd(yr + p, val.x);
+                    if (p + 1 >= 0 && p + 1 < len) atomicAdd(yr + p + 1, val.y);
+                }
+        });
+    }
 }
 
 }  // namespace
@@ -329,29 +405,46 @@ void spectrum_twiddle_rows(float2* out) {
     rows_for<16>(out + rowsOff(16));
 }
 
-cudaError_t launch_spectrum_fwd(const float* x, float2* X, const SpecTables& st, int batch,
+cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& st, int batch,
                                 cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    spectrum_fwd_kernel<<<2 * batch, SpecCfg<kPF>::T, smemOf<kPF>(), s>>>(x, X, st.hi, st.lo,
-                                                                       st.rows);
+    if (in.S > 0)
+        spectrum_fwd_kernel<true><<<2 * batch, SpecCfg<kPF>::T, smemOf<kPF>(), s>>>(
+            in, X, st.hi, st.lo, st.rows);
+    else
+        spectrum_fwd_kernel<false><<<2 * batch, SpecCfg<kPF>::T, smemOf<kPF>(), s>>>(
+            in, X, st.hi, st.lo, st.rows);
     return cudaGetLastError();
 }
 
-cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, float* y,
+cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
                                 const SpecTables& st, int batch, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    spectrum_inv_kernel<<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
-        E, tab.mask, y, st.hi, st.lo, st.rows, tab.nplanes);
+    if (out.S > 0)
+        spectrum_inv_kernel<true><<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
+            E, tab.mask, out, st.hi, st.lo, st.rows, tab.nplanes);
+    else
+        spectrum_inv_kernel<false><<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
+            E, tab.mask, out, st.hi, st.lo, st.rows, tab.nplanes);
     return cudaGetLastError();
 }
 
 cudaError_t init_spectrum_attributes() {
-    cudaError_t e = cudaFuncSetAttribute(spectrum_fwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         smemOf<kPF>());
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(spectrum_inv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                smemOf<kPI>());
+    const void* fwd[] = {(const void*)spectrum_fwd_kernel<false>,
+                         (const void*)spectrum_fwd_kernel<true>};
+    const void* inv[] = {(const void*)spectrum_inv_kernel<false>,
+                         (const void*)spectrum_inv_kernel<true>};
+    for (const void* f : fwd) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smemOf<kPF>());
+        if (e != cudaSuccess) return e;
+    }
+    for (const void* f : inv) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smemOf<kPI>());
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace fcqt

@@ -148,3 +148,92 @@ class Engine:
 
 def ctypes_stream(stream):
     return int(stream.cuda_stream)
+
+
+class SlicedEngine:
+    """The sliced streaming transform on one Engine (cqt_sliced_* entry points).
+
+    Signals are float32 [rows, length] (any row stride with unit element
+    stride); coefficients live in one complex64 buffer of rows * S * ncoef
+    values, group after group: octave groups as [rows, b, S*M], side groups as
+    [rows, S, M] (the layout of ``SlicedCQT.fwd``'s blocks)."""
+
+    def __init__(self, eng, window):
+        from . import _native
+        self.eng = eng
+        self.N = _native
+        if window.numel() != N:
+            raise ValueError("the slice window must have 65536 samples")
+        self.window = window.to(device=eng.dev, dtype=torch.float32).contiguous()
+        self.gspec = eng.heap.gspec
+
+    def count(self, length):
+        return int(self.N.lib().cqt_sliced_count(int(length)))
+
+    def coef_numel(self, rows, S):
+        return rows * S * self.eng.ncoef
+
+    def group_views(self, buf, lead, S):
+        """split the coefficient buffer into per-group views with leading dims
+        `lead` (rows = prod(lead)): octave [*lead, b, S*M], side [*lead, S, 1, M]"""
+        rows = 1
+        for d in lead:
+            rows *= d
+        out, off = [], 0
+        ngo = len(self.eng.heap.groups)
+        for gi, (b, M, _) in enumerate(self.gspec):
+            n = rows * S * b * M
+            v = buf[off:off + n]
+            out.append(v.view(*lead, b, S * M) if gi < ngo else v.view(*lead, S, 1, M))
+            off += n
+        return out[:ngo], out[ngo:]
+
+    def _sig(self, x, name):
+        if x.device != self.eng.dev or x.dtype != torch.float32 or x.dim() != 2:
+            raise ValueError(f"{name} must be float32 [rows, length] on {self.eng.dev}")
+        if x.stride(-1) != 1:
+            x = x.contiguous()
+        return x
+
+    def _call(self, name, *args):
+        with torch.cuda.device(self.eng.dev):
+            self.eng.tables.sliced(name, *args)
+
+    def analysis(self, x, S=None, out=None, adjoint_of_synthesis=False):
+        """x [rows, L] -> coefficient buffer complex64 [rows * S * ncoef]."""
+        x = self._sig(x, "signal")
+        rows, L = x.shape
+        S = self.count(L) if S is None else S
+        if out is None:
+            out = torch.empty(self.coef_numel(rows, S), dtype=torch.complex64,
+                              device=self.eng.dev)
+        ws = self.eng.workspace(rows * S)
+        stream = int(torch.cuda.current_stream(self.eng.dev).cuda_stream)
+        if adjoint_of_synthesis:
+            self._call("cqt_sliced_adj_synthesis", x.data_ptr(), x.stride(0), rows, L, S,
+                       out.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+        else:
+            self._call("cqt_sliced_analysis", x.data_ptr(), x.stride(0), rows, L, S,
+                       self.window.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                       stream)
+        return out
+
+    def synthesis(self, coef, rows, S, length, out=None, adjoint_of_analysis=False):
+        """coefficient buffer -> y [rows, length] (overlap-added)."""
+        if coef.dtype != torch.complex64 or coef.device != self.eng.dev:
+            raise ValueError("coefficients must be complex64 on the engine's device")
+        coef = coef.resolve_conj().contiguous()
+        if coef.numel() != self.coef_numel(rows, S):
+            raise ValueError("coefficient buffer does not match rows * S * ncoef")
+        if out is None:
+            out = torch.empty(rows, length, dtype=torch.float32, device=self.eng.dev)
+        ws = self.eng.workspace(rows * S)
+        stream = int(torch.cuda.current_stream(self.eng.dev).cuda_stream)
+        if adjoint_of_analysis:
+            self._call("cqt_sliced_adj_analysis", coef.data_ptr(), rows, S,
+                       self.window.data_ptr(), out.data_ptr(), out.stride(0), length,
+                       ws.data_ptr(), ws.numel(), stream)
+        else:
+            self._call("cqt_sliced_synthesis", coef.data_ptr(), rows, S, out.data_ptr(),
+                       out.stride(0), length, ws.data_ptr(), ws.numel(), stream)
+        return out

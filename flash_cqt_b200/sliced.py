@@ -11,13 +11,47 @@ the Tukey window, roll even slices by -H and odd ones by +H.  The coefficient
 arrangement (sliced.py:119-146) rolls each octave block by +-M/4 per parity
 and lays slices out along the time axis; ``bwd`` undoes both and overlap-adds
 (sliced.py:148-167).
+
+With the default engine all of that is fused into the CUDA kernels (the
+cqt_sliced_* entry points): the analysis front end reads the slices straight
+out of the signal with window and roll applied, the band kernels write the
+rolled block layout directly (blocks are zero-copy views of one buffer), and
+the synthesis back end un-rolls and overlap-adds in its store.  Gradients flow
+through the transposed kernels.  A swapped-in ``self.cqt`` takes the generic
+path (eager slicing around the engine's own fwd / bwd).
 """
 import math
 
 import torch
 
+from .engine import SlicedEngine
 from .layout import periodic_hann
 from .oct_cqt import OctCQT
+
+
+class _SlicedAnalysis(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x2, se, S):
+        ctx.se, ctx.rows, ctx.L, ctx.S = se, x2.shape[0], x2.shape[1], S
+        return se.analysis(x2, S)
+
+    @staticmethod
+    def backward(ctx, g):
+        gx = ctx.se.synthesis(g.contiguous(), ctx.rows, ctx.S, ctx.L,
+                              adjoint_of_analysis=True)
+        return gx, None, None
+
+
+class _SlicedSynthesis(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, buf, se, rows, S, length):
+        ctx.se, ctx.S = se, S
+        return se.synthesis(buf, rows, S, length)
+
+    @staticmethod
+    def backward(ctx, gy):
+        g = ctx.se.analysis(gy.contiguous(), ctx.S, adjoint_of_synthesis=True)
+        return g, None, None, None, None
 
 
 def makewnd(sl_len, tr_area, device="cpu", dtype=torch.float32):
@@ -56,6 +90,17 @@ class SlicedCQT:
         self.frqs_hz = self.cqt.frqs_hz
         self.tw = makewnd(sl_len, tr_area, device=device, dtype=dtype)
         self._roll = [m // 4 for m in self.size_per_oct]
+        self._fused_cqt = self.cqt
+        self._se = None
+
+    # the fused kernels serve the default engine on a CUDA device
+    def _fused(self, device):
+        if self.cqt is not self._fused_cqt or self.sl_len != 65536 or device.type != "cuda":
+            return None
+        if self._se is None or self._se.eng.dev != device:
+            eng = self.cqt._trainable(device).eng
+            self._se = SlicedEngine(eng, self.tw)
+        return self._se
 
     # latency helpers (sliced.py:71-98)
     def latency_ms(self, sl_len=None):
@@ -111,6 +156,11 @@ class SlicedCQT:
         [B, C, oct_bins[i], S * size_per_oct[i]] complex (slices in time
         order), side is (dc, nyq) kept per slice, [B, C, S, 1, M]"""
         B, C, L = x.shape
+        se = self._fused(x.device)
+        if se is not None:
+            S = self._num_slices(L)
+            buf = _SlicedAnalysis.apply(x.reshape(B * C, L), se, S)
+            return se.group_views(buf, (B, C), S)
         sl = self._slice(x)
         S = sl.shape[2]
         blocks, side = self.cqt.fwd(sl)
@@ -119,10 +169,36 @@ class SlicedCQT:
                   for c, b, m in zip(blocks, self.oct_bins, self.size_per_oct)]
         return blocks, side
 
+    def _fused_buffer(self, se, blocks, side, rows, S):
+        """the coefficient buffer behind (blocks, side): zero-copy when they
+        are untouched views of one buffer, else packed in group order"""
+        allb = list(blocks) + list(side if side is not None else [])
+        base = allb[0]._base
+        if side is not None and base is not None and base.dim() == 1 \
+                and base.numel() == se.coef_numel(rows, S) \
+                and all(c._base is base and c.is_contiguous() for c in allb):
+            offs, off = [], 0
+            for b, M, _ in se.gspec:
+                offs.append(off)
+                off += rows * S * b * M
+            if all(c.storage_offset() - base.storage_offset() == o
+                   for c, o in zip(allb, offs)):
+                return base
+        parts = [c.reshape(-1).to(torch.complex64) for c in allb]
+        if side is None:
+            nside = sum(rows * S * b * M for b, M, _ in se.gspec[len(blocks):])
+            parts.append(torch.zeros(nside, dtype=torch.complex64, device=parts[0].device))
+        return torch.cat(parts)
+
     def bwd(self, blocks, side=None, length=None):
         """inverse of fwd; length trims the tail padding"""
         B, C = blocks[0].shape[:2]
         S = blocks[0].shape[-1] // self.size_per_oct[0]
+        se = self._fused(blocks[0].device)
+        if se is not None:
+            L = S * 2 * self.H if length is None else int(length)
+            buf = self._fused_buffer(se, blocks, side, B * C, S)
+            return _SlicedSynthesis.apply(buf, se, B * C, S, L).view(B, C, L)
         blocks = [c.reshape(B, C, b, S, m).permute(0, 1, 3, 2, 4)
                   for c, b, m in zip(blocks, self.oct_bins, self.size_per_oct)]
         blocks = self._arrange(blocks, S, fwd=False)

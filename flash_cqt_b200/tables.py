@@ -161,6 +161,11 @@ def build_tables(heap):
             flags |= int(planes[0]) << (4 + 4 * w)
         geom[i] = (int(rg[0]), lg // 2, lg, flags)
     t["band_geom"] = geom
+    # coefficient groups in heap order (octave groups roll in the sliced
+    # layout, the DC and Nyquist side groups do not)
+    t["group_count"] = np.array([g[0] for g in heap.gspec], np.int32)
+    t["group_roll"] = np.array([1] * len(heap.groups) + [0] * len(heap.side_groups),
+                               np.int32)
 
     # band scheduling classes, largest block length first
     bands = heap.bands

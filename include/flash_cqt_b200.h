@@ -71,6 +71,12 @@ typedef struct cqt_host_tables {
      * and 8-11 hold the colour plane of the band for synthesis and for the
      * transpose of the analysis.  Upload checks it against the per-tap tables. */
     const int32_t* band_geom;
+    /* coefficient groups in heap order (octave groups, then the DC and the
+     * Nyquist side groups): bands per group and whether the sliced layout
+     * rolls the group's blocks by +-M/4 (1 for octave groups, 0 for sides) */
+    int32_t ngroups;            /* <= 16 */
+    const int32_t* group_count;
+    const int32_t* group_roll;
     int32_t nclasses;           /* <= 8 block-length classes, largest first */
     const int32_t* class_len;   /* [nclasses] block length M (32..2048) */
     const int32_t* class_count; /* [nclasses] bands in the class */
@@ -148,6 +154,37 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in,
  * on the GPU race.  Allocates nothing, never synchronises. */
 int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* c_re,
                          float* c_im, int layout, int batch, void* stream);
+
+/* ---- Sliced streaming transform (SlicedCQT, sliced.py:41-167) ----------
+ * A signal of `rows` rows (row stride `ld` floats, `length` samples) is cut
+ * into S = cqt_sliced_count(length) slices of 65536 samples at 50 % overlap:
+ * slice s covers samples 32768 (s - 1) + j, j < 65536, multiplied by the
+ * slice window, and is quarter-rolled (-16384 for even s, +16384 for odd s).
+ * Coefficients live in one interleaved complex64 buffer of
+ * rows * S * ncoef values, group after group (group g at offset
+ * rows * S * sum_{g' < g} count_g' M_g'): octave groups as [rows][count][S M]
+ * (slices in time order, each slice's block rolled by +M/4 (even s) or -M/4
+ * (odd s)), side groups as [rows][S][M] -- exactly the blocks of
+ * SlicedCQT.fwd.  Synthesis un-rolls and overlap-adds into a signal it
+ * zeroes first (two terms per sample, order-independent: deterministic).
+ * The workspace is cqt_workspace_bytes(t, rows * S).  window: device
+ * float32[65536] (the Tukey slice window), required for the analysis and
+ * its transpose. */
+int cqt_sliced_count(int64_t length);
+int cqt_sliced_analysis(const cqt_tables* t, const float* x, int64_t ld, int rows,
+                        int64_t length, int slices, const float* window, float* coef,
+                        void* workspace, size_t workspace_bytes, void* stream);
+int cqt_sliced_synthesis(const cqt_tables* t, const float* coef, int rows, int slices,
+                         float* y, int64_t ld, int64_t length, void* workspace,
+                         size_t workspace_bytes, void* stream);
+/* transposes: coefficient gradients -> dL/dx (window applied, overlap-add),
+ * dL/dy -> coefficient gradients (no window) */
+int cqt_sliced_adj_analysis(const cqt_tables* t, const float* gcoef, int rows, int slices,
+                            const float* window, float* gx, int64_t ld, int64_t length,
+                            void* workspace, size_t workspace_bytes, void* stream);
+int cqt_sliced_adj_synthesis(const cqt_tables* t, const float* gy, int64_t ld, int rows,
+                             int64_t length, int slices, float* gcoef, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* cqt_last_error(void);

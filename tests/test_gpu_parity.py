@@ -226,3 +226,99 @@ def test_sliced_matches_oracle(dev):
     assert snr_db(r["sliced_blocks_s"], bs) >= COEF_DB - 5
     y = sl.bwd(blocks, side, length=L)
     assert snr_db(x.astype(np.float64), _np(y).reshape(-1)) >= RT_DB
+
+
+class _PluginEngine:
+    """An OctCQT-shaped engine swapped into SlicedCQT.cqt (the reference's
+    plugin point, used by bench/scoreboard.py): forces the generic path."""
+
+    def __init__(self, cqt):
+        self.inner = cqt
+
+    def fwd(self, x):
+        return self.inner.fwd(x)
+
+    def bwd(self, blocks, side=None):
+        return self.inner.bwd(blocks, side)
+
+
+def _flat(blocks, side):
+    return torch.cat([c.reshape(-1) for c in list(blocks) + list(side)])
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 150000), (2, 2, 65537), (1, 3, 262144)])
+def test_sliced_fused_equals_generic_path(dev, shape):
+    from flash_cqt_b200 import SlicedCQT
+    g = torch.Generator(device="cpu").manual_seed(sum(shape))
+    x = torch.randn(*shape, generator=g).to(dev)
+    fused = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
+    gen = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
+    gen.cqt = _PluginEngine(gen.cqt)
+    fb, fs_ = fused.fwd(x)
+    gb, gs = gen.fwd(x)
+    for a, b in zip(list(fb) + list(fs_), list(gb) + list(gs)):
+        assert a.shape == b.shape
+    assert snr_db(_np(_flat(gb, gs)), _np(_flat(fb, fs_))) >= COEF_DB
+    L = shape[-1]
+    yf = fused.bwd(fb, fs_, length=L)
+    yg = gen.bwd(gb, gs, length=L)
+    assert snr_db(_np(yg).astype(np.float64), _np(yf)) >= RT_DB
+    assert snr_db(_np(x).astype(np.float64), _np(yf)) >= RT_DB
+    # blocks handed back untouched are used in place; a copy takes the packing path
+    yc = fused.bwd([c.clone() for c in fb], [c.clone() for c in fs_], length=L)
+    assert torch.equal(yc, yf)
+    yd = fused.bwd(fb, fs_)
+    assert yd.shape[-1] == fused._num_slices(L) * 2 * fused.H
+
+
+def test_sliced_gradients_match_generic_autograd(dev):
+    from flash_cqt_b200 import SlicedCQT
+    g = torch.Generator(device="cpu").manual_seed(99)
+    L = 120000
+    x0 = torch.randn(1, 2, L, generator=g).to(dev)
+    fused = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
+    gen = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
+    gen.cqt = _PluginEngine(gen.cqt)
+    # analysis gradient
+    grads = []
+    for sl in (fused, gen):
+        x = x0.clone().requires_grad_(True)
+        b, s = sl.fwd(x)
+        w = torch.randn(_flat(b, s).shape, dtype=torch.complex64,
+                        generator=torch.Generator(device="cpu").manual_seed(5)).to(dev)
+        (torch.view_as_real(_flat(b, s)) * torch.view_as_real(w)).sum().backward()
+        grads.append(_np(x.grad))
+    assert snr_db(grads[1].astype(np.float64), grads[0]) >= GRAD_DB
+    # synthesis gradient w.r.t. leaf blocks, and the chain
+    b0, s0 = fused.fwd(x0)
+    u = torch.randn(1, 2, L, generator=torch.Generator(device="cpu").manual_seed(6)).to(dev)
+    sg = []
+    for sl in (fused, gen):
+        leaves = [c.detach().clone().requires_grad_(True) for c in list(b0) + list(s0)]
+        y = sl.bwd(leaves[:9], leaves[9:], length=L)
+        (y * u).sum().backward()
+        sg.append(_np(torch.cat([lv.grad.reshape(-1) for lv in leaves])))
+    assert snr_db(sg[1], sg[0]) >= GRAD_DB
+
+
+def test_sliced_stream_matches_whole_buffer(dev):
+    """streaming with one half slice of state == whole-buffer transform
+    (the reference's own check, bench/sliced.py:112-135)"""
+    from flash_cqt_b200 import SlicedCQT
+    sl = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
+    hop = sl.hop
+    n = 4
+    x = torch.randn(1, 1, n * hop, generator=torch.Generator(device="cpu").manual_seed(8)).to(dev)
+    wb, ws = sl.fwd(x)
+    chunks = [x[..., i * hop:(i + 1) * hop] for i in range(n)]
+    out = list(sl.stream_fwd(iter(chunks)))
+    assert len(out) == sl._num_slices(n * hop)
+    for k, (bl, sd) in enumerate(out):
+        for c, blk, m in zip(bl, wb, sl.size_per_oct):
+            ref = blk[..., k * m:(k + 1) * m]
+            assert snr_db(_np(ref), _np(c)) >= COEF_DB - 5 or \
+                float(ref.abs().max()) < 1e-6
+    ys = torch.cat(list(sl.stream_bwd(iter(out))), dim=-1)
+    yw = sl.bwd(wb, ws)
+    m = min(ys.shape[-1], yw.shape[-1])
+    assert snr_db(_np(yw[..., :m]).astype(np.float64), _np(ys[..., :m])) >= RT_DB
