@@ -42,6 +42,17 @@ class HostTables(ctypes.Structure):
     ]
 
 
+class CqtSignal(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("ld", ctypes.c_int64),
+                ("sample0", ctypes.c_int64), ("count", ctypes.c_int64),
+                ("length", ctypes.c_int64)]
+
+
+class CqtSlices(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int32), ("slice0", ctypes.c_int32),
+                ("slices", ctypes.c_int32), ("window", ctypes.c_void_p)]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -84,10 +95,11 @@ def lib():
             i64 = ctypes.c_int64
             L.cqt_sliced_count.argtypes = [i64]
             L.cqt_sliced_count.restype = ci
-            L.cqt_sliced_analysis.argtypes = [vp, vp, i64, ci, i64, ci, vp, vp, vp, sz, vp]
-            L.cqt_sliced_adj_synthesis.argtypes = [vp, vp, i64, ci, i64, ci, vp, vp, sz, vp]
-            L.cqt_sliced_synthesis.argtypes = [vp, vp, ci, ci, vp, i64, i64, vp, sz, vp]
-            L.cqt_sliced_adj_analysis.argtypes = [vp, vp, ci, ci, vp, vp, i64, i64, vp, sz, vp]
+            sigp, slp = ctypes.POINTER(CqtSignal), ctypes.POINTER(CqtSlices)
+            L.cqt_sliced_analysis.argtypes = [vp, sigp, slp, vp, vp, sz, vp]
+            L.cqt_sliced_adj_synthesis.argtypes = [vp, sigp, slp, vp, vp, sz, vp]
+            L.cqt_sliced_synthesis.argtypes = [vp, vp, slp, sigp, vp, sz, vp]
+            L.cqt_sliced_adj_analysis.argtypes = [vp, vp, slp, sigp, vp, sz, vp]
             for nm in ("cqt_sliced_analysis", "cqt_sliced_adj_synthesis",
                        "cqt_sliced_synthesis", "cqt_sliced_adj_analysis"):
                 getattr(L, nm).restype = ci

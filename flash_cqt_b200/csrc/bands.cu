@@ -212,7 +212,8 @@ __device__ __forceinline__ CoefAddr coef_addr(const BandParams& bp, int slice, i
         const int s = slice % S;
         const int gi = (d.w >> 12) & 15, r = (d.w >> 16) & 255;
         a.base = bp.sl.goff[gi] + ((row * bp.sl.grows[gi] + r) * S + s) * (long long)M;
-        a.roll = bp.sl.groll[gi] ? ((s & 1) ? -(M / 4) : M / 4) : 0;
+        // roll parity follows the global slice index
+        a.roll = bp.sl.groll[gi] ? (((bp.sl.slice0 + s) & 1) ? -(M / 4) : M / 4) : 0;
     }
     return a;
 }

@@ -103,9 +103,10 @@ BandParams band_params(const cqt_tables* t, int batch) {
     return bp;
 }
 
-BandParams band_params_sliced(const cqt_tables* t, int rows, int slices) {
+BandParams band_params_sliced(const cqt_tables* t, int rows, int slice0, int slices) {
     BandParams bp = band_params(t, rows * slices);
     bp.sl.S = slices;
+    bp.sl.slice0 = slice0;
     long long off = 0;
     for (int g = 0; g < t->ngroups; ++g) {
         bp.sl.goff[g] = off;
@@ -116,8 +117,8 @@ BandParams band_params_sliced(const cqt_tables* t, int rows, int slices) {
     return bp;
 }
 
-SigMap contiguous_in(const float* x) { return SigMap{x, nullptr, 0, 0, 0, nullptr}; }
-SigMap contiguous_out(float* y) { return SigMap{nullptr, y, 0, 0, 0, nullptr}; }
+SigMap contiguous_in(const float* x) { return SigMap{x, nullptr, 0, 0, 0, 0, 0, 0, nullptr}; }
+SigMap contiguous_out(float* y) { return SigMap{nullptr, y, 0, 0, 0, 0, 0, 0, nullptr}; }
 
 // one analysis-engine pass: real signal -> spectrum -> bands
 int run_fwd(const cqt_tables* t, int which, const SigMap& sig, CoefPtr out,
@@ -159,18 +160,34 @@ int sliced_count(long long length) {
     return (int)((nb + 1) / 2 + 1);
 }
 
-int check_sliced(const cqt_tables* t, int rows, int slices, long long ld, long long length,
-                 void* ws, size_t ws_bytes) {
-    if (!t) return fail(CQT_ERR_ARG, "null tables");
-    if (rows < 0 || slices < 1 || length < 0 || ld < length)
-        return fail(CQT_ERR_ARG, "bad sliced geometry (rows, slices, ld >= length)");
-    if ((long long)rows * slices > (1LL << 30))
+int check_sliced(const cqt_tables* t, const cqt_slices* sl, const cqt_signal* sig, void* ws,
+                 size_t ws_bytes) {
+    if (!t || !sl || !sig) return fail(CQT_ERR_ARG, "null tables, slicing or signal");
+    if (sl->rows < 0 || sl->slices < 1 || sl->slice0 < 0)
+        return fail(CQT_ERR_ARG, "bad slicing (rows >= 0, slices >= 1, slice0 >= 0)");
+    if (sig->length < 0 || sig->count < 0 || sig->ld < sig->count)
+        return fail(CQT_ERR_ARG, "bad signal geometry (length, count >= 0, ld >= count)");
+    if ((long long)sl->rows * sl->slices > (1LL << 30))
         return fail(CQT_ERR_ARG, "too many slices in one call");
     if (t->ngroups < 1) return fail(CQT_ERR_ARG, "tables carry no group layout");
-    if (rows > 0 && (!ws || ws_bytes < ws_need(t, rows * slices)))
+    if (sl->rows > 0 && (!ws || ws_bytes < ws_need(t, sl->rows * sl->slices)))
         return fail(CQT_ERR_ARG, "workspace missing or smaller than cqt_workspace_bytes(rows * S)");
     if (((uintptr_t)ws & 15u) != 0) return fail(CQT_ERR_ARG, "workspace not 16-byte aligned");
     return check_device(t);
+}
+
+SigMap sig_map(const cqt_slices* sl, const cqt_signal* sig, bool input, const float* window) {
+    SigMap m{};
+    m.x = input ? sig->data : nullptr;
+    m.y = input ? nullptr : sig->data;
+    m.ld = sig->ld;
+    m.length = sig->length;
+    m.sample0 = sig->sample0;
+    m.count = sig->count;
+    m.S = sl->slices;
+    m.slice0 = sl->slice0;
+    m.window = window;
+    return m;
 }
 
 }  // namespace
@@ -575,63 +592,64 @@ extern "C" {
 
 int cqt_sliced_count(int64_t length) { return sliced_count(length); }
 
-int cqt_sliced_analysis(const cqt_tables* t, const float* x, int64_t ld, int rows,
-                        int64_t length, int slices, const float* window, float* coef,
-                        void* ws, size_t ws_bytes, void* stream) {
-    int rc = check_sliced(t, rows, slices, ld, length, ws, ws_bytes);
+int cqt_sliced_analysis(const cqt_tables* t, const cqt_signal* x, const cqt_slices* sl,
+                        float* coef, void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_sliced(t, sl, x, ws, ws_bytes);
     if (rc) return rc;
-    if (rows == 0) return CQT_OK;
-    if (!x || !coef || !window) return fail(CQT_ERR_ARG, "null signal, coefficients or window");
+    if (sl->rows == 0) return CQT_OK;
+    if (!x->data || !coef || !sl->window)
+        return fail(CQT_ERR_ARG, "null signal, coefficients or window");
     if ((uintptr_t)coef & 7u) return fail(CQT_ERR_ARG, "coefficient buffer not 8-byte aligned");
-    const SigMap in{x, nullptr, ld, length, slices, window};
     const CoefPtr out{coef, nullptr, 1};
-    return run_fwd(t, 0, in, out, band_params_sliced(t, rows, slices), rows * slices, ws,
-                   static_cast<cudaStream_t>(stream));
+    return run_fwd(t, 0, sig_map(sl, x, true, sl->window), out,
+                   band_params_sliced(t, sl->rows, sl->slice0, sl->slices),
+                   sl->rows * sl->slices, ws, static_cast<cudaStream_t>(stream));
 }
 
-int cqt_sliced_adj_synthesis(const cqt_tables* t, const float* gy, int64_t ld, int rows,
-                             int64_t length, int slices, float* gcoef, void* ws,
-                             size_t ws_bytes, void* stream) {
-    int rc = check_sliced(t, rows, slices, ld, length, ws, ws_bytes);
+int cqt_sliced_adj_synthesis(const cqt_tables* t, const cqt_signal* gy, const cqt_slices* sl,
+                             float* gcoef, void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_sliced(t, sl, gy, ws, ws_bytes);
     if (rc) return rc;
-    if (rows == 0) return CQT_OK;
-    if (!gy || !gcoef) return fail(CQT_ERR_ARG, "null gradient buffers");
+    if (sl->rows == 0) return CQT_OK;
+    if (!gy->data || !gcoef) return fail(CQT_ERR_ARG, "null gradient buffers");
     if ((uintptr_t)gcoef & 7u) return fail(CQT_ERR_ARG, "coefficient buffer not 8-byte aligned");
-    const SigMap in{gy, nullptr, ld, length, slices, nullptr};
     const CoefPtr out{gcoef, nullptr, 1};
-    return run_fwd(t, 1, in, out, band_params_sliced(t, rows, slices), rows * slices, ws,
-                   static_cast<cudaStream_t>(stream));
+    return run_fwd(t, 1, sig_map(sl, gy, true, nullptr), out,
+                   band_params_sliced(t, sl->rows, sl->slice0, sl->slices),
+                   sl->rows * sl->slices, ws, static_cast<cudaStream_t>(stream));
 }
 
-static int sliced_inv(const cqt_tables* t, int which, const float* coef, int rows, int slices,
-                      const float* window, float* y, int64_t ld, int64_t length, void* ws,
-                      size_t ws_bytes, void* stream) {
-    int rc = check_sliced(t, rows, slices, ld, length, ws, ws_bytes);
+static int sliced_inv(const cqt_tables* t, int which, const float* coef, const cqt_slices* sl,
+                      const float* window, const cqt_signal* y, void* ws, size_t ws_bytes,
+                      void* stream) {
+    int rc = check_sliced(t, sl, y, ws, ws_bytes);
     if (rc) return rc;
-    if (rows == 0) return CQT_OK;
-    if (!coef || !y) return fail(CQT_ERR_ARG, "null coefficients or output");
+    if (sl->rows == 0) return CQT_OK;
+    if (!coef || !y->data) return fail(CQT_ERR_ARG, "null coefficients or output");
     if ((uintptr_t)coef & 7u) return fail(CQT_ERR_ARG, "coefficient buffer not 8-byte aligned");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // overlap-add target: zero the rows first (stream-ordered, capturable)
-    cudaError_t e = cudaMemset2DAsync(y, (size_t)ld * sizeof(float), 0,
-                                      (size_t)length * sizeof(float), rows, s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync(overlap-add target)");
-    const SigMap out{nullptr, y, ld, length, slices, window};
+    if (y->count > 0) {
+        cudaError_t e = cudaMemset2DAsync(y->data, (size_t)y->ld * sizeof(float), 0,
+                                          (size_t)y->count * sizeof(float), sl->rows, s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync(overlap-add target)");
+    }
     const CoefPtr in{const_cast<float*>(coef), nullptr, 1};
-    return run_inv(t, which, in, out, band_params_sliced(t, rows, slices), rows * slices, ws, s);
+    return run_inv(t, which, in, sig_map(sl, y, false, window),
+                   band_params_sliced(t, sl->rows, sl->slice0, sl->slices),
+                   sl->rows * sl->slices, ws, s);
 }
 
-int cqt_sliced_synthesis(const cqt_tables* t, const float* coef, int rows, int slices,
-                         float* y, int64_t ld, int64_t length, void* ws, size_t ws_bytes,
-                         void* stream) {
-    return sliced_inv(t, 0, coef, rows, slices, nullptr, y, ld, length, ws, ws_bytes, stream);
+int cqt_sliced_synthesis(const cqt_tables* t, const float* coef, const cqt_slices* sl,
+                         const cqt_signal* y, void* ws, size_t ws_bytes, void* stream) {
+    return sliced_inv(t, 0, coef, sl, nullptr, y, ws, ws_bytes, stream);
 }
 
-int cqt_sliced_adj_analysis(const cqt_tables* t, const float* gcoef, int rows, int slices,
-                            const float* window, float* gx, int64_t ld, int64_t length,
-                            void* ws, size_t ws_bytes, void* stream) {
-    if (!window) return fail(CQT_ERR_ARG, "the transpose of the sliced analysis needs the window");
-    return sliced_inv(t, 1, gcoef, rows, slices, window, gx, ld, length, ws, ws_bytes, stream);
+int cqt_sliced_adj_analysis(const cqt_tables* t, const float* gcoef, const cqt_slices* sl,
+                            const cqt_signal* gx, void* ws, size_t ws_bytes, void* stream) {
+    if (!sl || !sl->window)
+        return fail(CQT_ERR_ARG, "the transpose of the sliced analysis needs the window");
+    return sliced_inv(t, 1, gcoef, sl, sl->window, gx, ws, ws_bytes, stream);
 }
 
 }  // extern "C"

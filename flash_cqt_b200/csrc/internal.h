@@ -39,7 +39,8 @@ constexpr int kMaxGroups = 16;
 // or -M/4 (odd slice), sliced.py:119-146) and [rows][S][M] (DC and Nyquist
 // side groups, not rolled).  S == 0 selects the per-slice heap layout.
 struct SliceLayout {
-    int S;                          // slices per signal row
+    int S;                          // slices per signal row in this call
+    int slice0;                     // global index of the first slice (roll parity)
     long long goff[kMaxGroups];     // complex offset of each group block
     int grows[kMaxGroups];          // bands in the group
     int groll[kMaxGroups];          // 1: coefficients rolled by +-M/4
@@ -47,20 +48,26 @@ struct SliceLayout {
 
 // where a slice's samples come from (analysis front end) or go to
 // (synthesis back end).  S == 0: contiguous [B][65536] slices.  S > 0:
-// slice s of row r covers samples 2H (s - 1) + j, j < 4H (H = 16384) of a
-// [rows][ld] signal of `length` samples, in the quarter-rolled order of
-// sliced.py:106-117 (sample n of the slice is j = (n +- H) mod 4H, + for even
-// s); the window (if not null) multiplies sample j; outside [0, length) the
-// input reads zero and the output drops the sample.  Outputs overlap-add
-// (two slices per sample) into a zeroed signal.
+// local slice s is global slice g = slice0 + s of a [rows][length] signal and
+// covers global samples 2H (g - 1) + j, j < 4H (H = 16384), in the quarter-
+// rolled order of sliced.py:106-117 (sample n of the slice is
+// j = (n +- H) mod 4H, + for even g); the window (if not null) multiplies
+// sample j.  The buffer row holds global samples [sample0, sample0 + count)
+// at stride ld; samples outside that window or outside [0, length) read as
+// zero / are dropped.  Outputs overlap-add (two slices per sample) into a
+// zeroed buffer.
 struct SigMap {
     const float* x;        // input signal (analysis engine)
     float* y;              // output signal (synthesis engine)
     long long ld;          // row stride in floats
-    long long length;
+    long long length;      // global signal length
+    long long sample0;     // global sample index of buffer column 0
+    long long count;       // samples held per buffer row
     int S;
+    int slice0;
     const float* window;   // [65536] or null
 };
+
 // everything a band kernel needs besides the per-tap tables, passed by value
 // (kernel parameters live in the constant bank: no dependent global loads)
 struct BandParams {

@@ -146,9 +146,10 @@ __device__ __forceinline__ void spec_stages(float2 (&v)[P], float2* buf, const f
 
 // one packed input pair z[n] = (sample 2n, sample 2n + 1) of slice g
 struct SliceReader {
-    const float* row;      // signal row (sliced) or slice base (contiguous)
-    long long p0;          // sample of slice position 0 (sliced)
-    long long length;
+    const float* row;      // buffer row (sliced) or slice base (contiguous)
+    long long p0;          // global sample of slice position 0 (sliced)
+    long long lo, hi;      // readable global samples [lo, hi)
+    long long sample0;     // global sample of row[0]
     int shift;             // +-H
     const float* window;
     bool sliced;
@@ -157,8 +158,8 @@ struct SliceReader {
         const int j = (2 * n + shift) & (kSlice - 1);
         const long long p = p0 + j;
         float2 v;
-        v.x = (p >= 0 && p < length) ? __ldg(row + p) : 0.f;
-        v.y = (p + 1 >= 0 && p + 1 < length) ? __ldg(row + p + 1) : 0.f;
+        v.x = (p >= lo && p < hi) ? __ldg(row + (p - sample0)) : 0.f;
+        v.y = (p + 1 >= lo && p + 1 < hi) ? __ldg(row + (p + 1 - sample0)) : 0.f;
         if (window) {
             v.x *= __ldg(window + j);
             v.y *= __ldg(window + j + 1);
@@ -167,22 +168,30 @@ struct SliceReader {
     }
 };
 
+// global sample range a buffer row can hold: [max(0, sample0), min(length, sample0 + count))
+__device__ __forceinline__ void sample_range(const SigMap& m, long long& lo, long long& hi) {
+    lo = m.sample0 > 0 ? m.sample0 : 0;
+    hi = m.sample0 + m.count < m.length ? m.sample0 + m.count : m.length;
+}
+
 template <bool SLICED>
 __device__ __forceinline__ SliceReader make_reader(const SigMap& m, long long g) {
     SliceReader r;
     r.sliced = SLICED;
     r.window = m.window;
-    r.length = m.length;
     if constexpr (!SLICED) {
         r.row = m.x + g * kSlice;
         r.p0 = 0;
+        r.lo = r.hi = r.sample0 = 0;
         r.shift = 0;
     } else {
         const long long row = g / m.S;
-        const int s = (int)(g % m.S);
+        const int sg = m.slice0 + (int)(g % m.S);
         r.row = m.x + row * m.ld;
-        r.p0 = 2LL * kQuarter * (s - 1);
-        r.shift = (s & 1) ? -kQuarter : kQuarter;
+        r.p0 = 2LL * kQuarter * (sg - 1);
+        sample_range(m, r.lo, r.hi);
+        r.sample0 = m.sample0;
+        r.shift = (sg & 1) ? -kQuarter : kQuarter;
     }
     return r;
 }
@@ -342,12 +351,13 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
         // sample receives exactly two terms, and a + b == b + a, so the
         // result does not depend on the order of the two atomic adds
         const long long row = slice / out.S;
-        const int s = (int)(slice % out.S);
-        float* yr = out.y + row * out.ld;
-        const long long p0 = 2LL * kQuarter * (s - 1);
-        const int shift = (s & 1) ? -kQuarter : kQuarter;
+        const int sg = out.slice0 + (int)(slice % out.S);
+        float* yr = out.y + row * out.ld - out.sample0;   // indexed by global sample
+        const long long p0 = 2LL * kQuarter * (sg - 1);
+        const int shift = (sg & 1) ? -kQuarter : kQuarter;
         const float* wnd = out.window;
-        const long long len = out.length;
+        long long lo, hi;
+        sample_range(out, lo, hi);
         spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
             constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
 #pragma unroll
@@ -362,8 +372,8 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
                         val.y *= __ldg(wnd + j + 1);
                     }
                     const long long p = p0 + j;
-                    if (p >= 0 && p < len) atomicAdd(yr + p, val.x);
-                    if (p + 1 >= 0 && p + 1 < len) atomicAdd(yr + p + 1, val.y);
+                    if (p >= lo && p < hi) atomicAdd(yr + p, val.x);
+                    if (p + 1 >= lo && p + 1 < hi) atomicAdd(yr + p + 1, val.y);
                 }
         });
     }

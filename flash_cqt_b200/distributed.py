@@ -1,0 +1,125 @@
+"""Slice-range partitioning of the sliced transform over several GPUs.
+
+One process per GPU (``torch.distributed``, NCCL for CUDA tensors).  A long
+stream of S slices (SlicedCQT, 50 % overlap, hop 2H = 32768 samples) is cut
+into contiguous slice ranges, rank r owning slices [s0, s1) and the output
+samples [2H s0, 2H s1):
+
+* analysis needs no communication -- slice g reads global samples
+  [2H (g - 1), 2H (g + 1)), so a rank reads its range plus one hop of input
+  halo at each end (``input_window``), from a replicated signal or from the
+  chunk it was handed;
+* synthesis overlap-adds inside the rank; output hop q receives slices q and
+  q + 1, so the only hop a rank cannot finish alone is its last one, which
+  also gets the first-half contribution of the next rank's first slice.  Each
+  rank r > 0 therefore sends one hop (2H samples per row) to rank r - 1, which
+  adds it in (``exchange_halo``); nothing else crosses NVLink.
+
+The partition is pure bookkeeping on slice indices; the transform itself is
+the fused sliced kernels (``SlicedEngine``) on each rank's device.
+"""
+import torch
+import torch.distributed as dist
+
+
+def slice_ranges(S, world):
+    """Balanced contiguous slice ranges [(s0, s1)] for `world` ranks."""
+    base, extra = divmod(S, world)
+    out, s = [], 0
+    for r in range(world):
+        n = base + (1 if r < extra else 0)
+        out.append((s, s + n))
+        s += n
+    return out
+
+
+class Partition:
+    """Geometry of one rank's share of a stream of `length` samples."""
+
+    def __init__(self, length, S, rank, world, hop=32768):
+        self.length, self.S, self.rank, self.world, self.hop = length, S, rank, world, hop
+        self.s0, self.s1 = slice_ranges(S, world)[rank]
+        self.nslices = self.s1 - self.s0
+
+    def input_window(self):
+        """global input samples the rank's slices read: [start, stop)"""
+        return self.hop * (self.s0 - 1), self.hop * (self.s1 + 1)
+
+    def synthesis_window(self):
+        """global samples the rank's slices overlap-add into: one hop before
+        the owned range (sent to the left neighbour) plus the owned range"""
+        return self.hop * (self.s0 - 1), self.hop * self.s1
+
+    def owned(self):
+        """global output samples the rank owns after the halo exchange"""
+        lo = self.hop * self.s0
+        hi = min(self.hop * self.s1, self.length)
+        return lo, max(lo, hi)
+
+
+def exchange_halo(local, part, group=None):
+    """local [rows, 2H + owned...]: the rank's overlap-added synthesis over
+    ``part.synthesis_window()``.  Sends the first hop to rank - 1, adds the
+    hop received from rank + 1 into the last owned hop, and returns the owned
+    part (a view of `local`).  Every rank makes the same calls in the same
+    order (ranks with no neighbour skip the matching side)."""
+    H2 = part.hop
+    ops = []
+    recv = None
+    if part.rank > 0 and part.nslices > 0:
+        ops.append(dist.P2POp(dist.isend, local[:, :H2].contiguous(), part.rank - 1,
+                              group=group))
+    if part.rank + 1 < part.world:
+        recv = torch.empty(local.shape[0], H2, dtype=local.dtype, device=local.device)
+        ops.append(dist.P2POp(dist.irecv, recv, part.rank + 1, group=group))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+    if recv is not None and part.nslices > 0:
+        local[:, -H2:] += recv
+    lo, hi = part.owned()
+    start = lo - part.synthesis_window()[0]
+    return local[:, start:start + (hi - lo)]
+
+
+class PartitionedSlicedCQT:
+    """A SlicedCQT whose slices are spread over the ranks of a process group.
+
+        part = PartitionedSlicedCQT(SlicedCQT(..., device=f"cuda:{rank}"), rank, world)
+        blocks, side = part.fwd(x_chunk, length, sample0)   # this rank's slices
+        y_owned = part.bwd(blocks, side, length)           # owned samples only
+    """
+
+    def __init__(self, sliced, rank, world, group=None):
+        self.sl = sliced
+        self.rank, self.world, self.group = rank, world, group
+
+    def partition(self, length):
+        return Partition(length, self.sl._num_slices(length), self.rank, self.world,
+                         self.sl.hop)
+
+    def fwd(self, x, length, sample0=0):
+        """x [B, C, count]: global samples [sample0, sample0 + count) of the
+        signals (the rank's input window, or the whole replicated signal).
+        Returns the blocks of the rank's slices in SlicedCQT.fwd's layout."""
+        B, C, _ = x.shape
+        p = self.partition(length)
+        se = self.sl._fused(x.device)
+        if se is None:
+            raise RuntimeError("the partitioned transform needs the default CUDA engine")
+        buf = se.analysis(x.reshape(B * C, -1), p.nslices, slice0=p.s0,
+                          sample0=sample0, length=length)
+        return se.group_views(buf, (B, C), p.nslices)
+
+    def bwd(self, blocks, side, length):
+        """synthesis of the rank's slices + halo exchange -> the rank's owned
+        output samples [B, C, owned]"""
+        B, C = blocks[0].shape[:2]
+        p = self.partition(length)
+        se = self.sl._fused(blocks[0].device)
+        buf = self.sl._fused_buffer(se, blocks, side, B * C, p.nslices)
+        lo, hi = p.synthesis_window()
+        local = se.synthesis(buf, B * C, p.nslices, length, slice0=p.s0, sample0=lo,
+                             count=hi - lo)
+        own = exchange_halo(local, p, self.group)
+        return own.reshape(B, C, -1)

@@ -3,6 +3,8 @@
 PyTorch only provides device memory and the current stream here; every
 transform runs in the sm_100a kernels of ``libflashcqt_b200.so``.
 """
+import ctypes
+
 import torch
 
 from . import _native
@@ -190,7 +192,7 @@ class SlicedEngine:
 
     def _sig(self, x, name):
         if x.device != self.eng.dev or x.dtype != torch.float32 or x.dim() != 2:
-            raise ValueError(f"{name} must be float32 [rows, length] on {self.eng.dev}")
+            raise ValueError(f"{name} must be float32 [rows, samples] on {self.eng.dev}")
         if x.stride(-1) != 1:
             x = x.contiguous()
         return x
@@ -199,41 +201,62 @@ class SlicedEngine:
         with torch.cuda.device(self.eng.dev):
             self.eng.tables.sliced(name, *args)
 
-    def analysis(self, x, S=None, out=None, adjoint_of_synthesis=False):
-        """x [rows, L] -> coefficient buffer complex64 [rows * S * ncoef]."""
+    def _slices(self, rows, slice0, S, window):
+        return self.N.CqtSlices(rows, slice0, S, window.data_ptr() if window is not None else None)
+
+    def _signal(self, t, sample0, length):
+        return self.N.CqtSignal(t.data_ptr(), t.stride(0), int(sample0), t.shape[1],
+                                int(length))
+
+    def analysis(self, x, S=None, out=None, adjoint_of_synthesis=False, slice0=0,
+                 sample0=0, length=None):
+        """x [rows, count] holding global samples [sample0, sample0 + count)
+        of signals of global length `length` (default sample0 + count) ->
+        coefficients of global slices [slice0, slice0 + S), complex64
+        [rows * S * ncoef].  The transpose of the synthesis uses no window."""
         x = self._sig(x, "signal")
-        rows, L = x.shape
-        S = self.count(L) if S is None else S
+        rows, count = x.shape
+        length = sample0 + count if length is None else int(length)
+        S = self.count(length) - slice0 if S is None else int(S)
         if out is None:
             out = torch.empty(self.coef_numel(rows, S), dtype=torch.complex64,
                               device=self.eng.dev)
         ws = self.eng.workspace(rows * S)
         stream = int(torch.cuda.current_stream(self.eng.dev).cuda_stream)
+        sig = self._signal(x, sample0, length)
         if adjoint_of_synthesis:
-            self._call("cqt_sliced_adj_synthesis", x.data_ptr(), x.stride(0), rows, L, S,
+            sl = self._slices(rows, slice0, S, None)
+            self._call("cqt_sliced_adj_synthesis", ctypes.byref(sig), ctypes.byref(sl),
                        out.data_ptr(), ws.data_ptr(), ws.numel(), stream)
         else:
-            self._call("cqt_sliced_analysis", x.data_ptr(), x.stride(0), rows, L, S,
-                       self.window.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
-                       stream)
+            sl = self._slices(rows, slice0, S, self.window)
+            self._call("cqt_sliced_analysis", ctypes.byref(sig), ctypes.byref(sl),
+                       out.data_ptr(), ws.data_ptr(), ws.numel(), stream)
         return out
 
-    def synthesis(self, coef, rows, S, length, out=None, adjoint_of_analysis=False):
-        """coefficient buffer -> y [rows, length] (overlap-added)."""
+    def synthesis(self, coef, rows, S, length, out=None, adjoint_of_analysis=False,
+                  slice0=0, sample0=0, count=None):
+        """coefficients of global slices [slice0, slice0 + S) -> overlap-added
+        output [rows, count] holding global samples [sample0, sample0 + count)
+        (default: the whole signal [0, length)).  The transpose of the
+        analysis applies the window."""
         if coef.dtype != torch.complex64 or coef.device != self.eng.dev:
             raise ValueError("coefficients must be complex64 on the engine's device")
         coef = coef.resolve_conj().contiguous()
         if coef.numel() != self.coef_numel(rows, S):
             raise ValueError("coefficient buffer does not match rows * S * ncoef")
+        count = int(length) - sample0 if count is None else int(count)
         if out is None:
-            out = torch.empty(rows, length, dtype=torch.float32, device=self.eng.dev)
+            out = torch.empty(rows, count, dtype=torch.float32, device=self.eng.dev)
         ws = self.eng.workspace(rows * S)
         stream = int(torch.cuda.current_stream(self.eng.dev).cuda_stream)
+        sig = self._signal(out, sample0, length)
         if adjoint_of_analysis:
-            self._call("cqt_sliced_adj_analysis", coef.data_ptr(), rows, S,
-                       self.window.data_ptr(), out.data_ptr(), out.stride(0), length,
-                       ws.data_ptr(), ws.numel(), stream)
+            sl = self._slices(rows, slice0, S, self.window)
+            self._call("cqt_sliced_adj_analysis", coef.data_ptr(), ctypes.byref(sl),
+                       ctypes.byref(sig), ws.data_ptr(), ws.numel(), stream)
         else:
-            self._call("cqt_sliced_synthesis", coef.data_ptr(), rows, S, out.data_ptr(),
-                       out.stride(0), length, ws.data_ptr(), ws.numel(), stream)
+            sl = self._slices(rows, slice0, S, None)
+            self._call("cqt_sliced_synthesis", coef.data_ptr(), ctypes.byref(sl),
+                       ctypes.byref(sig), ws.data_ptr(), ws.numel(), stream)
         return out

@@ -156,35 +156,55 @@ int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* c_re,
                          float* c_im, int layout, int batch, void* stream);
 
 /* ---- Sliced streaming transform (SlicedCQT, sliced.py:41-167) ----------
- * A signal of `rows` rows (row stride `ld` floats, `length` samples) is cut
- * into S = cqt_sliced_count(length) slices of 65536 samples at 50 % overlap:
- * slice s covers samples 32768 (s - 1) + j, j < 65536, multiplied by the
- * slice window, and is quarter-rolled (-16384 for even s, +16384 for odd s).
+ * A signal of `rows` rows and global length `length` is cut into
+ * S = cqt_sliced_count(length) slices of 65536 samples at 50 % overlap:
+ * global slice g covers global samples 32768 (g - 1) + j, j < 65536,
+ * multiplied by the slice window (analysis), and is quarter-rolled (-16384
+ * for even g, +16384 for odd g).  One call processes slices
+ * [slice0, slice0 + slices) of every row, so a long stream can be split
+ * into slice ranges (e.g. one per GPU).
+ * Signal buffers (cqt_signal) hold, per row at stride ld, the global samples
+ * [sample0, sample0 + count); samples outside that window or outside
+ * [0, length) read as zero (inputs) or are dropped (outputs).  Outputs are
+ * zeroed, then overlap-added: a sample gets the terms of the (at most two)
+ * slices of the call that cover it, order-independent (deterministic).
  * Coefficients live in one interleaved complex64 buffer of
- * rows * S * ncoef values, group after group (group g at offset
- * rows * S * sum_{g' < g} count_g' M_g'): octave groups as [rows][count][S M]
- * (slices in time order, each slice's block rolled by +M/4 (even s) or -M/4
- * (odd s)), side groups as [rows][S][M] -- exactly the blocks of
- * SlicedCQT.fwd.  Synthesis un-rolls and overlap-adds into a signal it
- * zeroes first (two terms per sample, order-independent: deterministic).
- * The workspace is cqt_workspace_bytes(t, rows * S).  window: device
- * float32[65536] (the Tukey slice window), required for the analysis and
- * its transpose. */
+ * rows * slices * ncoef values, group after group (group k at offset
+ * rows * slices * sum_{k' < k} count_k' M_k'): octave groups as
+ * [rows][count][slices * M] (slices in time order, each slice's block rolled
+ * by +M/4 (even g) or -M/4 (odd g)), side groups as [rows][slices][M] --
+ * exactly the blocks of SlicedCQT.fwd.  Workspace:
+ * cqt_workspace_bytes(t, rows * slices). */
+typedef struct cqt_signal {
+    float* data;        /* device; const for inputs */
+    int64_t ld;         /* row stride in floats, >= count */
+    int64_t sample0;    /* global sample held in data[0] (may be negative) */
+    int64_t count;      /* samples held per row */
+    int64_t length;     /* global signal length */
+} cqt_signal;
+
+typedef struct cqt_slices {
+    int32_t rows;
+    int32_t slice0;          /* global index of the first slice of the call */
+    int32_t slices;          /* slices per row in the call */
+    const float* window;     /* device float32[65536] slice window; analysis
+                                and its transpose only */
+} cqt_slices;
+
 int cqt_sliced_count(int64_t length);
-int cqt_sliced_analysis(const cqt_tables* t, const float* x, int64_t ld, int rows,
-                        int64_t length, int slices, const float* window, float* coef,
-                        void* workspace, size_t workspace_bytes, void* stream);
-int cqt_sliced_synthesis(const cqt_tables* t, const float* coef, int rows, int slices,
-                         float* y, int64_t ld, int64_t length, void* workspace,
-                         size_t workspace_bytes, void* stream);
+int cqt_sliced_analysis(const cqt_tables* t, const cqt_signal* x, const cqt_slices* sl,
+                        float* coef, void* workspace, size_t workspace_bytes, void* stream);
+int cqt_sliced_synthesis(const cqt_tables* t, const float* coef, const cqt_slices* sl,
+                         const cqt_signal* y, void* workspace, size_t workspace_bytes,
+                         void* stream);
 /* transposes: coefficient gradients -> dL/dx (window applied, overlap-add),
  * dL/dy -> coefficient gradients (no window) */
-int cqt_sliced_adj_analysis(const cqt_tables* t, const float* gcoef, int rows, int slices,
-                            const float* window, float* gx, int64_t ld, int64_t length,
-                            void* workspace, size_t workspace_bytes, void* stream);
-int cqt_sliced_adj_synthesis(const cqt_tables* t, const float* gy, int64_t ld, int rows,
-                             int64_t length, int slices, float* gcoef, void* workspace,
-                             size_t workspace_bytes, void* stream);
+int cqt_sliced_adj_analysis(const cqt_tables* t, const float* gcoef, const cqt_slices* sl,
+                            const cqt_signal* gx, void* workspace, size_t workspace_bytes,
+                            void* stream);
+int cqt_sliced_adj_synthesis(const cqt_tables* t, const cqt_signal* gy, const cqt_slices* sl,
+                             float* gcoef, void* workspace, size_t workspace_bytes,
+                             void* stream);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* cqt_last_error(void);
