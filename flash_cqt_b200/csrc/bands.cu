@@ -79,6 +79,7 @@ struct TwLayout {
 template <int M>
 __device__ __forceinline__ void fill_twiddles(float2* tws, const float2* __restrict__ w2048) {
     using L = TwLayout<M>;
+#pragma unroll
     for (int e = threadIdx.x; e < L::n2 + L::n3; e += kBandThreads) {
         int r, k, span, R;
         if (e < L::n2) {
@@ -249,7 +250,13 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
             lo = in.d.y;
             n = d_lg(in.d);
         }
-        for (int i = t; i < n; i += T) cp_async8(buf + PADI<kSH>(i), Xs + lo + i);
+        // fixed trip count (n <= M), predicated: no loop control
+        const float2* xsrc = Xs + lo;
+#pragma unroll
+        for (int k = 0; k < kP; ++k) {
+            const int i = t + k * T;
+            if (i < n) cp_async8(buf + PADI<kSH>(i), xsrc + i);
+        }
     }
     fill_twiddles<M>(tws, bp.tw2048);
     // stage 1 taps: element r of butterfly b is tap t + T b + r M / R1.
@@ -339,10 +346,15 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     if (in.valid) {
         if (in_c.interleaved) {
             const float2* src = reinterpret_cast<const float2*>(in_c.re) + ca.base;
-            for (int i = t; i < M; i += T)
+#pragma unroll
+            for (int k = 0; k < kP; ++k) {
+                const int i = t + k * T;
                 cp_async8(buf + PADI<kSH>(i), src + (SLICED ? ((i + ca.roll) & (M - 1)) : i));
+            }
         } else {
-            for (int i = t; i < M; i += T) {
+#pragma unroll
+            for (int k = 0; k < kP; ++k) {
+                const int i = t + k * T;
                 const long long ix = ca.base + (SLICED ? ((i + ca.roll) & (M - 1)) : i);
                 cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)), in_c.re + ix);
                 cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)) + 1, in_c.im + ix);

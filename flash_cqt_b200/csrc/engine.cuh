@@ -36,26 +36,68 @@ __device__ __forceinline__ float2 tw64k(const float2* hi, const float2* lo, int 
 }
 
 // ---------------------------------------------------------------- stages
+// PADI<SH>(a + c) == PADI<SH>(a) + c + (c >> SH) whenever c is a multiple of
+// 2^SH, so every shared-memory address below is one per-thread base plus
+// compile-time offsets when the stage geometry allows it (it does for all
+// but the smallest block lengths); otherwise the generic formula is used.
+
 // Read the inputs of a radix-R stage of length M for butterflies
 // j = t + T * b (b < P / R) from a padded shared buffer.
 template <int M, int T, int R, int SH, int P>
 __device__ __forceinline__ void stage_load(float2 (&v)[P], const float2* buf, int t) {
+    constexpr int Q = 1 << SH;
+    if constexpr ((T % Q) == 0 && ((M / R) % Q) == 0) {
+        const float2* p = buf + PADI<SH>(t);
 #pragma unroll
-    for (int b = 0; b < P / R; ++b)
+        for (int b = 0; b < P / R; ++b)
 #pragma unroll
-        for (int r = 0; r < R; ++r)
-            v[b * R + r] = buf[PADI<SH>(t + T * b + r * (M / R))];
+            for (int r = 0; r < R; ++r) {
+                const int c = T * b + r * (M / R);
+                v[b * R + r] = p[c + (c >> SH)];
+            }
+    } else {
+#pragma unroll
+        for (int b = 0; b < P / R; ++b)
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                v[b * R + r] = buf[PADI<SH>(t + T * b + r * (M / R))];
+    }
 }
 
 // Write the outputs of a radix-R stage with span NS to a padded shared buffer.
 template <int M, int T, int R, int NS, int SH, int P>
 __device__ __forceinline__ void stage_store(const float2 (&v)[P], float2* buf, int t) {
+    constexpr int Q = 1 << SH;
+    // butterfly b of the thread starts at base(t) + T R b when NS divides T
+    constexpr bool lin_b = (T % NS) == 0 && ((T * R) % Q) == 0;
+    if constexpr (lin_b && (NS % Q) == 0) {
+        float2* p = buf + PADI<SH>((t / NS) * NS * R + (t % NS));
 #pragma unroll
-    for (int b = 0; b < P / R; ++b) {
-        const int j = t + T * b;
-        const int base = (j / NS) * NS * R + (j % NS);
+        for (int b = 0; b < P / R; ++b)
 #pragma unroll
-        for (int r = 0; r < R; ++r) buf[PADI<SH>(base + r * NS)] = v[b * R + r];
+            for (int r = 0; r < R; ++r) {
+                const int c = T * R * b + r * NS;
+                p[c + (c >> SH)] = v[b * R + r];
+            }
+    } else if constexpr (lin_b && NS == 1 && (R % Q) == 0) {
+        // base = t R is a multiple of 2^SH and r < R <= ... stays inside one
+        // padding period per 2^SH outputs
+        float2* p = buf + PADI<SH>(t * R);
+#pragma unroll
+        for (int b = 0; b < P / R; ++b)
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int c = T * R * b + r;
+                p[c + (c >> SH)] = v[b * R + r];
+            }
+    } else {
+#pragma unroll
+        for (int b = 0; b < P / R; ++b) {
+            const int j = t + T * b;
+            const int base = (j / NS) * NS * R + (j % NS);
+#pragma unroll
+            for (int r = 0; r < R; ++r) buf[PADI<SH>(base + r * NS)] = v[b * R + r];
+        }
     }
 }
 
