@@ -79,8 +79,11 @@ struct TwLayout {
 template <int M>
 __device__ __forceinline__ void fill_twiddles(float2* tws, const float2* __restrict__ w2048) {
     using L = TwLayout<M>;
+    constexpr int NT = (L::n2 + L::n3 + kBandThreads - 1) / kBandThreads;
 #pragma unroll
-    for (int e = threadIdx.x; e < L::n2 + L::n3; e += kBandThreads) {
+    for (int it = 0; it < NT; ++it) {
+        const int e = threadIdx.x + it * kBandThreads;
+        if (e >= L::n2 + L::n3) break;
         int r, k, span, R;
         if (e < L::n2) {
             r = e / L::R1 + 1;
@@ -135,8 +138,13 @@ __device__ __forceinline__ Inst locate(const BandParams& bp, int c) {
     const int inst = (blockIdx.x - bp.sc.cta0[c]) * IPC + in.il;
     const int B = bp.sc.batch;
     in.valid = inst < bp.sc.nb[c] * B;
-    in.slice = in.valid ? inst % B : 0;
-    in.d = bp.desc[bp.sc.first[c] + (in.valid ? inst / B : 0)];
+    // inst / B by a float reciprocal (inst < 2^24) and one correction step
+    int q = __float2int_rz(__int2float_rn(inst) * bp.sc.inv_batch);
+    int rem = inst - q * B;
+    if (rem >= B) { ++q; rem -= B; }
+    if (rem < 0) { --q; rem += B; }
+    in.slice = in.valid ? rem : 0;
+    in.d = bp.desc[bp.sc.first[c] + (in.valid ? q : 0)];
     return in;
 }
 
@@ -309,6 +317,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     __syncthreads();   // the staged segment is dead; stage 1 reuses the buffer
 
     const CoefAddr ca = coef_addr<M, SLICED>(bp, in.slice, in.d);
+    const bool interleaved = out.interleaved != 0;   // uniform: hoisted out of the stores
     band_rest<M, +1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
@@ -320,7 +329,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
                 const float2 val = w[b * R + r];
                 const long long ix =
                     SLICED ? ca.base + ((nn + ca.roll) & (M - 1)) : ca.base + nn;
-                if (out.interleaved) {
+                if (interleaved) {
                     reinterpret_cast<float2*>(out.re)[ix] = val;
                 } else {
                     out.re[ix] = val.x;
@@ -419,9 +428,13 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     });
 }
 
+// class of this CTA: the number of class boundaries at or below blockIdx.x
+// (branch-free; unused classes have cta0 == grid)
 __device__ __forceinline__ int find_class(const BandSched& sc) {
     int c = 0;
-    while (c + 1 < sc.ncls && (int)blockIdx.x >= sc.cta0[c + 1]) ++c;
+#pragma unroll
+    for (int k = 1; k < kMaxClasses; ++k)
+        c += (k < sc.ncls && (int)blockIdx.x >= sc.cta0[k]) ? 1 : 0;
     return c;
 }
 
@@ -471,6 +484,7 @@ BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, in
     BandSched sc{};
     sc.ncls = ncls;
     sc.batch = batch;
+    sc.inv_batch = batch > 0 ? 1.0f / (float)batch : 0.f;
     int cta = 0;
     for (int c = 0; c < ncls; ++c) {
         sc.M[c] = M[c];

@@ -28,6 +28,7 @@ struct BandSched {         // CTA ranges of the block-length classes for one lau
     int first[kMaxClasses];    // first entry of the class in band_list
     int cta0[kMaxClasses + 1]; // first CTA of each class, cta0[ncls] = grid
     int batch;
+    float inv_batch;           // 1 / batch, for the instance -> (band, slice) split
 };
 
 constexpr int kMaxBands = 160;

@@ -235,7 +235,11 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     // untangle the (q, L - q) pairs of this parity: X[q] = E + W_N^q O
     float2* Xs = X + slice * kPlaneStride;
     const int npairs = h == 0 ? kQuarter / 2 + 1 : kQuarter / 2;
-    for (int kp = t; kp < npairs; kp += T) {
+    constexpr int NPIT = (kQuarter / 2 + 1 + T - 1) / T;
+#pragma unroll
+    for (int it = 0; it < NPIT; ++it) {
+        const int kp = t + it * T;
+        if (kp >= npairs) break;
         const int kq = h == 0 ? ((kQuarter - kp) & (kQuarter - 1)) : (kQuarter - 1 - kp);
         const float2 zq = buf[PADI<SH>(kp)];
         const float2 zb = buf[PADI<SH>(kq)];
@@ -302,7 +306,11 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
     const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
 
     // quads {n, L - n, Q + n, Q - n}: four bins in, u_h[n] and u_h[Q - n] out
-    for (int n = t; n <= kQuarter / 2; n += T) {
+    constexpr int NQIT = (kQuarter / 2 + 1 + T - 1) / T;
+#pragma unroll
+    for (int it = 0; it < NQIT; ++it) {
+        const int n = t + it * T;
+        if (n > kQuarter / 2) break;
         const int m = (kQuarter - n) & (kQuarter - 1);
         float2 fA = plane_sum(Es, mask, n, nplanes);
         float2 fB = plane_sum(Es, mask, kHalf - n, nplanes);
