@@ -306,11 +306,7 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
     const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
 
     // quads {n, L - n, Q + n, Q - n}: four bins in, u_h[n] and u_h[Q - n] out
-    constexpr int NQIT = (kQuarter / 2 + 1 + T - 1) / T;
-#pragma unroll
-    for (int it = 0; it < NQIT; ++it) {
-        const int n = t + it * T;
-        if (n > kQuarter / 2) break;
+    for (int n = t; n <= kQuarter / 2; n += T) {
         const int m = (kQuarter - n) & (kQuarter - 1);
         float2 fA = plane_sum(Es, mask, n, nplanes);
         float2 fB = plane_sum(Es, mask, kHalf - n, nplanes);
