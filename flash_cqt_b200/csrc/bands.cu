@@ -275,17 +275,24 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     float gain[kP];
     int src[kP];
     const int l = d_l(in.d);
+    {
+        const float* gp = tab.gain + off + t;
 #pragma unroll
-    for (int b = 0; b < kP / R1; ++b)
+        for (int b = 0; b < kP / R1; ++b)
 #pragma unroll
-        for (int r = 0; r < R1; ++r) {
-            const int m = t + T * b + r * (M / R1);
-            gain[b * R1 + r] = in.valid ? __ldg(tab.gain + off + m) : 0.f;
-            if (side) {
-                const int sv = in.valid ? __ldg(tab.src + off + m) : -1;
+            for (int r = 0; r < R1; ++r)
+                gain[b * R1 + r] = in.valid ? __ldg(gp + T * b + r * (M / R1)) : 0.f;
+    }
+    if (side) {   // uniform per instance: one branch, not one per tap
+        const int* sp = tab.src + off + t;
+#pragma unroll
+        for (int b = 0; b < kP / R1; ++b)
+#pragma unroll
+            for (int r = 0; r < R1; ++r) {
+                const int sv = in.valid ? __ldg(sp + T * b + r * (M / R1)) : -1;
                 src[b * R1 + r] = sv < 0 ? -1 : (((sv & 0xFFFF) - lo) | (sv & 0x10000));
             }
-        }
+    }
     cp_async_wait_all();
     __syncthreads();
     float2 v[kP];
@@ -321,21 +328,28 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     band_rest<M, +1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
+        if (interleaved) {
+            float2* o = reinterpret_cast<float2*>(out.re) + ca.base;
 #pragma unroll
-        for (int b = 0; b < kP / R; ++b)
+            for (int b = 0; b < kP / R; ++b)
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int nn = t + T * b + r * NS;
-                const float2 val = w[b * R + r];
-                const long long ix =
-                    SLICED ? ca.base + ((nn + ca.roll) & (M - 1)) : ca.base + nn;
-                if (interleaved) {
-                    reinterpret_cast<float2*>(out.re)[ix] = val;
-                } else {
-                    out.re[ix] = val.x;
-                    out.im[ix] = val.y;
+                for (int r = 0; r < R; ++r) {
+                    const int nn = t + T * b + r * NS;
+                    o[SLICED ? ((nn + ca.roll) & (M - 1)) : nn] = w[b * R + r];
                 }
-            }
+        } else {
+            float* ore = out.re + ca.base;
+            float* oim = out.im + ca.base;
+#pragma unroll
+            for (int b = 0; b < kP / R; ++b)
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int nn = t + T * b + r * NS;
+                    const int ix = SLICED ? ((nn + ca.roll) & (M - 1)) : nn;
+                    ore[ix] = w[b * R + r].x;
+                    oim[ix] = w[b * R + r].y;
+                }
+        }
     });
 }
 
@@ -404,27 +418,34 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     band_rest<M, -1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
+        if (side) {
 #pragma unroll
-        for (int b = 0; b < kP / R; ++b)
+            for (int b = 0; b < kP / R; ++b)
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int m = t + T * b + r * NS;
-                const float2 val = w[b * R + r];
-                if (side) {
+                for (int r = 0; r < R; ++r) {
+                    const int m = t + T * b + r * NS;
+                    const float2 val = w[b * R + r];
                     const int d = __ldg(tab.dest + off + m);
                     if (d >= 0)
                         Es[d] = make_float2(val.x * __ldg(tab.gre + off + m),
                                             val.y * __ldg(tab.gim + off + m));
-                } else {
+                }
+        } else {
+            float2* eb = Es + pbase;
+#pragma unroll
+            for (int b = 0; b < kP / R; ++b)
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int m = t + T * b + r * NS;
                     const int i = (m + l) & (M - 1);
 #if FCQT_PREFETCH_GAINS
                     const float g = gpre[b * R + r];
 #else
                     const float g = __ldg(tab.gre + off + m);
 #endif
-                    if (i < lg && g != 0.f) Es[pbase + i] = cscale(val, g);
+                    if (i < lg && g != 0.f) eb[i] = cscale(w[b * R + r], g);
                 }
-            }
+        }
     });
 }
 
