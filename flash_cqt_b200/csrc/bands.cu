@@ -259,11 +259,14 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
             n = d_lg(in.d);
         }
         // fixed trip count (n <= M), predicated: no loop control
-        const float2* xsrc = Xs + lo;
+        // X is parity-major; the thread stride T is even, so the parity of
+        // bin lo + t + k T is fixed and its slot advances by T / 2 per k
+        static_assert(T % 2 == 0, "band staging needs an even thread stride");
+        const float2* xsrc = Xs + xslot(lo + t);
 #pragma unroll
         for (int k = 0; k < kP; ++k) {
             const int i = t + k * T;
-            if (i < n) cp_async8(buf + PADI<kSH>(i), xsrc + i);
+            if (i < n) cp_async8(buf + PADI<kSH>(i), xsrc + k * (T / 2));
         }
     }
     fill_twiddles<M>(tws, bp.tw2048);

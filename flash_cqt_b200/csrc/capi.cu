@@ -120,6 +120,13 @@ BandParams band_params_sliced(const cqt_tables* t, int rows, int slice0, int sli
 SigMap contiguous_in(const float* x) { return SigMap{x, nullptr, 0, 0, 0, 0, 0, 0, nullptr}; }
 SigMap contiguous_out(float* y) { return SigMap{nullptr, y, 0, 0, 0, 0, 0, 0, nullptr}; }
 
+// contiguous signals are moved as float2 / float4: null or misaligned rows fail
+int check_signal(const float* p, bool input) {
+    if (!p) return fail(CQT_ERR_ARG, input ? "null input" : "null output");
+    if ((uintptr_t)p & 7u) return fail(CQT_ERR_ARG, "signal not 8-byte aligned");
+    return CQT_OK;
+}
+
 // one analysis-engine pass: real signal -> spectrum -> bands
 int run_fwd(const cqt_tables* t, int which, const SigMap& sig, CoefPtr out,
             const BandParams& bp, int batch, void* ws, cudaStream_t s) {
@@ -367,6 +374,19 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     size_t i_sym = add(h->sy_mask, maskB);
     size_t i_aad = add(h->aa_dest, nI), i_aar = add(h->aa_gre, nI), i_aai = add(h->aa_gim, nI);
     size_t i_aam = add(h->aa_mask, maskB);
+    // quad masks of the inverse spectrum engine
+    std::vector<uint16_t> qm_sy(kQuarter / 2 + 1), qm_aa(kQuarter / 2 + 1);
+    for (int n = 0; n <= kQuarter / 2; ++n) {
+        const int bins[4] = {n, kHalf - n, kQuarter + n, kQuarter - n};
+        uint16_t a = 0, b = 0;
+        for (int k = 0; k < 4; ++k) {
+            a |= (uint16_t)((h->sy_mask[bins[k]] & 15) << (4 * k));
+            b |= (uint16_t)((h->aa_mask[bins[k]] & 15) << (4 * k));
+        }
+        qm_sy[n] = a;
+        qm_aa[n] = b;
+    }
+    size_t i_qsy = add(qm_sy.data(), qm_sy.size() * 2), i_qaa = add(qm_aa.data(), qm_aa.size() * 2);
     size_t i_tw = add(h->tw2048, 2048 * 8), i_hi = add(h->tw_hi, 256 * 8), i_lo = add(h->tw_lo, 256 * 8);
     std::vector<float2> rows(spectrum_twiddle_count());
     spectrum_twiddle_rows(rows.data());
@@ -408,9 +428,11 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     t->fwd[0] = FwdTab{(const int*)P(i_ans), (const float*)P(i_ang), (const int2*)P(i_ansg)};
     t->fwd[1] = FwdTab{(const int*)P(i_ass), (const float*)P(i_asg), (const int2*)P(i_assg)};
     t->inv[0] = InvTab{(const int*)P(i_syd), (const float*)P(i_syr), (const float*)P(i_syi),
-                       (const unsigned char*)P(i_sym), h->sy_nplanes};
+                       (const unsigned char*)P(i_sym), (const unsigned short*)P(i_qsy),
+                       h->sy_nplanes};
     t->inv[1] = InvTab{(const int*)P(i_aad), (const float*)P(i_aar), (const float*)P(i_aai),
-                       (const unsigned char*)P(i_aam), h->aa_nplanes};
+                       (const unsigned char*)P(i_aam), (const unsigned short*)P(i_qaa),
+                       h->aa_nplanes};
     t->tw2048 = (const float2*)P(i_tw);
     t->ngroups = h->ngroups;
     for (int g = 0; g < h->ngroups; ++g) {
@@ -448,7 +470,7 @@ int cqt_analysis(const cqt_tables* t, const float* x, float* c_re, float* c_im, 
                  int batch, void* ws, size_t ws_bytes, void* stream) {
     int rc = check_common(t, batch, ws, ws_bytes, layout);
     if (rc) return rc;
-    if (batch && !x) return fail(CQT_ERR_ARG, "null input");
+    if (batch && (rc = check_signal(x, true))) return rc;
     CoefPtr out;
     if (batch && (rc = coef_ptr(c_re, c_im, layout, &out))) return rc;
     return run_fwd_engine(t, 0, x, out, batch, ws, static_cast<cudaStream_t>(stream));
@@ -458,7 +480,7 @@ int cqt_adj_synthesis(const cqt_tables* t, const float* gy, float* g_re, float* 
                       int layout, int batch, void* ws, size_t ws_bytes, void* stream) {
     int rc = check_common(t, batch, ws, ws_bytes, layout);
     if (rc) return rc;
-    if (batch && !gy) return fail(CQT_ERR_ARG, "null input");
+    if (batch && (rc = check_signal(gy, true))) return rc;
     CoefPtr out;
     if (batch && (rc = coef_ptr(g_re, g_im, layout, &out))) return rc;
     return run_fwd_engine(t, 1, gy, out, batch, ws, static_cast<cudaStream_t>(stream));
@@ -468,7 +490,7 @@ int cqt_synthesis(const cqt_tables* t, const float* c_re, const float* c_im, int
                   float* y, int batch, void* ws, size_t ws_bytes, void* stream) {
     int rc = check_common(t, batch, ws, ws_bytes, layout);
     if (rc) return rc;
-    if (batch && !y) return fail(CQT_ERR_ARG, "null output");
+    if (batch && (rc = check_signal(y, false))) return rc;
     CoefPtr in;
     if (batch && (rc = coef_ptr(c_re, c_im, layout, &in))) return rc;
     return run_inv_engine(t, 0, in, y, batch, ws, static_cast<cudaStream_t>(stream));
@@ -478,7 +500,7 @@ int cqt_adj_analysis(const cqt_tables* t, const float* g_re, const float* g_im, 
                      float* gx, int batch, void* ws, size_t ws_bytes, void* stream) {
     int rc = check_common(t, batch, ws, ws_bytes, layout);
     if (rc) return rc;
-    if (batch && !gx) return fail(CQT_ERR_ARG, "null output");
+    if (batch && (rc = check_signal(gx, false))) return rc;
     CoefPtr in;
     if (batch && (rc = coef_ptr(g_re, g_im, layout, &in))) return rc;
     return run_inv_engine(t, 1, in, gx, batch, ws, static_cast<cudaStream_t>(stream));
@@ -495,7 +517,7 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
     CoefPtr cp;
     switch (stage) {
     case 0:
-        if (!sig_in) return fail(CQT_ERR_ARG, "null input");
+        if ((rc = check_signal(sig_in, true))) return rc;
         e = launch_spectrum_fwd(contiguous_in(sig_in), static_cast<float2*>(ws), t->spec, batch,
                                 s);
         break;
@@ -510,7 +532,7 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
                              s);
         break;
     case 3:
-        if (!sig_out) return fail(CQT_ERR_ARG, "null output");
+        if ((rc = check_signal(sig_out, false))) return rc;
         e = launch_spectrum_inv(static_cast<const float2*>(ws), t->inv[0],
                                 contiguous_out(sig_out), t->spec, batch, s);
         break;
@@ -579,7 +601,7 @@ extern "C" int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* 
         }
     }
     if (batch == 0) return CQT_OK;
-    if (!x) return fail(CQT_ERR_ARG, "null input");
+    if ((rc = check_signal(x, true))) return rc;
     CoefPtr out;
     if ((rc = coef_ptr(c_re, c_im, layout, &out))) return rc;
     return run_fwd_engine(t, 0, x, out, batch, scratch, static_cast<cudaStream_t>(stream));

@@ -16,6 +16,9 @@ struct InvTab {            // synthesis-engine tap table (one per use)
     const float* gre;      // gain on the real part
     const float* gim;      // gain on the imaginary part
     const unsigned char* mask;  // per bin: bit p set when plane p holds a term
+    // per quad n in [0, Q/2]: the masks of bins n, L - n, Q + n, Q - n in
+    // bits 0-3, 4-7, 8-11, 12-15 (derived from `mask` at upload)
+    const unsigned short* qmask;
     int nplanes;
 };
 

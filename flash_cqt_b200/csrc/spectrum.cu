@@ -25,6 +25,9 @@
 // read lane-consecutive, hi rows are warp-uniform broadcasts).  The library
 // generates the rows in double precision at table upload.
 #include <cmath>
+#include <cstdint>
+
+#include <cooperative_groups.h>
 
 #include "engine.cuh"
 #include "internal.h"
@@ -196,11 +199,46 @@ __device__ __forceinline__ SliceReader make_reader(const SigMap& m, long long g)
     return r;
 }
 
+// L2 prefetch of one 128-byte line
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// Each spectrum CTA holds a whole SM (one CTA per SM), so its load phase and
+// its shared-memory stages cannot overlap another CTA's.  Instead, on entry it
+// prefetches into L2 the input of the CTA one wave ahead (`ahead` = the number
+// of resident CTAs), which that CTA then reads at L2 speed.  Only addresses
+// inside the readable ranges are touched.
+template <bool SLICED, int T>
+__device__ __forceinline__ void prefetch_signal_half(const SigMap& m, long g, int half, int t) {
+    if constexpr (!SLICED) {
+        const float* base = m.x + g * kSlice + half * (kSlice / 2);
+        for (int i = t; i < kSlice / 2 / 32; i += T) prefetch_l2(base + 32 * i);
+    } else {
+        const long long row = g / m.S;
+        const int sg = m.slice0 + (int)(g % m.S);
+        long long lo, hi;
+        lo = m.sample0 > 0 ? m.sample0 : 0;
+        hi = m.sample0 + m.count < m.length ? m.sample0 + m.count : m.length;
+        long long a = 2LL * kQuarter * (sg - 1) + half * (kSlice / 2);
+        long long b = a + kSlice / 2;
+        a = a > lo ? a : lo;
+        b = b < hi ? b : hi;
+        if (a >= b) return;
+        const float* r = m.x + row * m.ld - m.sample0;
+        const int lines = (int)((b - a + 31) / 32);
+        for (int i = t; i < lines; i += T) {
+            const long long p = a + 32LL * i;
+            prefetch_l2(r + (p < b ? p : b - 1));
+        }
+    }
+}
+
 template <bool SLICED>
 __global__ void __launch_bounds__(SpecCfg<kPF>::T, 1)
 spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                     const float2* __restrict__ ghi, const float2* __restrict__ glo,
-                    const float2* __restrict__ gtw) {
+                    const float2* __restrict__ gtw, int ahead) {
     constexpr int P = kPF, T = SpecCfg<P>::T, SH = shiftOf<P>();
     using C = SpecCfg<P>;
     extern __shared__ float4 smem_raw[];
@@ -210,6 +248,10 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     const int h = blockIdx.x & 1;
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
+    if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
+        const long nb = blockIdx.x + (long)ahead;
+        prefetch_signal_half<SLICED, T>(in, nb >> 1, (int)(nb & 1), t);
+    }
     load_tables<P>(hl, tws, ghi, glo, gtw);
     __syncthreads();
     const Tw64k tw{hl, hl + 256};
@@ -232,8 +274,10 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     });
     __syncthreads();
 
-    // untangle the (q, L - q) pairs of this parity: X[q] = E + W_N^q O
-    float2* Xs = X + slice * kPlaneStride;
+    // untangle the (q, L - q) pairs of this parity: X[q] = E + W_N^q O, into
+    // this parity's half of the (parity-major) spectrum row: bin q = 2 kp + h
+    // at slot kp, bin L - q at slot Q - h - kp
+    float2* Xp = X + slice * kPlaneStride + (h ? kOddX : 0);
     const int npairs = h == 0 ? kQuarter / 2 + 1 : kQuarter / 2;
     constexpr int NPIT = (kQuarter / 2 + 1 + T - 1) / T;
 #pragma unroll
@@ -249,26 +293,22 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
         const float2 dq = csub(zq, cconj(zb));
         const float2 wd = cmul(w, dq);
         // X[q] = (sq - i W^q dq) / 2
-        Xs[q] = make_float2(0.5f * (sq.x + wd.y), 0.5f * (sq.y - wd.x));
+        Xp[kp] = make_float2(0.5f * (sq.x + wd.y), 0.5f * (sq.y - wd.x));
         if (kq != kp || q == 0) {
             // X[L - q] = (conj(sq) + i conj(W^q) (-conj(dq))) / 2
             const float2 sb = cconj(sq);
             const float2 db = make_float2(-dq.x, dq.y);
             const float2 wdb = cmulc(db, w);
-            Xs[kHalf - q] = make_float2(0.5f * (sb.x - wdb.y), 0.5f * (sb.y + wdb.x));
+            Xp[kQuarter - h - kp] = make_float2(0.5f * (sb.x - wdb.y), 0.5f * (sb.y + wdb.x));
         }
     }
 }
 
-// F[q] from the colour planes, planes flagged in mask[q], fixed plane order.
+// F[q] from the colour planes flagged in the 4-bit mask mk, fixed plane order.
 // Planes 0 and 1 cover almost every bin, so they are loaded unconditionally
-// (in parallel with the mask) and selected; planes 2 and 3 are rare.
-__device__ __forceinline__ float2 plane_sum(const float2* __restrict__ Es,
-                                            const unsigned char* __restrict__ mask,
-                                            int q, int nplanes) {
-    const unsigned mk = __ldg(mask + q);
-    const float2 e0 = Es[q];
-    const float2 e1 = nplanes > 1 ? Es[kPlaneStride + q] : make_float2(0.f, 0.f);
+// (e0, e1, in parallel with the mask) and selected; planes 2 and 3 are rare.
+__device__ __forceinline__ float2 plane_pick(const float2* __restrict__ Es, unsigned mk, int q,
+                                             float2 e0, float2 e1) {
     float2 acc = make_float2(0.f, 0.f);
     if (mk & 1u) acc = cadd(acc, e0);
     if (mk & 2u) acc = cadd(acc, e1);
@@ -285,33 +325,54 @@ __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
     return make_float2(e.x - o.y, e.y + o.x);
 }
 
+// The two CTAs of a slice form a cluster.  Each rebuilds half of the quads
+// {n, L - n, Q + n, Q - n} (four bins in; u_0 and u_1 at n and Q - n out)
+// and writes the partner's half-spectrum values straight into the partner's
+// shared memory, so every plane value is loaded once.  After the inverse
+// stages the pair swaps halves of the result, so that each CTA stores a
+// contiguous half of y (z[2m] and z[2m + 1] side by side: whole sectors).
 template <bool SLICED>
-__global__ void __launch_bounds__(SpecCfg<kPI>::T, 1)
-spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restrict__ mask,
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SpecCfg<kPI>::T, 1)
+spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restrict__ qmask,
                     const SigMap out, const float2* __restrict__ ghi,
                     const float2* __restrict__ glo, const float2* __restrict__ gtw,
                     int nplanes) {
     constexpr int P = kPI, T = SpecCfg<P>::T, SH = shiftOf<P>();
     using C = SpecCfg<P>;
+    namespace cg = cooperative_groups;
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
     float2* hl = buf + padded<SH>(kQuarter);
     float2* tws = hl + 512;
-    const int h = blockIdx.x & 1;
+    cg::cluster_group cl = cg::this_cluster();
+    const int h = (int)cl.block_rank();
+    float2* peer = cl.map_shared_rank(buf, h ^ 1);
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
     load_tables<P>(hl, tws, ghi, glo, gtw);
-    __syncthreads();
+    cl.sync();   // tables staged, and the partner is running (its buffer may be written)
     const Tw64k tw{hl, hl + 256};
     const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
+    const bool two = nplanes > 1;
 
-    // quads {n, L - n, Q + n, Q - n}: four bins in, u_h[n] and u_h[Q - n] out
-    for (int n = t; n <= kQuarter / 2; n += T) {
-        const int m = (kQuarter - n) & (kQuarter - 1);
-        float2 fA = plane_sum(Es, mask, n, nplanes);
-        float2 fB = plane_sum(Es, mask, kHalf - n, nplanes);
-        const float2 fC = plane_sum(Es, mask, kQuarter + n, nplanes);
-        const float2 fD = plane_sum(Es, mask, kQuarter - n, nplanes);
+    // quads n in [0, Q/4) on CTA 0, [Q/4, Q/2] on CTA 1
+    const int nlo = h ? kQuarter / 4 : 0;
+    const int nhi = h ? kQuarter / 2 + 1 : kQuarter / 4;
+    float2* u0 = h ? peer : buf;   // receives u_0
+    float2* u1 = h ? buf : peer;   // receives u_1
+    for (int n = nlo + t; n < nhi; n += T) {
+        const int bA = n, bB = kHalf - n, bC = kQuarter + n, bD = kQuarter - n;
+        const unsigned qm = __ldg(qmask + n);
+        const float2 zero = make_float2(0.f, 0.f);
+        const float2 a0 = Es[bA], b0 = Es[bB], c0 = Es[bC], d0 = Es[bD];
+        const float2 a1 = two ? Es[kPlaneStride + bA] : zero;
+        const float2 b1 = two ? Es[kPlaneStride + bB] : zero;
+        const float2 c1 = two ? Es[kPlaneStride + bC] : zero;
+        const float2 d1 = two ? Es[kPlaneStride + bD] : zero;
+        float2 fA = plane_pick(Es, qm & 15u, bA, a0, a1);
+        float2 fB = plane_pick(Es, (qm >> 4) & 15u, bB, b0, b1);
+        const float2 fC = plane_pick(Es, (qm >> 8) & 15u, bC, c0, c1);
+        const float2 fD = plane_pick(Es, qm >> 12, bD, d0, d1);
         if (n == 0) {  // irfft ignores the imaginary parts of DC and Nyquist
             fA.y = 0.f;
             fB.y = 0.f;
@@ -320,36 +381,54 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
         // (W = W_65536, W^Q = -i): W^{Q+n} = -i W^n, W^{Q-n} = -i conj(W^n),
         // W^{2Q-n} = -conj(W^n), W^{2Q-2n} = -conj(W^2n)
         const float2 wn = tw(n);
-        const float2 w2n = h == 0 ? make_float2(1.f, 0.f) : tw(2 * n);
+        const float2 w2n = tw(2 * n);
         const float2 z0 = retangle(fA, fB, wn);
         const float2 z1 = retangle(fC, fD, make_float2(wn.y, -wn.x));
-        buf[PADI<SH>(n)] = h == 0 ? cadd(z0, z1) : cmulc(csub(z0, z1), w2n);
-        if (m != n) {
+        u0[PADI<SH>(n)] = cadd(z0, z1);
+        u1[PADI<SH>(n)] = cmulc(csub(z0, z1), w2n);
+        const int m = kQuarter - n;
+        if (m != n && m < kQuarter) {
             const float2 z2 = retangle(fD, fC, make_float2(-wn.y, -wn.x));
             const float2 z3 = retangle(fB, fA, make_float2(-wn.x, wn.y));
-            buf[PADI<SH>(m)] =
-                h == 0 ? cadd(z2, z3) : cmulc(csub(z2, z3), make_float2(-w2n.x, w2n.y));
+            u0[PADI<SH>(m)] = cadd(z2, z3);
+            u1[PADI<SH>(m)] = cmulc(csub(z2, z3), make_float2(-w2n.x, w2n.y));
         }
     }
-    __syncthreads();
+    cl.sync();   // both halves of u_h are in place
 
     float2 v[P];
     stage_load<kQuarter, T, C::R1, SH>(v, buf, t);
     __syncthreads();
     spec_compute<P, 1, +1>(v, t, tws);
+    spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+        stage_store<kQuarter, T, sR<P>(C::NST), sNS<P>(C::NST), SH>(w, buf, t);
+    });
+    cl.sync();   // z[2m + h] of both CTAs in shared memory
+
+    // CTA h writes y[4m .. 4m + 3] = (z[2m], z[2m + 1]) for m in its half
+    const float2* ze = h ? peer : buf;   // z[2m]
+    const float2* zo = h ? buf : peer;   // z[2m + 1]
     const float inv = 1.0f / (float)kHalf;
+    constexpr int kOut = kQuarter / 2;
     if constexpr (!SLICED) {
-        float2* ys = reinterpret_cast<float2*>(out.y + slice * kSlice);
-        spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-            constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
-#pragma unroll
-            for (int b = 0; b < P / R; ++b)
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int nn = t + T * b + NS * r;
-                    ys[2 * nn + h] = cscale(w[b * R + r], inv);
-                }
-        });
+        float* ys = out.y + slice * kSlice;
+        if ((reinterpret_cast<uintptr_t>(ys) & 15u) == 0) {
+            float4* y4 = reinterpret_cast<float4*>(ys);
+#pragma unroll 4
+            for (int i = t; i < kOut; i += T) {
+                const int m = h * kOut + i;
+                const float2 a = ze[PADI<SH>(m)], b = zo[PADI<SH>(m)];
+                y4[m] = make_float4(a.x * inv, a.y * inv, b.x * inv, b.y * inv);
+            }
+        } else {
+            float2* y2 = reinterpret_cast<float2*>(ys);
+#pragma unroll 4
+            for (int i = t; i < kOut; i += T) {
+                const int m = h * kOut + i;
+                y2[2 * m] = cscale(ze[PADI<SH>(m)], inv);
+                y2[2 * m + 1] = cscale(zo[PADI<SH>(m)], inv);
+            }
+        }
     } else {
         // un-roll by +-H and overlap-add into the zeroed output: every output
         // sample receives exactly two terms, and a + b == b + a, so the
@@ -362,25 +441,22 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned char* __restric
         const float* wnd = out.window;
         long long lo, hi;
         sample_range(out, lo, hi);
-        spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-            constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
+#pragma unroll 2
+        for (int i = t; i < kOut; i += T) {
+            const int m = h * kOut + i;
+            const float2 a = ze[PADI<SH>(m)], b = zo[PADI<SH>(m)];
+            const float val[4] = {a.x * inv, a.y * inv, b.x * inv, b.y * inv};
+            const int j0 = (4 * m + shift) & (kSlice - 1);   // 4 consecutive, no wrap
 #pragma unroll
-            for (int b = 0; b < P / R; ++b)
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int nn = t + T * b + NS * r;
-                    float2 val = cscale(w[b * R + r], inv);
-                    const int j = (2 * (2 * nn + h) + shift) & (kSlice - 1);
-                    if (wnd) {
-                        val.x *= __ldg(wnd + j);
-                        val.y *= __ldg(wnd + j + 1);
-                    }
-                    const long long p = p0 + j;
-                    if (p >= lo && p < hi) atomicAdd(yr + p, val.x);
-                    if (p + 1 >= lo && p + 1 < hi) atomicAdd(yr + p + 1, val.y);
-                }
-        });
+            for (int e = 0; e < 4; ++e) {
+                const int j = j0 + e;
+                const float vv = wnd ? val[e] * __ldg(wnd + j) : val[e];
+                const long long p = p0 + j;
+                if (p >= lo && p < hi) atomicAdd(yr + p, vv);
+            }
+        }
     }
+    cl.sync();   // the partner has finished reading this CTA's shared memory
 }
 
 }  // namespace
@@ -419,15 +495,37 @@ void spectrum_twiddle_rows(float2* out) {
     rows_for<16>(out + rowsOff(16));
 }
 
+#ifndef FCQT_SPEC_PREFETCH
+#define FCQT_SPEC_PREFETCH 1
+#endif
+
+namespace {
+// CTAs resident at once on the current device (one spectrum CTA per SM)
+int wave_ctas() {
+    if (!FCQT_SPEC_PREFETCH) return 0;
+    static int sms[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (sms[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return 0;
+        sms[dev] = n;
+    }
+    return sms[dev];
+}
+}  // namespace
+
 cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& st, int batch,
                                 cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
+    const int ahead = wave_ctas();
     if (in.S > 0)
         spectrum_fwd_kernel<true><<<2 * batch, SpecCfg<kPF>::T, smemOf<kPF>(), s>>>(
-            in, X, st.hi, st.lo, st.rows);
+            in, X, st.hi, st.lo, st.rows, ahead);
     else
         spectrum_fwd_kernel<false><<<2 * batch, SpecCfg<kPF>::T, smemOf<kPF>(), s>>>(
-            in, X, st.hi, st.lo, st.rows);
+            in, X, st.hi, st.lo, st.rows, ahead);
     return cudaGetLastError();
 }
 
@@ -436,10 +534,10 @@ cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap
     if (batch <= 0) return cudaSuccess;
     if (out.S > 0)
         spectrum_inv_kernel<true><<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
-            E, tab.mask, out, st.hi, st.lo, st.rows, tab.nplanes);
+            E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes);
     else
         spectrum_inv_kernel<false><<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
-            E, tab.mask, out, st.hi, st.lo, st.rows, tab.nplanes);
+            E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes);
     return cudaGetLastError();
 }
 

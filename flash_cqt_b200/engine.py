@@ -65,7 +65,9 @@ class Engine:
             raise TypeError(f"{name} must be float32, got {t.dtype}")
         if t.dim() != 2 or t.shape[-1] != N:
             raise ValueError(f"{name} must be [B, {N}], got {tuple(t.shape)}")
-        return t.contiguous()
+        t = t.contiguous()
+        # the engines move signals as float2 / float4 vectors
+        return t if t.data_ptr() % 16 == 0 else t.clone()
 
     def _coef(self, c, name):
         if not torch.is_tensor(c) or c.device != self.dev:

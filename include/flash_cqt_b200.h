@@ -23,7 +23,8 @@
  *   - Every pointer except the host tables of cqt_tables_upload is a device
  *     pointer on the device the tables were uploaded to; that device must be
  *     current when an entry point is called.
- *   - x, y, gx, gy: float32 [batch][65536].
+ *   - x, y, gx, gy: float32 [batch][65536], 8-byte aligned (CQT_ERR_ARG
+ *     otherwise; rows at 16-byte alignment take the vector store path).
  *   - coefficients: the heap of one slice is ncoef complex values (octave
  *     groups lowest first, then the DC and the Nyquist side block, each group
  *     [bins][M] row-major).  layout CQT_LAYOUT_PLANAR: c_re and c_im are two
