@@ -26,6 +26,8 @@
 // inter-stage twiddles sit in conflict-free shared rows, and one 256-thread
 // CTA processes 8192 points = 8192 / M (band, slice) instances of one block
 // length so small bands batch up.
+#include <cstdint>
+
 #include "engine.cuh"
 #include "internal.h"
 
@@ -201,6 +203,23 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
 }
 
+// TMA bulk copies (no multicast): shared -> global stores tracked by a bulk
+// group; the issuing thread waits only until shared memory has been read
+__device__ __forceinline__ bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, unsigned bytes) {
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(ssrc));
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n"
+                 ::"l"(gdst), "r"(sa), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit_wait_read() {
+    asm volatile("cp.async.bulk.commit_group;\ncp.async.bulk.wait_group.read 0;\n" ::: "memory");
+}
+
 // where an instance's M coefficients live: element n at
 // base + ((n + roll) mod M) -- the per-slice heap (roll 0) or the sliced
 // block layout (SliceLayout, roll +-M/4 on octave groups)
@@ -328,21 +347,47 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
 
     const CoefAddr ca = coef_addr<M, SLICED>(bp, in.slice, in.d);
     const bool interleaved = out.interleaved != 0;   // uniform: hoisted out of the stores
+    float2* og = reinterpret_cast<float2*>(out.re) + ca.base;
+    float* ore = out.re + ca.base;
+    float* oim = out.im + ca.base;
+    // the instance's M outputs are gathered in shared memory in destination
+    // order (roll applied) and leave as one TMA bulk store per array; a
+    // destination that is not 16-byte aligned takes per-element stores
+    const bool bulk = in.valid && (interleaved ? aligned16(og) : aligned16(ore) && aligned16(oim));
     band_rest<M, +1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
-        if (interleaved) {
-            float2* o = reinterpret_cast<float2*>(out.re) + ca.base;
+        if (bulk) {
+            if (interleaved) {
+#pragma unroll
+                for (int b = 0; b < kP / R; ++b)
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        const int nn = t + T * b + r * NS;
+                        buf[SLICED ? ((nn + ca.roll) & (M - 1)) : nn] = w[b * R + r];
+                    }
+            } else {
+                float* sre = reinterpret_cast<float*>(buf);
+                float* sim = sre + M;
+#pragma unroll
+                for (int b = 0; b < kP / R; ++b)
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        const int nn = t + T * b + r * NS;
+                        const int ix = SLICED ? ((nn + ca.roll) & (M - 1)) : nn;
+                        sre[ix] = w[b * R + r].x;
+                        sim[ix] = w[b * R + r].y;
+                    }
+            }
+        } else if (interleaved) {
 #pragma unroll
             for (int b = 0; b < kP / R; ++b)
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
                     const int nn = t + T * b + r * NS;
-                    o[SLICED ? ((nn + ca.roll) & (M - 1)) : nn] = w[b * R + r];
+                    og[SLICED ? ((nn + ca.roll) & (M - 1)) : nn] = w[b * R + r];
                 }
         } else {
-            float* ore = out.re + ca.base;
-            float* oim = out.im + ca.base;
 #pragma unroll
             for (int b = 0; b < kP / R; ++b)
 #pragma unroll
@@ -354,6 +399,19 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
                 }
         }
     });
+    // every thread's shared writes -> visible to the async proxy -> one
+    // thread per instance issues the copies (the barrier is CTA-uniform)
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (bulk && t == 0) {
+        if (interleaved) {
+            bulk_store(og, buf, M * 8);
+        } else {
+            bulk_store(ore, buf, M * 4);
+            bulk_store(oim, reinterpret_cast<float*>(buf) + M, M * 4);
+        }
+        bulk_commit_wait_read();   // shared memory stays live until read
+    }
 }
 
 template <int M, bool SLICED>

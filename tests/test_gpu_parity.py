@@ -149,6 +149,44 @@ def test_planar_and_interleaved_agree_bitwise(dev):
     assert [tuple(b.shape[1:]) for b in bl] == [(b, M) for b, M, _ in f.gspec]
 
 
+def _offset_view(shape, dtype, dev, elems):
+    """a contiguous view whose data pointer sits `elems` elements past an
+    allocation's (256-byte aligned) start"""
+    n = int(np.prod(shape))
+    return torch.empty(n + elems, dtype=dtype, device=dev)[elems:].view(*shape)
+
+
+def test_unaligned_buffers_agree_bitwise(eng, dev):
+    """buffers that are 8- (complex, signals) or 4-byte (planar) aligned take
+    the per-element copies instead of the TMA bulk / float4 ones: same bits"""
+    from flash_cqt_b200 import _native
+    B = 3
+    x = torch.from_numpy(np.stack([x_noise()[0]] * B)).to(dev)
+    a = eng.analysis(x)
+    c8 = _offset_view((B, eng.ncoef), torch.complex64, dev, 1)
+    assert c8.data_ptr() % 16 == 8
+    assert torch.equal(eng.analysis(x, out=c8), a)
+    kr = _offset_view((B, eng.ncoef), torch.float32, dev, 1)
+    ki = _offset_view((B, eng.ncoef), torch.float32, dev, 3)
+    eng.analysis_planar(x, kr, ki)
+    assert torch.equal(kr, a.real) and torch.equal(ki, a.imag)
+    y = eng.synthesis(a)
+    y8 = _offset_view((B, 65536), torch.float32, dev, 2)
+    assert torch.equal(eng.synthesis(c8, out=y8), y)
+    y16 = _offset_view((B, 65536), torch.float32, dev, 4)
+    assert torch.equal(eng.synthesis_planar(kr, ki, y16), y)
+    # a 4-byte aligned signal is refused at the C ABI
+    x4 = _offset_view((B, 65536), torch.float32, dev, 1)
+    x4.copy_(x)
+    ws = eng.workspace(B)
+    with pytest.raises(RuntimeError, match="aligned"):
+        eng.tables.call("cqt_analysis", x4.data_ptr(), a.data_ptr(), None,
+                        _native.CQT_LAYOUT_COMPLEX, B, ws.data_ptr(), ws.numel(),
+                        int(torch.cuda.current_stream(dev).cuda_stream))
+    # through the Python engine the same tensor is realigned, not refused
+    assert torch.equal(eng.analysis(x4), a)
+
+
 def test_deterministic(eng, dev):
     x = torch.from_numpy(x_noise()).to(dev)
     a1 = eng.analysis(x)
