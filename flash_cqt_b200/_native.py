@@ -71,6 +71,8 @@ def lib():
             vp, sz, ci = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
             L.cqt_version.restype = ci
             L.cqt_last_error.restype = ctypes.c_char_p
+            L.cqt_wait_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint)]
+            L.cqt_wait_timeouts.restype = ci
             L.cqt_tables_upload.argtypes = [ctypes.POINTER(HostTables), ci,
                                             ctypes.POINTER(vp)]
             L.cqt_tables_upload.restype = ci
@@ -114,7 +116,15 @@ def exported_symbols():
             "cqt_adj_analysis", "cqt_adj_synthesis", "cqt_launch_stage",
             "cqt_analysis_noalloc", "cqt_sliced_count", "cqt_sliced_analysis",
             "cqt_sliced_synthesis", "cqt_sliced_adj_analysis",
-            "cqt_sliced_adj_synthesis", "cqt_last_error", "cqt_version"]
+            "cqt_sliced_adj_synthesis", "cqt_wait_timeouts", "cqt_last_error",
+            "cqt_version"]
+
+
+def wait_timeouts():
+    """Bounded kernel waits that gave up on the current device (0 when healthy)."""
+    n = ctypes.c_uint(0)
+    _check(lib().cqt_wait_timeouts(ctypes.byref(n)), "cqt_wait_timeouts")
+    return int(n.value)
 
 
 def _check(rc, what):

@@ -220,6 +220,45 @@ __device__ __forceinline__ void bulk_commit_wait_read() {
     asm volatile("cp.async.bulk.commit_group;\ncp.async.bulk.wait_group.read 0;\n" ::: "memory");
 }
 
+// TMA bulk loads completing on an mbarrier.  Every wait is bounded: after
+// kMaxWaitSpins polls (each try_wait also suspends for a while) the wait
+// counts itself in g_wait_timeouts and returns, so a lost completion cannot
+// hang the GPU.
+constexpr int kMaxWaitSpins = 1 << 22;
+__device__ unsigned int g_wait_timeouts;
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+    return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* mbar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n"
+                 "fence.mbarrier_init.release.cluster;\n"
+                 ::"r"(smem_u32(mbar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect(unsigned long long* mbar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n"
+                 ::"r"(smem_u32(mbar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* sdst, const void* gsrc, unsigned bytes,
+                                          unsigned long long* mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1], %2, [%3];\n"
+                 ::"r"(smem_u32(sdst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_wait(unsigned long long* mbar, unsigned phase) {
+    const unsigned a = smem_u32(mbar);
+    for (int i = 0; i < kMaxWaitSpins; ++i) {
+        unsigned done;
+        asm volatile("{\n.reg .pred p;\n"
+                     "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                     "selp.u32 %0, 1, 0, p;\n}\n"
+                     : "=r"(done) : "r"(a), "r"(phase) : "memory");
+        if (done) return true;
+    }
+    atomicAdd(&g_wait_timeouts, 1u);
+    return false;
+}
+
 // where an instance's M coefficients live: element n at
 // base + ((n + roll) mod M) -- the per-slice heap (roll 0) or the sliced
 // block layout (SliceLayout, roll +-M/4 on octave groups)
@@ -416,40 +455,80 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
 
 template <int M, bool SLICED>
 __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandParams& bp, int c,
-                         float2* __restrict__ E, float2* smem, float2* tws) {
+                         float2* __restrict__ E, float2* smem, float2* tws,
+                         unsigned long long* mbar) {
     constexpr int T = M / kP;
     constexpr int R1 = Sched<M>::R1;
+    constexpr int IPC = kBandThreads / T;
     const Inst in = locate<M>(bp, c);
     const int t = in.t;
     float2* buf = smem + in.il * padded<kSH>(M);
     const int off = in.d.x;
     const CoefAddr ca = coef_addr<M, SLICED>(bp, in.slice, in.d);
 
-    // stage the instance's M coefficients into shared memory with
-    // asynchronous copies (coalesced, no registers held while in flight)
-    if (in.valid) {
-        if (in_c.interleaved) {
-            const float2* src = reinterpret_cast<const float2*>(in_c.re) + ca.base;
-#pragma unroll
-            for (int k = 0; k < kP; ++k) {
-                const int i = t + k * T;
-                cp_async8(buf + PADI<kSH>(i), src + (SLICED ? ((i + ca.roll) & (M - 1)) : i));
+    // stage the instance's M coefficients into shared memory, unpadded, in
+    // tap order (roll undone): interleaved as float2[M], planar as float[M]
+    // re then float[M] im.  One TMA bulk load per contiguous piece, issued by
+    // the instance's first thread; unaligned sources take per-element copies.
+    const bool interleaved = in_c.interleaved != 0;
+    const float2* src2 = reinterpret_cast<const float2*>(in_c.re) + ca.base;
+    const float* sre = in_c.re + ca.base;
+    const float* sim = in_c.im + ca.base;
+    const bool bulk = in.valid && (interleaved ? aligned16(src2) : aligned16(sre) && aligned16(sim));
+    float* bre = reinterpret_cast<float*>(buf);
+    float* bim = bre + M;
+    if (threadIdx.x == 0) mbar_init(mbar, IPC);
+    __syncthreads();
+    if (t == 0) {
+        mbar_arrive_expect(mbar, bulk ? M * 8 : 0);
+        if (bulk) {
+            // smem [0, M - r) <- src [r, M), smem [M - r, M) <- src [0, r)
+            const int r = SLICED ? (ca.roll & (M - 1)) : 0;
+            if (interleaved) {
+                bulk_load(buf, src2 + r, (M - r) * 8, mbar);
+                if (r) bulk_load(buf + (M - r), src2, r * 8, mbar);
+            } else {
+                bulk_load(bre, sre + r, (M - r) * 4, mbar);
+                bulk_load(bim, sim + r, (M - r) * 4, mbar);
+                if (r) {
+                    bulk_load(bre + (M - r), sre, r * 4, mbar);
+                    bulk_load(bim + (M - r), sim, r * 4, mbar);
+                }
             }
-        } else {
+        }
+    }
+    if (in.valid && !bulk) {
 #pragma unroll
-            for (int k = 0; k < kP; ++k) {
-                const int i = t + k * T;
-                const long long ix = ca.base + (SLICED ? ((i + ca.roll) & (M - 1)) : i);
-                cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)), in_c.re + ix);
-                cp_async4(reinterpret_cast<float*>(buf + PADI<kSH>(i)) + 1, in_c.im + ix);
+        for (int k = 0; k < kP; ++k) {
+            const int i = t + k * T;
+            const int ix = SLICED ? ((i + ca.roll) & (M - 1)) : i;
+            if (interleaved) {
+                cp_async8(buf + i, src2 + ix);
+            } else {
+                cp_async4(bre + i, sre + ix);
+                cp_async4(bim + i, sim + ix);
             }
         }
     }
     fill_twiddles<M>(tws, bp.tw2048);
     cp_async_wait_all();
+    mbar_wait(mbar, 0);
     __syncthreads();
     float2 v[kP];
-    stage_load<M, T, R1, kSH>(v, buf, t);
+    if (interleaved) {
+#pragma unroll
+        for (int b = 0; b < kP / R1; ++b)
+#pragma unroll
+            for (int r = 0; r < R1; ++r) v[b * R1 + r] = buf[t + T * b + r * (M / R1)];
+    } else {
+#pragma unroll
+        for (int b = 0; b < kP / R1; ++b)
+#pragma unroll
+            for (int r = 0; r < R1; ++r) {
+                const int i = t + T * b + r * (M / R1);
+                v[b * R1 + r] = make_float2(bre[i], bim[i]);
+            }
+    }
     if (!in.valid) {
 #pragma unroll
         for (int i = 0; i < kP; ++i) v[i] = make_float2(0.f, 0.f);
@@ -545,17 +624,18 @@ __global__ void __launch_bounds__(kBandThreads, kBandMinBlocks)
 bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ BandParams bp,
                  float2* __restrict__ E) {
     extern __shared__ float4 smem_raw[];
+    __shared__ unsigned long long mbar;
     float2* smem = reinterpret_cast<float2*>(smem_raw);
     float2* tws = smem + kBandData;
     const int c = find_class(bp.sc);
     switch (bp.sc.M[c]) {
-    case 2048: band_inv<2048, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
-    case 1024: band_inv<1024, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
-    case 512:  band_inv<512, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
-    case 256:  band_inv<256, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
-    case 128:  band_inv<128, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
-    case 64:   band_inv<64, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
-    case 32:   band_inv<32, SLICED>(in, tab, which, bp, c, E, smem, tws); break;
+    case 2048: band_inv<2048, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
+    case 1024: band_inv<1024, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
+    case 512:  band_inv<512, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
+    case 256:  band_inv<256, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
+    case 128:  band_inv<128, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
+    case 64:   band_inv<64, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
+    case 32:   band_inv<32, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
     default: break;
     }
 }
@@ -601,6 +681,10 @@ cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const Ban
     else
         bands_inv_kernel<false><<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E);
     return cudaGetLastError();
+}
+
+cudaError_t read_wait_timeouts(unsigned* count) {
+    return cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned));
 }
 
 cudaError_t init_band_attributes() {

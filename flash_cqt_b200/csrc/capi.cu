@@ -205,6 +205,13 @@ int cqt_version(void) { return 100; }
 
 const char* cqt_last_error(void) { return g_err.c_str(); }
 
+int cqt_wait_timeouts(unsigned int* count) {
+    if (!count) return fail(CQT_ERR_ARG, "null count");
+    *count = 0;
+    const cudaError_t e = read_wait_timeouts(count);
+    return e == cudaSuccess ? CQT_OK : cuda_fail(e, "reading the wait-timeout counter");
+}
+
 int32_t cqt_ncoef(const cqt_tables* t) { return t ? t->ncoef : -1; }
 
 size_t cqt_workspace_bytes(const cqt_tables* t, int batch) {

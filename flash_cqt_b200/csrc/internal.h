@@ -119,6 +119,7 @@ cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& s
                                 cudaStream_t s);
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
                                 const SpecTables& st, int batch, cudaStream_t s);
+cudaError_t read_wait_timeouts(unsigned* count);   // expired bounded waits (device)
 cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParams& bp,
                              CoefPtr out, cudaStream_t s);
 cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const BandParams& bp,

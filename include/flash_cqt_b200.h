@@ -207,6 +207,14 @@ int cqt_sliced_adj_synthesis(const cqt_tables* t, const cqt_signal* gy, const cq
                              float* gcoef, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* Diagnostic (no reference counterpart): the number of bounded waits in the
+ * kernels (TMA bulk-copy completions) that gave up on the current device since
+ * the library was loaded.  Every wait polls a fixed number of times and then
+ * counts itself here and lets the kernel finish instead of hanging; a nonzero
+ * count means results computed since then are not trustworthy.  Synchronous
+ * (reads device memory). */
+int cqt_wait_timeouts(unsigned int* count);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* cqt_last_error(void);
 

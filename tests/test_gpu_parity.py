@@ -360,3 +360,11 @@ def test_sliced_stream_matches_whole_buffer(dev):
     yw = sl.bwd(wb, ws)
     m = min(ys.shape[-1], yw.shape[-1])
     assert snr_db(_np(yw[..., :m]).astype(np.float64), _np(ys[..., :m])) >= RT_DB
+
+
+def test_no_bounded_wait_expired(eng, dev):
+    """every bounded wait on a TMA completion in the kernels run so far ended
+    by completion, not by its poll limit"""
+    from flash_cqt_b200._native import wait_timeouts
+    torch.cuda.synchronize()
+    assert wait_timeouts() == 0
