@@ -294,9 +294,11 @@ __device__ __forceinline__ int d_plane(int4 d, int which) { return (d.w >> (4 + 
 
 template <int M, bool SLICED>
 __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const BandParams& bp,
-                         int c, CoefPtr out, float2* smem, float2* tws) {
+                         int c, CoefPtr out, float2* smem, float2* tws,
+                         unsigned long long* mbar) {
     constexpr int T = M / kP;
     constexpr int R1 = Sched<M>::R1;
+    constexpr int IPC = kBandThreads / T;
     const Inst in = locate<M>(bp, c);
     const int t = in.t;
     float2* buf = smem + in.il * padded<kSH>(M);
@@ -304,8 +306,11 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     const int off = in.d.x;
     const bool side = d_side(in.d);
 
-    // stage the band's contiguous spectrum segment (<= M bins) into shared
-    // memory with asynchronous copies, independent of the gain loads
+    // stage the band's contiguous spectrum segment [lo, lo + n), n <= M,
+    // into shared memory with one TMA bulk load issued by the instance's
+    // first thread: bins [lo & ~1, (lo + n + 1) & ~1) (16-byte aligned ends;
+    // spectrum rows are 16-byte aligned and hold bins up to 32775), unpadded,
+    // so bin lo + i sits at buf[i + (lo & 1)]
     int lo = 0, n = 0;
     if (in.valid) {
         if (side) {
@@ -316,16 +321,14 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
             lo = in.d.y;
             n = d_lg(in.d);
         }
-        // fixed trip count (n <= M), predicated: no loop control
-        // X is parity-major; the thread stride T is even, so the parity of
-        // bin lo + t + k T is fixed and its slot advances by T / 2 per k
-        static_assert(T % 2 == 0, "band staging needs an even thread stride");
-        const float2* xsrc = Xs + xslot(lo + t);
-#pragma unroll
-        for (int k = 0; k < kP; ++k) {
-            const int i = t + k * T;
-            if (i < n) cp_async8(buf + PADI<kSH>(i), xsrc + k * (T / 2));
-        }
+    }
+    const int sh = lo & 1;
+    if (threadIdx.x == 0) mbar_init(mbar, IPC);
+    __syncthreads();
+    if (t == 0) {
+        const int a = lo - sh, bytes = n > 0 ? (((lo + n + 1) & ~1) - a) * 8 : 0;
+        mbar_arrive_expect(mbar, (unsigned)bytes);
+        if (bytes) bulk_load(buf, Xs + a, (unsigned)bytes, mbar);
     }
     fill_twiddles<M>(tws, bp.tw2048);
     // stage 1 taps: element r of butterfly b is tap t + T b + r M / R1.
@@ -354,16 +357,17 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
                 src[b * R1 + r] = sv < 0 ? -1 : (((sv & 0xFFFF) - lo) | (sv & 0x10000));
             }
     }
-    cp_async_wait_all();
+    mbar_wait(mbar, 0);
     __syncthreads();
     float2 v[kP];
+    const float2* seg = buf + sh;
     if (!side) {
 #pragma unroll
         for (int b = 0; b < kP / R1; ++b)
 #pragma unroll
             for (int r = 0; r < R1; ++r) {
                 const int i = (t + T * b + r * (M / R1) + l) & (M - 1);
-                v[b * R1 + r] = i < n ? cscale(buf[PADI<kSH>(i)], gain[b * R1 + r])
+                v[b * R1 + r] = i < n ? cscale(seg[i], gain[b * R1 + r])
                                       : make_float2(0.f, 0.f);
             }
     } else {
@@ -372,7 +376,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
             const int sv = src[i];
             float2 val = make_float2(0.f, 0.f);
             if (sv >= 0) {
-                float2 xv = buf[PADI<kSH>(sv & 0xFFFF)];
+                float2 xv = seg[sv & 0xFFFF];
                 if (sv & 0x10000) xv.y = -xv.y;
                 val = cscale(xv, gain[i]);
             }
@@ -604,17 +608,18 @@ __global__ void __launch_bounds__(kBandThreads, kBandMinBlocks)
 bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant__ BandParams bp,
                  CoefPtr out) {
     extern __shared__ float4 smem_raw[];
+    __shared__ unsigned long long mbar;
     float2* smem = reinterpret_cast<float2*>(smem_raw);
     float2* tws = smem + kBandData;
     const int c = find_class(bp.sc);
     switch (bp.sc.M[c]) {
-    case 2048: band_fwd<2048, SLICED>(X, tab, bp, c, out, smem, tws); break;
-    case 1024: band_fwd<1024, SLICED>(X, tab, bp, c, out, smem, tws); break;
-    case 512:  band_fwd<512, SLICED>(X, tab, bp, c, out, smem, tws); break;
-    case 256:  band_fwd<256, SLICED>(X, tab, bp, c, out, smem, tws); break;
-    case 128:  band_fwd<128, SLICED>(X, tab, bp, c, out, smem, tws); break;
-    case 64:   band_fwd<64, SLICED>(X, tab, bp, c, out, smem, tws); break;
-    case 32:   band_fwd<32, SLICED>(X, tab, bp, c, out, smem, tws); break;
+    case 2048: band_fwd<2048, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
+    case 1024: band_fwd<1024, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
+    case 512:  band_fwd<512, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
+    case 256:  band_fwd<256, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
+    case 128:  band_fwd<128, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
+    case 64:   band_fwd<64, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
+    case 32:   band_fwd<32, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
     default: break;
     }
 }

@@ -23,14 +23,6 @@ constexpr int kSlice = 65536;            // samples per slice
 constexpr int kHalf = kSlice / 2;        // packed complex length L
 constexpr int kQuarter = kHalf / 2;      // per-CTA sub-transform length
 constexpr int kPlaneStride = kHalf + 8;  // complex elements per spectrum row / colour plane
-// The half spectrum X is stored parity-major inside its row: even bins
-// 0..32768 at slots [0, 16385), odd bins 1..32767 from slot kOddX on.  Each
-// CTA of the forward engine produces one parity, so it writes whole sectors.
-constexpr int kOddX = kQuarter + 8;
-__host__ __device__ __forceinline__ constexpr int xslot(int bin) {
-    return (bin & 1) ? kOddX + (bin >> 1) : (bin >> 1);
-}
-static_assert(kOddX + kQuarter <= kPlaneStride, "parity-major X must fit in a row");
 constexpr int kMaxPlanes = 4;
 
 template <int SH = 5>

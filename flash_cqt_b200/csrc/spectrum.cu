@@ -274,10 +274,9 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     });
     __syncthreads();
 
-    // untangle the (q, L - q) pairs of this parity: X[q] = E + W_N^q O, into
-    // this parity's half of the (parity-major) spectrum row: bin q = 2 kp + h
-    // at slot kp, bin L - q at slot Q - h - kp
-    float2* Xp = X + slice * kPlaneStride + (h ? kOddX : 0);
+    // untangle the (q, L - q) pairs of this parity: X[q] = E + W_N^q O
+    // (natural bin order; the partner CTA writes the other parity)
+    float2* Xs = X + slice * kPlaneStride;
     const int npairs = h == 0 ? kQuarter / 2 + 1 : kQuarter / 2;
     constexpr int NPIT = (kQuarter / 2 + 1 + T - 1) / T;
 #pragma unroll
@@ -293,13 +292,13 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
         const float2 dq = csub(zq, cconj(zb));
         const float2 wd = cmul(w, dq);
         // X[q] = (sq - i W^q dq) / 2
-        Xp[kp] = make_float2(0.5f * (sq.x + wd.y), 0.5f * (sq.y - wd.x));
+        Xs[q] = make_float2(0.5f * (sq.x + wd.y), 0.5f * (sq.y - wd.x));
         if (kq != kp || q == 0) {
             // X[L - q] = (conj(sq) + i conj(W^q) (-conj(dq))) / 2
             const float2 sb = cconj(sq);
             const float2 db = make_float2(-dq.x, dq.y);
             const float2 wdb = cmulc(db, w);
-            Xp[kQuarter - h - kp] = make_float2(0.5f * (sb.x - wdb.y), 0.5f * (sb.y + wdb.x));
+            Xs[kHalf - q] = make_float2(0.5f * (sb.x - wdb.y), 0.5f * (sb.y + wdb.x));
         }
     }
 }
