@@ -359,19 +359,39 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     const int nhi = h ? kQuarter / 2 + 1 : kQuarter / 4;
     float2* u0 = h ? peer : buf;   // receives u_0
     float2* u1 = h ? buf : peer;   // receives u_1
-    for (int n = nlo + t; n < nhi; n += T) {
-        const int bA = n, bB = kHalf - n, bC = kQuarter + n, bD = kQuarter - n;
-        const unsigned qm = __ldg(qmask + n);
+    // software-pipelined by hand: the next quad's plane values are loaded
+    // before this quad's shared-memory stores (the compiler may not move
+    // global loads across stores through generic pointers)
+    struct QuadIn {
+        unsigned qm;
+        float2 a0, b0, c0, d0, a1, b1, c1, d1;
+    };
+    auto load_quad = [&](int n) {
+        QuadIn q;
         const float2 zero = make_float2(0.f, 0.f);
-        const float2 a0 = Es[bA], b0 = Es[bB], c0 = Es[bC], d0 = Es[bD];
-        const float2 a1 = two ? Es[kPlaneStride + bA] : zero;
-        const float2 b1 = two ? Es[kPlaneStride + bB] : zero;
-        const float2 c1 = two ? Es[kPlaneStride + bC] : zero;
-        const float2 d1 = two ? Es[kPlaneStride + bD] : zero;
-        float2 fA = plane_pick(Es, qm & 15u, bA, a0, a1);
-        float2 fB = plane_pick(Es, (qm >> 4) & 15u, bB, b0, b1);
-        const float2 fC = plane_pick(Es, (qm >> 8) & 15u, bC, c0, c1);
-        const float2 fD = plane_pick(Es, qm >> 12, bD, d0, d1);
+        q.qm = __ldg(qmask + n);
+        q.a0 = Es[n];
+        q.b0 = Es[kHalf - n];
+        q.c0 = Es[kQuarter + n];
+        q.d0 = Es[kQuarter - n];
+        q.a1 = two ? Es[kPlaneStride + n] : zero;
+        q.b1 = two ? Es[kPlaneStride + kHalf - n] : zero;
+        q.c1 = two ? Es[kPlaneStride + kQuarter + n] : zero;
+        q.d1 = two ? Es[kPlaneStride + kQuarter - n] : zero;
+        return q;
+    };
+    int n = nlo + t;
+    QuadIn cur;
+    if (n < nhi) cur = load_quad(n);
+    for (; n < nhi; n += T) {
+        QuadIn nxt;
+        if (n + T < nhi) nxt = load_quad(n + T);
+        const int bA = n, bB = kHalf - n, bC = kQuarter + n, bD = kQuarter - n;
+        const unsigned qm = cur.qm;
+        float2 fA = plane_pick(Es, qm & 15u, bA, cur.a0, cur.a1);
+        float2 fB = plane_pick(Es, (qm >> 4) & 15u, bB, cur.b0, cur.b1);
+        const float2 fC = plane_pick(Es, (qm >> 8) & 15u, bC, cur.c0, cur.c1);
+        const float2 fD = plane_pick(Es, qm >> 12, bD, cur.d0, cur.d1);
         if (n == 0) {  // irfft ignores the imaginary parts of DC and Nyquist
             fA.y = 0.f;
             fB.y = 0.f;
@@ -392,6 +412,7 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
             u0[PADI<SH>(m)] = cadd(z2, z3);
             u1[PADI<SH>(m)] = cmulc(csub(z2, z3), make_float2(-w2n.x, w2n.y));
         }
+        cur = nxt;
     }
     cl.sync();   // both halves of u_h are in place
 
