@@ -203,17 +203,33 @@ __device__ __forceinline__ SliceReader make_reader(const SigMap& m, long long g)
 __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
+// bulk L2 prefetch (TMA, no multicast) of a 16-byte aligned range, in 64 KB
+// pieces issued by threads 0, 1, ...; p and bytes multiples of 16
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, long long bytes, int t) {
+    constexpr long long kPiece = 65536;
+    const long long at = (long long)t * kPiece;
+    if (at < bytes) {
+        const long long n = bytes - at < kPiece ? bytes - at : kPiece;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                         static_cast<const char*>(p) + at), "r"((unsigned)n) : "memory");
+    }
+}
 
-// Each spectrum CTA holds a whole SM (one CTA per SM), so its load phase and
-// its shared-memory stages cannot overlap another CTA's.  Instead, on entry it
-// prefetches into L2 the input of the CTA one wave ahead (`ahead` = the number
-// of resident CTAs), which that CTA then reads at L2 speed.  Only addresses
+// Each spectrum CTA holds a whole SM (one CTA per SM), and the CTAs of a wave
+// move in step: all load, then all compute while HBM idles.  So once a CTA
+// has its own input it prefetches into L2 the input of the CTA one wave
+// ahead (`ahead` = the number of resident CTAs), overlapping that HBM traffic
+// with its compute; the next wave then loads at L2 speed.  Only addresses
 // inside the readable ranges are touched.
 template <bool SLICED, int T>
 __device__ __forceinline__ void prefetch_signal_half(const SigMap& m, long g, int half, int t) {
     if constexpr (!SLICED) {
         const float* base = m.x + g * kSlice + half * (kSlice / 2);
-        for (int i = t; i < kSlice / 2 / 32; i += T) prefetch_l2(base + 32 * i);
+        if ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+            prefetch_l2_bulk(base, kSlice / 2 * 4, t);
+        } else {   // 8-byte aligned signal: per-line prefetches
+            for (int i = t; i < kSlice / 2 / 32; i += T) prefetch_l2(base + 32 * i);
+        }
     } else {
         const long long row = g / m.S;
         const int sg = m.slice0 + (int)(g % m.S);
@@ -248,10 +264,6 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     const int h = blockIdx.x & 1;
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
-    if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
-        const long nb = blockIdx.x + (long)ahead;
-        prefetch_signal_half<SLICED, T>(in, nb >> 1, (int)(nb & 1), t);
-    }
     load_tables<P>(hl, tws, ghi, glo, gtw);
     __syncthreads();
     const Tw64k tw{hl, hl + 256};
@@ -268,7 +280,11 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
             const float2 c = z(n + kQuarter);
             v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
         }
-    spec_compute<P, 1, -1>(v, t, tws);
+    spec_compute<P, 1, -1>(v, t, tws);   // consumes the loads
+    if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
+        const long nb = blockIdx.x + (long)ahead;
+        prefetch_signal_half<SLICED, T>(in, nb >> 1, (int)(nb & 1), t);
+    }
     spec_stages<P, 2, -1>(v, buf, tws, t, [&](float2 (&w)[P]) {
         stage_store<kQuarter, T, sR<P>(C::NST), sNS<P>(C::NST), SH>(w, buf, t);
     });
@@ -335,7 +351,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SpecCfg<kPI>::T, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restrict__ qmask,
                     const SigMap out, const float2* __restrict__ ghi,
                     const float2* __restrict__ glo, const float2* __restrict__ gtw,
-                    int nplanes) {
+                    int nplanes, int ahead) {
     constexpr int P = kPI, T = SpecCfg<P>::T, SH = shiftOf<P>();
     using C = SpecCfg<P>;
     namespace cg = cooperative_groups;
@@ -413,6 +429,16 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
             u1[PADI<SH>(m)] = cmulc(csub(z2, z3), make_float2(-w2n.x, w2n.y));
         }
         cur = nxt;
+    }
+    if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
+        // planes 0 and 1 (read unconditionally) of the slice one wave ahead:
+        // CTA h of that pair prefetches plane h (rows are 16-byte aligned)
+        const long nb = blockIdx.x + (long)ahead;
+        const int pl = (int)(nb & 1);
+        if (pl < nplanes)
+            prefetch_l2_bulk(E + (nb >> 1) * (long)(nplanes * kPlaneStride) +
+                                 (long)pl * kPlaneStride,
+                             (long long)kPlaneStride * 8, t);
     }
     cl.sync();   // both halves of u_h are in place
 
@@ -552,12 +578,13 @@ cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& s
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
                                 const SpecTables& st, int batch, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
+    const int ahead = wave_ctas();
     if (out.S > 0)
         spectrum_inv_kernel<true><<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
-            E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes);
+            E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
     else
         spectrum_inv_kernel<false><<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
-            E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes);
+            E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
     return cudaGetLastError();
 }
 
