@@ -30,28 +30,43 @@ from .oct_cqt import OctCQT
 
 
 class _SlicedAnalysis(torch.autograd.Function):
+    """x2 [rows, count] holds global samples [sample0, sample0 + count) of
+    signals of global length `length`; -> coefficients of slices
+    [slice0, slice0 + S)"""
+
     @staticmethod
-    def forward(ctx, x2, se, S):
-        ctx.se, ctx.rows, ctx.L, ctx.S = se, x2.shape[0], x2.shape[1], S
-        return se.analysis(x2, S)
+    def forward(ctx, x2, se, S, slice0=0, sample0=0, length=None):
+        length = sample0 + x2.shape[1] if length is None else length
+        ctx.se, ctx.rows, ctx.count, ctx.S = se, x2.shape[0], x2.shape[1], S
+        ctx.map = (slice0, sample0, length)
+        return se.analysis(x2, S, slice0=slice0, sample0=sample0, length=length)
 
     @staticmethod
     def backward(ctx, g):
-        gx = ctx.se.synthesis(g.contiguous(), ctx.rows, ctx.S, ctx.L,
-                              adjoint_of_analysis=True)
-        return gx, None, None
+        slice0, sample0, length = ctx.map
+        gx = ctx.se.synthesis(g.contiguous(), ctx.rows, ctx.S, length,
+                              adjoint_of_analysis=True, slice0=slice0,
+                              sample0=sample0, count=ctx.count)
+        return gx, None, None, None, None, None
 
 
 class _SlicedSynthesis(torch.autograd.Function):
+    """coefficients of slices [slice0, slice0 + S) -> overlap-added output
+    holding global samples [sample0, sample0 + count)"""
+
     @staticmethod
-    def forward(ctx, buf, se, rows, S, length):
+    def forward(ctx, buf, se, rows, S, length, slice0=0, sample0=0, count=None):
         ctx.se, ctx.S = se, S
-        return se.synthesis(buf, rows, S, length)
+        ctx.map = (slice0, sample0, length)
+        return se.synthesis(buf, rows, S, length, slice0=slice0, sample0=sample0,
+                            count=count)
 
     @staticmethod
     def backward(ctx, gy):
-        g = ctx.se.analysis(gy.contiguous(), ctx.S, adjoint_of_synthesis=True)
-        return g, None, None, None, None
+        slice0, sample0, length = ctx.map
+        g = ctx.se.analysis(gy.contiguous(), ctx.S, adjoint_of_synthesis=True,
+                            slice0=slice0, sample0=sample0, length=length)
+        return g, None, None, None, None, None, None, None
 
 
 def makewnd(sl_len, tr_area, device="cpu", dtype=torch.float32):
@@ -213,40 +228,81 @@ class SlicedCQT:
         return out if length is None else out[..., :length]
 
     # streaming API, state of one half slice (sliced.py:171-209)
+    #
+    # With the default engine the state stays on the device: stream_fwd keeps
+    # the previous hop in a [rows, 2 hops] window buffer and runs the fused
+    # sliced analysis on that window as global slice k (global samples
+    # [hop (k - 1), hop (k + 1)), the +-H / +-M/4 rolls by the parity of k);
+    # stream_bwd runs the fused synthesis of slice k into a [rows, 2 hops]
+    # buffer and adds the tail kept from slice k - 1.  Coefficients and output
+    # are bit-identical to the whole-buffer fwd / bwd (each output sample is
+    # the same sum of two terms).
     def stream_fwd(self, chunks):
         """chunks yields [B, C, hop] pieces (pad the last one); yields one
         (blocks, side) per slice, blocks[i] [B, C, oct_bins[i], M_i]"""
         prev = None
+        win = None
         k = 0
+        hop = self.hop
 
-        def one(prev, chunk, k):
+        def one_generic(prev, chunk, k):
             sl = torch.cat([prev, chunk], dim=-1) * self.tw
             sl = torch.roll(sl, -self.H if k % 2 == 0 else self.H, -1)
             blocks, side = self.cqt.fwd(sl.unsqueeze(2))
             blocks = self._arrange(blocks, 1, fwd=(k % 2 == 0))
             return [c[:, :, 0] for c in blocks], [c[:, :, 0] for c in side]
 
+        def one_fused(se, win, lead, k):
+            buf = _SlicedAnalysis.apply(win, se, 1, k, hop * (k - 1), hop * (k + 1))
+            blocks, side = se.group_views(buf, lead, 1)
+            return blocks, [c[:, :, 0] for c in side]
+
+        se = None
         for chunk in chunks:
             if prev is None:
                 prev = torch.zeros_like(chunk)
-            yield one(prev, chunk, k)
+                se = self._fused(chunk.device) if chunk.shape[-1] == hop else None
+            if se is None:
+                yield one_generic(prev, chunk, k)
+            else:
+                B, C, _ = chunk.shape
+                if win is None or chunk.requires_grad:   # fresh buffer under autograd
+                    win = chunk.new_zeros(B * C, 2 * hop)
+                win[:, :hop] = prev.reshape(B * C, hop)
+                win[:, hop:] = chunk.reshape(B * C, hop)
+                yield one_fused(se, win, (B, C), k)
             prev = chunk
             k += 1
         if prev is not None:
-            yield one(prev, torch.zeros_like(prev), k)
+            if se is None:
+                yield one_generic(prev, torch.zeros_like(prev), k)
+            else:
+                B, C, _ = prev.shape
+                win = prev.new_zeros(B * C, 2 * hop)
+                win[:, :hop] = prev.reshape(B * C, hop)
+                yield one_fused(se, win, (B, C), k)
 
     def stream_bwd(self, slice_coeffs):
         """slice_coeffs yields (blocks, side) per slice as stream_fwd emits;
         yields [B, C, hop] output pieces, one slice behind the input"""
         tail = None
         k = 0
+        hop = self.hop
         for blocks, side in slice_coeffs:
-            blocks = [c.unsqueeze(2) for c in blocks]
-            side = [c.unsqueeze(2) for c in side] if side is not None else None
-            blocks = self._arrange(blocks, 1, fwd=not (k % 2 == 0))
-            y = self.cqt.bwd(blocks, side)[:, :, 0]
-            y = torch.roll(y, self.H if k % 2 == 0 else -self.H, -1)
+            B, C = blocks[0].shape[:2]
+            se = self._fused(blocks[0].device)
+            if se is not None and blocks[0].shape[-1] == self.size_per_oct[0]:
+                sd = [c.unsqueeze(2) for c in side] if side is not None else None
+                buf = self._fused_buffer(se, blocks, sd, B * C, 1)
+                y = _SlicedSynthesis.apply(buf, se, B * C, 1, hop * (k + 1), k,
+                                           hop * (k - 1), 2 * hop).view(B, C, 2 * hop)
+            else:
+                blocks = [c.unsqueeze(2) for c in blocks]
+                side = [c.unsqueeze(2) for c in side] if side is not None else None
+                blocks = self._arrange(blocks, 1, fwd=not (k % 2 == 0))
+                y = self.cqt.bwd(blocks, side)[:, :, 0]
+                y = torch.roll(y, self.H if k % 2 == 0 else -self.H, -1)
             if tail is not None:
-                yield tail + y[..., :self.hop]
-            tail = y[..., self.hop:]
+                yield tail + y[..., :hop]
+            tail = y[..., hop:]
             k += 1
