@@ -34,7 +34,9 @@ struct BandSched {         // CTA ranges of the block-length classes for one lau
     float inv_batch;           // 1 / batch, for the instance -> (band, slice) split
 };
 
-constexpr int kMaxBands = 160;
+// band descriptors travel in the kernel parameters (8 KB at 512 bands; the
+// limit for kernel parameters is 32,764 bytes)
+constexpr int kMaxBands = 512;
 constexpr int kMaxGroups = 16;
 
 // Coefficient layout of the sliced transform: one interleaved complex buffer

@@ -143,7 +143,11 @@ def build_tables(heap):
                        gim[s].astype(np.float32), maskp, nplanes)
     t["nplanes"] = max(v[4] for v in t["inv"].values())
 
-    # per band geometry for the closed-form octave path: lo, l, Lg, flags
+    # per band geometry for the closed-form octave path: lo, l, Lg, flags.
+    # A band takes the closed form only where it reproduces every per-tap
+    # table entry exactly; the DC / Nyquist side bands, and octave bands that
+    # touch an edge bin or a mirrored (conjugated) bin, take the table path
+    # (flags bit 0).
     geom = np.zeros((len(heap.bands), 4), np.int32)
     nocts = sum(g[0].shape[0] for g in heap.groups)
     for i, (M, o) in enumerate(heap.bands):
@@ -152,14 +156,8 @@ def build_tables(heap):
             continue
         rg = bank.ranges[i + 1]                 # octave bands are windows 1..nb
         lg = rg.size
-        flags = 0
-        for w, s in enumerate(INV_SETS):
-            d = t["inv"][s][0][o:o + M]
-            planes = np.unique(d[d >= 0] // PLANE_STRIDE)
-            if planes.size != 1:
-                raise RuntimeError("octave band %d spans several colour planes" % i)
-            flags |= int(planes[0]) << (4 + 4 * w)
-        geom[i] = (int(rg[0]), lg // 2, lg, flags)
+        g = _octave_geometry(t, o, M, int(rg[0]), lg // 2, lg)
+        geom[i] = g if g is not None else (0, 0, 0, 1)
     t["band_geom"] = geom
     # coefficient groups in heap order (octave groups roll in the sliced
     # layout, the DC and Nyquist side groups do not)
@@ -189,6 +187,33 @@ def build_tables(heap):
     t["tw_hi"] = _cplx32(np.exp(-2j * math.pi * (256 * e) / 65536))
     t["tw_lo"] = _cplx32(np.exp(-2j * math.pi * e / 65536))
     return t
+
+
+def _octave_geometry(t, o, M, lo, l, lg):
+    """(lo, l, Lg, flags) when tap m of the band at heap offset o maps to bin
+    lo + ((m + l) mod M) inside the window support (live iff that index is
+    below Lg) in every gather and scatter table, with one colour plane per
+    inverse set and equal real / imaginary scatter gains; else None"""
+    m = np.arange(M)
+    ii = (m + l) % M
+    live = ii < lg
+    bins = lo + ii
+    for src, gain in t["fwd"].values():
+        s_, g_ = src[o:o + M], gain[o:o + M]
+        ok = np.where(s_ >= 0, live & (s_ == bins), g_ == 0)
+        if not ok.all():
+            return None
+    flags = 0
+    for w, s in enumerate(INV_SETS):
+        dest, gr, gi = (a[o:o + M] for a in t["inv"][s][:3])
+        writes = live & (gr != 0)
+        if ((dest >= 0) != writes).any() or (gi[writes] != gr[writes]).any():
+            return None
+        planes = np.unique(dest[writes] // PLANE_STRIDE)
+        if planes.size != 1 or (dest[writes] % PLANE_STRIDE != bins[writes]).any():
+            return None
+        flags |= int(planes[0]) << (4 + 4 * w)
+    return (lo, l, lg, flags)
 
 
 def _cplx32(z):

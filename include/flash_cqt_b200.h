@@ -62,7 +62,7 @@ extern "C" {
 /* Host-side tables, built once per filterbank (the Python side builds them in
  * float64 and rounds once).  Per-tap arrays have ncoef entries in heap order. */
 typedef struct cqt_host_tables {
-    int32_t nbands;
+    int32_t nbands;             /* <= 512 */
     int32_t ncoef;
     const int32_t* band_off;    /* [nbands] heap offset of each band */
     const int32_t* band_list;   /* [nbands] band ids grouped by class */

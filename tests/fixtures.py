@@ -7,6 +7,7 @@ import numpy as np
 from signals import chirp, normal, sinusoids  # noqa: F401
 
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "reference_fixtures.npz"
+GOLDEN_ALT = pathlib.Path(__file__).resolve().parent / "golden" / "reference_fixtures_alt.npz"
 STRIDE = 13
 STRIDE_SLICED = 41
 N = 65536
@@ -22,6 +23,29 @@ def ref():
 def oracle():
     from oracle.cqt_oracle import OctCQTOracle
     return OctCQTOracle()
+
+
+# other filterbanks (band lengths 32..2048), as in tests/golden/make_golden.py
+ALT_CONFIGS = [([4, 4, 1], [8, 16, 32]), ([2, 2, 2, 3], [8, 12, 16, 32]),
+               ([3, 4, 2], [8, 64, 64])]
+STRIDE_ALT = 37
+
+
+@functools.lru_cache(maxsize=1)
+def ref_alt():
+    with np.load(GOLDEN_ALT) as f:
+        return {k: f[k] for k in f.files}
+
+
+@functools.lru_cache(maxsize=4)
+def oracle_alt(i):
+    from oracle.cqt_oracle import OctCQTOracle
+    no, bpo = ALT_CONFIGS[i]
+    return OctCQTOracle(no, bpo)
+
+
+def x_alt():
+    return normal(21, (2, N))
 
 
 def x_noise():

@@ -2,7 +2,8 @@
 
 Run once, in a container where the reference checkout is mounted read-only::
 
-    python tests/golden/make_golden.py /path/to/Flash-CQT
+    python tests/golden/make_golden.py /path/to/Flash-CQT          # default bank
+    python tests/golden/make_golden.py /path/to/Flash-CQT --alt    # other banks
 
 It imports the reference package (``flash_cqt``) and runs its own public API
 (``OctCQT.fwd/bwd``, torch autograd through them, ``SlicedCQT.fwd/bwd``) on
@@ -142,7 +143,50 @@ def main(ref_root):
     print("round trip (noise)", out["rt_noise_db"], "sliced", out["sliced_rt_db"])
 
 
+# Filterbanks other than the default, all with band lengths 32..2048 (the
+# range of the reference's fused kernels, radix_impl.cuh:435-441): one inside
+# the default's band count, two above it.
+ALT_CONFIGS = [([4, 4, 1], [8, 16, 32]), ([2, 2, 2, 3], [8, 12, 16, 32]),
+               ([3, 4, 2], [8, 64, 64])]
+STRIDE_ALT = 37
+
+
+def main_alt(ref_root):
+    """reference_fixtures_alt.npz: per alternative filterbank, the layout
+    checksums, strided coefficient samples and the round trip of two N(0,1)
+    slices through the reference OctCQT"""
+    sys.path.insert(0, str(ref_root))
+    import torch
+    from flash_cqt import OctCQT
+
+    torch.set_num_threads(8)
+    N = 65536
+    out = {}
+    x = normal(21, (2, N))
+    xt = torch.from_numpy(x)
+    for i, (no, bpo) in enumerate(ALT_CONFIGS):
+        cqt = OctCQT(no, bpo, fs=44100, audio_len=N)
+        groups = list(cqt.groups) + list(cqt.side_groups)
+        lay = []
+        for idx, gv, pos, gdv, conj in groups:
+            b, M = idx.shape
+            w = torch.arange(1, b * M + 1, dtype=torch.int64)
+            lay.append([b, M, int(idx.reshape(-1).sum()), int((idx.reshape(-1) * w).sum()),
+                        int(pos.reshape(-1).sum()), int(conj.sum()), int((gv != 0).sum())])
+        blocks, side = cqt.fwd(xt)
+        h = torch.cat([c.reshape(2, -1) for c in list(blocks) + list(side)], -1)
+        y = cqt.bwd(blocks, side)
+        out[f"alt{i}_layout"] = np.array(lay, dtype=np.int64)
+        out[f"alt{i}_coef_s"] = h.reshape(-1)[::STRIDE_ALT].numpy()
+        out[f"alt{i}_y_s"] = y.reshape(-1)[::STRIDE_ALT].numpy()
+        print(no, bpo, "bands", sum(g[0].shape[0] for g in groups), "ncoef", h.shape[1])
+    np.savez_compressed(HERE / "reference_fixtures_alt.npz", **out)
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: make_golden.py <reference checkout>")
-    main(pathlib.Path(sys.argv[1]))
+    if len(sys.argv) not in (2, 3) or (len(sys.argv) == 3 and sys.argv[2] != "--alt"):
+        raise SystemExit("usage: make_golden.py <reference checkout> [--alt]")
+    if len(sys.argv) == 3:
+        main_alt(pathlib.Path(sys.argv[1]))
+    else:
+        main(pathlib.Path(sys.argv[1]))

@@ -64,13 +64,16 @@ def test_engine_refuses_cpu():
             cqt.fwd(torch.zeros(1, 65536))
 
 
-def test_valid_tables_pass_host_validation():
+@pytest.mark.parametrize("bank", [([3, 4, 2], [8, 16, 32]), ([4, 4, 1], [8, 16, 32]),
+                                  ([2, 2, 2, 3], [8, 12, 16, 32]), ([3, 4, 2], [8, 64, 64])])
+def test_valid_tables_pass_host_validation(bank):
     """Without a GPU the upload gets past every host-side check and fails only
     at the first CUDA call, so the product tables satisfy the ABI contract
-    (closed-form octave geometry == per-tap tables, every index in range)."""
+    (closed-form octave geometry == per-tap tables, every index in range),
+    for the default bank and for banks of 130, 170 and 410 bands."""
     if torch.cuda.is_available():
         pytest.skip("covered by the GPU tests when a device is present")
-    tabs = build_tables(HeapLayout(Filterbank([3, 4, 2], [8, 16, 32], 44100, 65536)))
+    tabs = build_tables(HeapLayout(Filterbank(bank[0], bank[1], 44100, 65536)))
     with pytest.raises(RuntimeError, match=r"cqt_tables_upload failed \(-2\)"):
         _native.DeviceTables(tabs, 0)
 

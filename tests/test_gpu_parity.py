@@ -399,6 +399,33 @@ def test_sliced_stream_gradient(dev):
     assert snr_db(_np(grads[1]).astype(np.float64), _np(grads[0])) >= GRAD_DB
 
 
+@pytest.mark.parametrize("i", range(3))
+def test_other_filterbanks(dev, i):
+    """banks of 130, 170 and 410 bands (band lengths 32..2048): analysis and
+    round trip against the oracle and the reference's fixtures, both
+    transposes against the oracle"""
+    from fixtures import ALT_CONFIGS, STRIDE_ALT, oracle_alt, ref_alt, x_alt
+    from flash_cqt_b200.engine import Engine
+    no, bpo = ALT_CONFIGS[i]
+    e = Engine.from_params(no, bpo, 44100, 65536, dev)
+    o, r = oracle_alt(i), ref_alt()
+    x = x_alt()
+    h = e.analysis(torch.from_numpy(x).float().to(dev))
+    want = o.heap(o.fwd(x))
+    assert snr_db(want, _np(h)) >= COEF_DB
+    assert snr_db(r[f"alt{i}_coef_s"], _np(h).reshape(-1)[::STRIDE_ALT]) >= COEF_DB
+    y = e.synthesis(h)
+    assert snr_db(x, _np(y)) >= RT_DB
+    assert snr_db(r[f"alt{i}_y_s"], _np(y).reshape(-1)[::STRIDE_ALT]) >= RT_DB
+    g = np.random.default_rng(i).standard_normal((2, 2, e.ncoef))
+    gc = (g[0] + 1j * g[1]).astype(np.complex64)
+    gx = e.adj_analysis(torch.from_numpy(gc).to(dev))
+    assert snr_db(o.adj_fwd(o.unheap(gc.astype(np.complex128))), _np(gx)) >= GRAD_DB
+    gy = np.random.default_rng(10 + i).standard_normal((2, 65536))
+    gk = e.adj_synthesis(torch.from_numpy(gy).float().to(dev))
+    assert snr_db(o.heap(o.adj_bwd(gy)), _np(gk)) >= GRAD_DB
+
+
 def test_no_bounded_wait_expired(eng, dev):
     """every bounded wait on a TMA completion in the kernels run so far ended
     by completion, not by its poll limit"""

@@ -7,8 +7,9 @@ float64, so agreement is bounded by float32 rounding (~130 dB).
 import numpy as np
 import pytest
 
-from fixtures import (STRIDE, STRIDE_SLICED, chirp, gc_seed, gy_seed, oracle,
-                      ref, sinusoids, x_noise)
+from fixtures import (ALT_CONFIGS, STRIDE, STRIDE_ALT, STRIDE_SLICED, chirp,
+                      gc_seed, gy_seed, oracle, oracle_alt, ref, ref_alt, sinusoids,
+                      x_alt, x_noise)
 from oracle.cqt_oracle import SlicedOracle, snr_db
 
 
@@ -104,3 +105,22 @@ def test_sliced_matches_reference(L):
     assert snr_db(r["sliced_y_s"], y.reshape(-1)[::STRIDE_SLICED]) > 125
     assert snr_db(x, y) > 200
     np.testing.assert_allclose(so.tw[::64], r["tukey"], atol=1e-7)
+
+
+@pytest.mark.parametrize("i", range(len(ALT_CONFIGS)))
+def test_other_filterbanks_match_reference(i):
+    """layout checksums exact, coefficients and round trip against the
+    reference on three other banks (130, 170 and 410 bands)"""
+    o, r = oracle_alt(i), ref_alt()
+    lay = []
+    for idx, gv, pos, gdv, conj in o.all_groups:
+        b, M = idx.shape
+        w = np.arange(1, b * M + 1, dtype=np.int64)
+        lay.append([b, M, idx.sum(), (idx.reshape(-1) * w).sum(), pos.sum(), conj.sum(),
+                    (gv != 0).sum()])
+    np.testing.assert_array_equal(np.array(lay, dtype=np.int64), r[f"alt{i}_layout"])
+    x = x_alt()
+    h = o.heap(o.fwd(x))
+    assert snr_db(r[f"alt{i}_coef_s"], h.reshape(-1)[::STRIDE_ALT]) >= 120
+    y = o.bwd(o.fwd(x))
+    assert snr_db(r[f"alt{i}_y_s"], y.reshape(-1)[::STRIDE_ALT]) >= 125
