@@ -343,9 +343,9 @@ __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
 // The two CTAs of a slice form a cluster.  Each rebuilds half of the quads
 // {n, L - n, Q + n, Q - n} (four bins in; u_0 and u_1 at n and Q - n out)
 // and writes the partner's half-spectrum values straight into the partner's
-// shared memory, so every plane value is loaded once.  After the inverse
-// stages the pair swaps halves of the result, so that each CTA stores a
-// contiguous half of y (z[2m] and z[2m + 1] side by side: whole sectors).
+// shared memory, so every plane value is loaded once.  After that exchange
+// the CTAs work alone: CTA h stores z[2m + h] into y (swapping halves through
+// distributed shared memory for whole-sector stores measured slower).
 template <bool SLICED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SpecCfg<kPI>::T, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restrict__ qmask,
@@ -446,35 +446,20 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     stage_load<kQuarter, T, C::R1, SH>(v, buf, t);
     __syncthreads();
     spec_compute<P, 1, +1>(v, t, tws);
-    spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-        stage_store<kQuarter, T, sR<P>(C::NST), sNS<P>(C::NST), SH>(w, buf, t);
-    });
-    cl.sync();   // z[2m + h] of both CTAs in shared memory
-
-    // CTA h writes y[4m .. 4m + 3] = (z[2m], z[2m + 1]) for m in its half
-    const float2* ze = h ? peer : buf;   // z[2m]
-    const float2* zo = h ? buf : peer;   // z[2m + 1]
     const float inv = 1.0f / (float)kHalf;
-    constexpr int kOut = kQuarter / 2;
     if constexpr (!SLICED) {
-        float* ys = out.y + slice * kSlice;
-        if ((reinterpret_cast<uintptr_t>(ys) & 15u) == 0) {
-            float4* y4 = reinterpret_cast<float4*>(ys);
-#pragma unroll 4
-            for (int i = t; i < kOut; i += T) {
-                const int m = h * kOut + i;
-                const float2 a = ze[PADI<SH>(m)], b = zo[PADI<SH>(m)];
-                y4[m] = make_float4(a.x * inv, a.y * inv, b.x * inv, b.y * inv);
-            }
-        } else {
-            float2* y2 = reinterpret_cast<float2*>(ys);
-#pragma unroll 4
-            for (int i = t; i < kOut; i += T) {
-                const int m = h * kOut + i;
-                y2[2 * m] = cscale(ze[PADI<SH>(m)], inv);
-                y2[2 * m + 1] = cscale(zo[PADI<SH>(m)], inv);
-            }
-        }
+        // z[2m + h] -> samples 4m + 2h, 4m + 2h + 1
+        float2* ys = reinterpret_cast<float2*>(out.y + slice * kSlice);
+        spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+            constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
+#pragma unroll
+            for (int b = 0; b < P / R; ++b)
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int nn = t + T * b + NS * r;
+                    ys[2 * nn + h] = cscale(w[b * R + r], inv);
+                }
+        });
     } else {
         // un-roll by +-H and overlap-add into the zeroed output: every output
         // sample receives exactly two terms, and a + b == b + a, so the
@@ -487,22 +472,25 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
         const float* wnd = out.window;
         long long lo, hi;
         sample_range(out, lo, hi);
-#pragma unroll 2
-        for (int i = t; i < kOut; i += T) {
-            const int m = h * kOut + i;
-            const float2 a = ze[PADI<SH>(m)], b = zo[PADI<SH>(m)];
-            const float val[4] = {a.x * inv, a.y * inv, b.x * inv, b.y * inv};
-            const int j0 = (4 * m + shift) & (kSlice - 1);   // 4 consecutive, no wrap
+        spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+            constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = j0 + e;
-                const float vv = wnd ? val[e] * __ldg(wnd + j) : val[e];
-                const long long p = p0 + j;
-                if (p >= lo && p < hi) atomicAdd(yr + p, vv);
-            }
-        }
+            for (int b = 0; b < P / R; ++b)
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int nn = t + T * b + NS * r;
+                    float2 val = cscale(w[b * R + r], inv);
+                    const int j = (2 * (2 * nn + h) + shift) & (kSlice - 1);
+                    if (wnd) {
+                        val.x *= __ldg(wnd + j);
+                        val.y *= __ldg(wnd + j + 1);
+                    }
+                    const long long p = p0 + j;
+                    if (p >= lo && p < hi) atomicAdd(yr + p, val.x);
+                    if (p + 1 >= lo && p + 1 < hi) atomicAdd(yr + p + 1, val.y);
+                }
+        });
     }
-    cl.sync();   // the partner has finished reading this CTA's shared memory
 }
 
 }  // namespace
