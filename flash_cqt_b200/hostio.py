@@ -1,0 +1,113 @@
+"""Host-resident batches through a device transform, copies overlapped.
+
+Audio that lives in host memory crosses PCIe twice per round trip: x in and
+y out, 256 KiB each per slice.  Issued one after the other, the two copies and
+the transform add up.  The GPU has one copy engine per direction, so a batch
+cut into chunks can run the host-to-device copy of chunk i + 1, the transform
+of chunk i and the device-to-host copy of chunk i - 1 at the same time; a
+step then takes about one direction's PCIe time instead of two plus compute.
+
+    pipe = HostPipeline(lambda x: f.bwd(*f.fwd(x)), chunk=64, device="cuda:0")
+    y_host = pipe(x_host)          # x_host: pinned float32 [B, 65536]
+
+The function runs as one CUDA graph per buffer slot (captured at the chunk
+size); its result is copied into the slot's output buffer inside the graph,
+so functions that return a reused workspace (``FusedOctCQT.bwd``) are safe.
+This helper has no counterpart in the reference, whose API takes device
+tensors only.
+"""
+import torch
+
+
+class HostPipeline:
+    """Runs ``fn`` over the rows of pinned host arrays in chunks.
+
+    fn(x [chunk, n] float32 on device) -> tensor [chunk, n_out] on device.
+    ``depth`` buffer slots (3: one chunk in each of copy-in, compute,
+    copy-out) are allocated once; calls on one pipeline must come from one
+    host thread.
+    """
+
+    def __init__(self, fn, chunk=64, n=65536, device=None, depth=3, warmup=2):
+        if not torch.cuda.is_available():
+            raise RuntimeError("HostPipeline needs a CUDA device")
+        self.dev = torch.device(device) if device is not None else torch.device("cuda")
+        if self.dev.index is None:
+            self.dev = torch.device("cuda", torch.cuda.current_device())
+        self.chunk, self.n, self.depth = int(chunk), int(n), int(depth)
+        if self.chunk < 1 or self.depth < 2:
+            raise ValueError("chunk >= 1 and depth >= 2 are required")
+        with torch.cuda.device(self.dev):
+            self.x = [torch.zeros(self.chunk, self.n, device=self.dev) for _ in range(depth)]
+            side = torch.cuda.Stream(self.dev)
+            side.wait_stream(torch.cuda.current_stream(self.dev))
+            with torch.cuda.stream(side), torch.no_grad():
+                for _ in range(warmup):
+                    probe = fn(self.x[0])
+            torch.cuda.current_stream(self.dev).wait_stream(side)
+            if not torch.is_tensor(probe) or probe.shape[0] != self.chunk:
+                raise ValueError("fn must return a [chunk, ...] tensor")
+            self.y = [torch.empty_like(probe) for _ in range(depth)]
+            self.graphs = []
+            for k in range(depth):
+                g = torch.cuda.CUDAGraph()
+                with torch.no_grad(), torch.cuda.graph(g):
+                    self.y[k].copy_(fn(self.x[k]))
+                self.graphs.append(g)
+            self.s_in = torch.cuda.Stream(self.dev)
+            self.s_out = torch.cuda.Stream(self.dev)
+            self.h2d = [torch.cuda.Event() for _ in range(depth)]
+            self.done = [torch.cuda.Event() for _ in range(depth)]
+            self.d2h = [torch.cuda.Event() for _ in range(depth)]
+        self.count = 0          # chunks issued so far (slot reuse spans calls)
+
+    @torch.no_grad()
+    def __call__(self, x_host, y_host=None, sync=True):
+        """x_host [B, n] float32 (pinned for asynchronous copies) ->
+        y_host [B, n_out].  The copies start after the work the current
+        stream holds at the call.  sync=True returns with y_host complete.
+        sync=False returns once everything is queued and does not make the
+        current stream wait, so back-to-back calls keep both copy directions
+        busy; call join() (or synchronize()) before using the results."""
+        if x_host.device.type != "cpu" or x_host.dim() != 2 or x_host.shape[1] != self.n:
+            raise ValueError(f"x_host must be a host tensor [B, {self.n}]")
+        B = x_host.shape[0]
+        if y_host is None:
+            y_host = torch.empty((B,) + tuple(self.y[0].shape[1:]), dtype=self.y[0].dtype,
+                                 pin_memory=True)
+        main = torch.cuda.current_stream(self.dev)
+        start = torch.cuda.Event()
+        start.record(main)
+        self.s_in.wait_event(start)
+        for c0 in range(0, B, self.chunk):
+            c = min(self.chunk, B - c0)
+            k = self.count % self.depth
+            reuse = self.count >= self.depth
+            with torch.cuda.stream(self.s_in):
+                if reuse:
+                    self.s_in.wait_event(self.done[k])       # slot's input consumed
+                self.x[k][:c].copy_(x_host[c0:c0 + c], non_blocking=True)
+                self.h2d[k].record(self.s_in)
+            main.wait_event(self.h2d[k])
+            if reuse:
+                main.wait_event(self.d2h[k])                  # slot's output drained
+            self.graphs[k].replay()
+            self.done[k].record(main)
+            with torch.cuda.stream(self.s_out):
+                self.s_out.wait_event(self.done[k])
+                y_host[c0:c0 + c].copy_(self.y[k][:c], non_blocking=True)
+                self.d2h[k].record(self.s_out)
+            self.count += 1
+        if sync:
+            self.synchronize()
+        return y_host
+
+    def join(self):
+        """make the current stream wait for every copy issued so far"""
+        main = torch.cuda.current_stream(self.dev)
+        main.wait_stream(self.s_in)
+        main.wait_stream(self.s_out)
+
+    def synchronize(self):
+        self.join()
+        torch.cuda.current_stream(self.dev).synchronize()
