@@ -26,6 +26,7 @@
 // generates the rows in double precision at table upload.
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #include <cooperative_groups.h>
 
@@ -45,46 +46,50 @@ namespace fcqt {
 
 namespace {
 
-template <int P> struct SpecCfg;
-template <> struct SpecCfg<32> {
-    static constexpr int T = 512, NST = 3, R1 = 32, R2 = 32, R3 = 16, R4 = 1;
+// a Stockham schedule: transform length N, P points per thread (T = N / P
+// threads), NST stages of radices R1..R4
+template <int N_, int P_, int NST_, int R1_, int R2_, int R3_, int R4_>
+struct SpecSched {
+    static constexpr int N = N_, P = P_, T = N_ / P_, NST = NST_;
+    static constexpr int R1 = R1_, R2 = R2_, R3 = R3_, R4 = R4_;
 };
-template <> struct SpecCfg<16> {
-    static constexpr int T = 1024, NST = 4, R1 = 16, R2 = 16, R3 = 16, R4 = 4;
-};
+// 16384 points per CTA (two CTAs per slice, one CTA per SM)
+using S16k32 = SpecSched<16384, 32, 3, 32, 32, 16, 1>;
+using S16k16 = SpecSched<16384, 16, 4, 16, 16, 16, 4>;
 
-template <int P>
-constexpr int sR(int s) {
-    using C = SpecCfg<P>;
-    return s == 1 ? C::R1 : s == 2 ? C::R2 : s == 3 ? C::R3 : C::R4;
-}
-template <int P>
-constexpr int sNS(int s) { return s <= 1 ? 1 : sNS<P>(s - 1) * sR<P>(s - 1); }
-template <int P>
-constexpr bool sSplit(int s) { return sNS<P>(s) > 32; }
-template <int P>
+template <class C>
+constexpr int sR(int s) { return s == 1 ? C::R1 : s == 2 ? C::R2 : s == 3 ? C::R3 : C::R4; }
+template <class C>
+constexpr int sNS(int s) { return s <= 1 ? 1 : sNS<C>(s - 1) * sR<C>(s - 1); }
+template <class C>
+constexpr bool sSplit(int s) { return sNS<C>(s) > 32; }
+template <class C>
 constexpr int sSize(int s) {
-    return (s < 2 || s > SpecCfg<P>::NST) ? 0
-           : sSplit<P>(s) ? sR<P>(s) * 32 + sR<P>(s) * (sNS<P>(s) / 32)
-                          : (sR<P>(s) - 1) * sNS<P>(s);
+    return (s < 2 || s > C::NST) ? 0
+           : sSplit<C>(s) ? sR<C>(s) * 32 + sR<C>(s) * (sNS<C>(s) / 32)
+                          : (sR<C>(s) - 1) * sNS<C>(s);
 }
-template <int P>
-constexpr int sOff(int s) { return s <= 2 ? 0 : sOff<P>(s - 1) + sSize<P>(s - 1); }
-template <int P>
-constexpr int twTotal() { return sOff<P>(SpecCfg<P>::NST + 1); }
-template <int P>
-constexpr int shiftOf() { return P == 32 ? 5 : 4; }   // shared padding shift
-template <int P>
-constexpr int smemOf() { return (padded<shiftOf<P>()>(kQuarter) + 512 + twTotal<P>()) * 8; }
+template <class C>
+constexpr int sOff(int s) { return s <= 2 ? 0 : sOff<C>(s - 1) + sSize<C>(s - 1); }
+template <class C>
+constexpr int twTotal() { return sOff<C>(C::NST + 1); }
+template <class C>
+constexpr int shiftOf() { return C::P == 32 ? 5 : 4; }   // shared padding shift
+template <class C>
+constexpr int smemOf() { return (padded<shiftOf<C>()>(C::N) + 512 + twTotal<C>()) * 8; }
 
-static_assert(sNS<16>(4) * sR<16>(4) == kQuarter && sNS<32>(3) * sR<32>(3) == kQuarter,
-              "stage radices must multiply to 16384");
+template <class C>
+constexpr bool sched_ok() { return sNS<C>(C::NST) * sR<C>(C::NST) == C::N; }
+static_assert(sched_ok<S16k32>() && sched_ok<S16k16>(),
+              "stage radices must multiply to the length");
 
-constexpr int kPF = FCQT_SPEC_P_FWD;
-constexpr int kPI = FCQT_SPEC_P_INV;
-// the twiddle-row blob holds the P = 32 rows, then the P = 16 rows
-constexpr int rowsOff(int P) { return P == 32 ? 0 : twTotal<32>(); }
-constexpr int kSpecRowsTotal = twTotal<32>() + twTotal<16>();
+// the twiddle-row blob holds the rows of every schedule, in this order
+template <class C>
+constexpr int rowsOff() { return std::is_same<C, S16k32>::value ? 0 : twTotal<S16k32>(); }
+constexpr int kSpecRowsTotal = twTotal<S16k32>() + twTotal<S16k16>();
+
+using CF = std::conditional<FCQT_SPEC_P_FWD == 32, S16k32, S16k16>::type;
+using CI = std::conditional<FCQT_SPEC_P_INV == 32, S16k32, S16k16>::type;
 
 struct Tw64k {
     const float2* hi;
@@ -92,11 +97,11 @@ struct Tw64k {
     __device__ __forceinline__ float2 operator()(int e) const { return tw64k(hi, lo, e); }
 };
 
-template <int P>
+template <class C>
 __device__ __forceinline__ void load_tables(float2* sm_hilo, float2* sm_tw, const float2* ghi,
                                             const float2* glo, const float2* gtw) {
-    gtw += rowsOff(P);
-    for (int i = threadIdx.x; i < 512 + twTotal<P>(); i += SpecCfg<P>::T) {
+    gtw += rowsOff<C>();
+    for (int i = threadIdx.x; i < 512 + twTotal<C>(); i += C::T) {
         if (i < 256) sm_hilo[i] = __ldg(ghi + i);
         else if (i < 512) sm_hilo[i] = __ldg(glo + i - 256);
         else sm_tw[i - 512] = __ldg(gtw + i - 512);
@@ -104,18 +109,18 @@ __device__ __forceinline__ void load_tables(float2* sm_hilo, float2* sm_tw, cons
 }
 
 // twiddle and DFT of stage s (all butterflies of the thread)
-template <int P, int s, int S>
-__device__ __forceinline__ void spec_compute(float2 (&v)[P], int t, const float2* tws) {
-    constexpr int R = sR<P>(s), NS = sNS<P>(s), off = sOff<P>(s);
-    constexpr int T = SpecCfg<P>::T;
-    static_for<0, P / R>([&](auto Bb) {
+template <class C, int s, int S>
+__device__ __forceinline__ void spec_compute(float2 (&v)[C::P], int t, const float2* tws) {
+    constexpr int R = sR<C>(s), NS = sNS<C>(s), off = sOff<C>(s);
+    constexpr int T = C::T;
+    static_for<0, C::P / R>([&](auto Bb) {
         constexpr int b = decltype(Bb)::value;
         if constexpr (s > 1) {
             const int k = (t + T * b) % NS;
 #pragma unroll
             for (int r = 1; r < R; ++r) {
                 float2 w;
-                if constexpr (sSplit<P>(s)) {
+                if constexpr (sSplit<C>(s)) {
                     w = cmul(tws[off + r * 32 + (k & 31)],
                              tws[off + R * 32 + r * (NS / 32) + (k >> 5)]);
                 } else {
@@ -131,19 +136,19 @@ __device__ __forceinline__ void spec_compute(float2 (&v)[P], int t, const float2
 
 // stages s..NST (stage s - 1 is computed and held in v); `fin` receives the
 // last stage's outputs, index n = j + r NS_last for j = t + T b
-template <int P, int s, int S, class Fin>
-__device__ __forceinline__ void spec_stages(float2 (&v)[P], float2* buf, const float2* tws,
+template <class C, int s, int S, class Fin>
+__device__ __forceinline__ void spec_stages(float2 (&v)[C::P], float2* buf, const float2* tws,
                                             int t, Fin fin) {
-    constexpr int T = SpecCfg<P>::T, SH = shiftOf<P>();
-    if constexpr (s > SpecCfg<P>::NST) {
+    constexpr int T = C::T, SH = shiftOf<C>();
+    if constexpr (s > C::NST) {
         fin(v);
     } else {
-        stage_store<kQuarter, T, sR<P>(s - 1), sNS<P>(s - 1), SH>(v, buf, t);
+        stage_store<C::N, T, sR<C>(s - 1), sNS<C>(s - 1), SH>(v, buf, t);
         __syncthreads();
-        stage_load<kQuarter, T, sR<P>(s), SH>(v, buf, t);
+        stage_load<C::N, T, sR<C>(s), SH>(v, buf, t);
         __syncthreads();
-        spec_compute<P, s, S>(v, t, tws);
-        spec_stages<P, s + 1, S>(v, buf, tws, t, fin);
+        spec_compute<C, s, S>(v, t, tws);
+        spec_stages<C, s + 1, S>(v, buf, tws, t, fin);
     }
 }
 
@@ -222,13 +227,15 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, long long bytes,
 // with its compute; the next wave then loads at L2 speed.  Only addresses
 // inside the readable ranges are touched.
 template <bool SLICED, int T>
-__device__ __forceinline__ void prefetch_signal_half(const SigMap& m, long g, int half, int t) {
+__device__ __forceinline__ void prefetch_signal_part(const SigMap& m, long g, int part, int parts,
+                                                     int t) {
+    const int len = kSlice / parts;
     if constexpr (!SLICED) {
-        const float* base = m.x + g * kSlice + half * (kSlice / 2);
+        const float* base = m.x + g * kSlice + part * len;
         if ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
-            prefetch_l2_bulk(base, kSlice / 2 * 4, t);
+            prefetch_l2_bulk(base, (long long)len * 4, t);
         } else {   // 8-byte aligned signal: per-line prefetches
-            for (int i = t; i < kSlice / 2 / 32; i += T) prefetch_l2(base + 32 * i);
+            for (int i = t; i < len / 32; i += T) prefetch_l2(base + 32 * i);
         }
     } else {
         const long long row = g / m.S;
@@ -236,8 +243,8 @@ __device__ __forceinline__ void prefetch_signal_half(const SigMap& m, long g, in
         long long lo, hi;
         lo = m.sample0 > 0 ? m.sample0 : 0;
         hi = m.sample0 + m.count < m.length ? m.sample0 + m.count : m.length;
-        long long a = 2LL * kQuarter * (sg - 1) + half * (kSlice / 2);
-        long long b = a + kSlice / 2;
+        long long a = 2LL * kQuarter * (sg - 1) + (long long)part * len;
+        long long b = a + len;
         a = a > lo ? a : lo;
         b = b < hi ? b : hi;
         if (a >= b) return;
@@ -251,12 +258,12 @@ __device__ __forceinline__ void prefetch_signal_half(const SigMap& m, long g, in
 }
 
 template <bool SLICED>
-__global__ void __launch_bounds__(SpecCfg<kPF>::T, 1)
+__global__ void __launch_bounds__(CF::T, 1)
 spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                     const float2* __restrict__ ghi, const float2* __restrict__ glo,
                     const float2* __restrict__ gtw, int ahead) {
-    constexpr int P = kPF, T = SpecCfg<P>::T, SH = shiftOf<P>();
-    using C = SpecCfg<P>;
+    using C = CF;
+    constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
     float2* hl = buf + padded<SH>(kQuarter);
@@ -264,7 +271,7 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     const int h = blockIdx.x & 1;
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
-    load_tables<P>(hl, tws, ghi, glo, gtw);
+    load_tables<C>(hl, tws, ghi, glo, gtw);
     __syncthreads();
     const Tw64k tw{hl, hl + 256};
 
@@ -280,13 +287,13 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
             const float2 c = z(n + kQuarter);
             v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
         }
-    spec_compute<P, 1, -1>(v, t, tws);   // consumes the loads
+    spec_compute<C, 1, -1>(v, t, tws);   // consumes the loads
     if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
         const long nb = blockIdx.x + (long)ahead;
-        prefetch_signal_half<SLICED, T>(in, nb >> 1, (int)(nb & 1), t);
+        prefetch_signal_part<SLICED, T>(in, nb >> 1, (int)(nb & 1), 2, t);
     }
-    spec_stages<P, 2, -1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-        stage_store<kQuarter, T, sR<P>(C::NST), sNS<P>(C::NST), SH>(w, buf, t);
+    spec_stages<C, 2, -1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+        stage_store<kQuarter, T, sR<C>(C::NST), sNS<C>(C::NST), SH>(w, buf, t);
     });
     __syncthreads();
 
@@ -347,13 +354,13 @@ __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
 // the CTAs work alone: CTA h stores z[2m + h] into y (swapping halves through
 // distributed shared memory for whole-sector stores measured slower).
 template <bool SLICED>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SpecCfg<kPI>::T, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CI::T, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restrict__ qmask,
                     const SigMap out, const float2* __restrict__ ghi,
                     const float2* __restrict__ glo, const float2* __restrict__ gtw,
                     int nplanes, int ahead) {
-    constexpr int P = kPI, T = SpecCfg<P>::T, SH = shiftOf<P>();
-    using C = SpecCfg<P>;
+    using C = CI;
+    constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
     namespace cg = cooperative_groups;
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
@@ -364,7 +371,7 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     float2* peer = cl.map_shared_rank(buf, h ^ 1);
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
-    load_tables<P>(hl, tws, ghi, glo, gtw);
+    load_tables<C>(hl, tws, ghi, glo, gtw);
     cl.sync();   // tables staged, and the partner is running (its buffer may be written)
     const Tw64k tw{hl, hl + 256};
     const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
@@ -445,13 +452,13 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     float2 v[P];
     stage_load<kQuarter, T, C::R1, SH>(v, buf, t);
     __syncthreads();
-    spec_compute<P, 1, +1>(v, t, tws);
+    spec_compute<C, 1, +1>(v, t, tws);
     const float inv = 1.0f / (float)kHalf;
     if constexpr (!SLICED) {
         // z[2m + h] -> samples 4m + 2h, 4m + 2h + 1
         float2* ys = reinterpret_cast<float2*>(out.y + slice * kSlice);
-        spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-            constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
+        spec_stages<C, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+            constexpr int R = sR<C>(C::NST), NS = sNS<C>(C::NST);
 #pragma unroll
             for (int b = 0; b < P / R; ++b)
 #pragma unroll
@@ -472,8 +479,8 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
         const float* wnd = out.window;
         long long lo, hi;
         sample_range(out, lo, hi);
-        spec_stages<P, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-            constexpr int R = sR<P>(C::NST), NS = sNS<P>(C::NST);
+        spec_stages<C, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+            constexpr int R = sR<C>(C::NST), NS = sNS<C>(C::NST);
 #pragma unroll
             for (int b = 0; b < P / R; ++b)
 #pragma unroll
@@ -498,17 +505,17 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
 int spectrum_twiddle_count() { return kSpecRowsTotal; }
 
 namespace {
-template <int P>
+template <class C>
 void rows_for(float2* out) {
     const double two_pi = 6.283185307179586476925286766559;
     auto w = [&](long e, long base) {
         const double a = -two_pi * (double)(e % base) / (double)base;
         return make_float2((float)std::cos(a), (float)std::sin(a));
     };
-    for (int s = 2; s <= SpecCfg<P>::NST; ++s) {
-        const int R = sR<P>(s), NS = sNS<P>(s), off = sOff<P>(s);
+    for (int s = 2; s <= C::NST; ++s) {
+        const int R = sR<C>(s), NS = sNS<C>(s), off = sOff<C>(s);
         const long base = (long)NS * R;
-        if (sSplit<P>(s)) {
+        if (sSplit<C>(s)) {
             for (int r = 0; r < R; ++r)
                 for (int k = 0; k < 32; ++k) out[off + r * 32 + k] = w((long)r * k, base);
             for (int r = 0; r < R; ++r)
@@ -522,11 +529,11 @@ void rows_for(float2* out) {
 }
 }  // namespace
 
-// stage twiddle rows of both schedules, forward sign, double precision
+// stage twiddle rows of every schedule, forward sign, double precision
 // rounded once
 void spectrum_twiddle_rows(float2* out) {
-    rows_for<32>(out + rowsOff(32));
-    rows_for<16>(out + rowsOff(16));
+    rows_for<S16k32>(out + rowsOff<S16k32>());
+    rows_for<S16k16>(out + rowsOff<S16k16>());
 }
 
 #ifndef FCQT_SPEC_PREFETCH
@@ -555,10 +562,10 @@ cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& s
     if (batch <= 0) return cudaSuccess;
     const int ahead = wave_ctas();
     if (in.S > 0)
-        spectrum_fwd_kernel<true><<<2 * batch, SpecCfg<kPF>::T, smemOf<kPF>(), s>>>(
+        spectrum_fwd_kernel<true><<<2 * batch, CF::T, smemOf<CF>(), s>>>(
             in, X, st.hi, st.lo, st.rows, ahead);
     else
-        spectrum_fwd_kernel<false><<<2 * batch, SpecCfg<kPF>::T, smemOf<kPF>(), s>>>(
+        spectrum_fwd_kernel<false><<<2 * batch, CF::T, smemOf<CF>(), s>>>(
             in, X, st.hi, st.lo, st.rows, ahead);
     return cudaGetLastError();
 }
@@ -568,10 +575,10 @@ cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap
     if (batch <= 0) return cudaSuccess;
     const int ahead = wave_ctas();
     if (out.S > 0)
-        spectrum_inv_kernel<true><<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
+        spectrum_inv_kernel<true><<<2 * batch, CI::T, smemOf<CI>(), s>>>(
             E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
     else
-        spectrum_inv_kernel<false><<<2 * batch, SpecCfg<kPI>::T, smemOf<kPI>(), s>>>(
+        spectrum_inv_kernel<false><<<2 * batch, CI::T, smemOf<CI>(), s>>>(
             E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
     return cudaGetLastError();
 }
@@ -583,12 +590,12 @@ cudaError_t init_spectrum_attributes() {
                          (const void*)spectrum_inv_kernel<true>};
     for (const void* f : fwd) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             smemOf<kPF>());
+                                             smemOf<CF>());
         if (e != cudaSuccess) return e;
     }
     for (const void* f : inv) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             smemOf<kPI>());
+                                             smemOf<CI>());
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
