@@ -159,7 +159,8 @@ def main():
         from datetime import timedelta
         if args.impl == "b200":
             torch.cuda.set_device(local)
-            dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
         else:
             dist.init_process_group("gloo", timeout=timedelta(seconds=300))
     if args.impl == "reference":
