@@ -42,6 +42,7 @@ class Engine:
         self.tables = _native.DeviceTables(self.host_tables, self.dev.index)
         assert self.tables.ncoef == self.ncoef
         self._ws = None
+        self._ws_retired = []   # outgrown workspaces, kept alive (see workspace())
 
     @classmethod
     def from_params(cls, num_octs, bins_per_oct, fs, audio_len, device=None):
@@ -50,8 +51,13 @@ class Engine:
 
     # ---------------------------------------------------------------- plumbing
     def workspace(self, batch):
+        """grow-only scratch shared by the calls on this engine.  An outgrown
+        buffer is retired, not freed: a CUDA graph captured earlier may still
+        address it (Graphed, HostPipeline, the streaming graphs)."""
         need = self.tables.workspace_bytes(batch)
         if self._ws is None or self._ws.numel() < need:
+            if self._ws is not None:
+                self._ws_retired.append(self._ws)
             self._ws = torch.empty(max(need, 16), dtype=torch.uint8, device=self.dev)
         return self._ws
 
@@ -160,7 +166,9 @@ class SlicedEngine:
     Signals are float32 [rows, length] (any row stride with unit element
     stride); coefficients live in one complex64 buffer of rows * S * ncoef
     values, group after group: octave groups as [rows, b, S*M], side groups as
-    [rows, S, M] (the layout of ``SlicedCQT.fwd``'s blocks)."""
+    [rows, S, M] (the layout of ``SlicedCQT.fwd``'s blocks).  ``ws`` overrides
+    the engine's shared workspace with a caller-owned uint8 device buffer of
+    at least ``eng.tables.workspace_bytes(rows * S)`` bytes."""
 
     def __init__(self, eng, window):
         from . import _native
@@ -211,7 +219,7 @@ class SlicedEngine:
                                 int(length))
 
     def analysis(self, x, S=None, out=None, adjoint_of_synthesis=False, slice0=0,
-                 sample0=0, length=None):
+                 sample0=0, length=None, ws=None):
         """x [rows, count] holding global samples [sample0, sample0 + count)
         of signals of global length `length` (default sample0 + count) ->
         coefficients of global slices [slice0, slice0 + S), complex64
@@ -223,7 +231,8 @@ class SlicedEngine:
         if out is None:
             out = torch.empty(self.coef_numel(rows, S), dtype=torch.complex64,
                               device=self.eng.dev)
-        ws = self.eng.workspace(rows * S)
+        if ws is None:
+            ws = self.eng.workspace(rows * S)
         stream = int(torch.cuda.current_stream(self.eng.dev).cuda_stream)
         sig = self._signal(x, sample0, length)
         if adjoint_of_synthesis:
@@ -237,7 +246,7 @@ class SlicedEngine:
         return out
 
     def synthesis(self, coef, rows, S, length, out=None, adjoint_of_analysis=False,
-                  slice0=0, sample0=0, count=None):
+                  slice0=0, sample0=0, count=None, ws=None):
         """coefficients of global slices [slice0, slice0 + S) -> overlap-added
         output [rows, count] holding global samples [sample0, sample0 + count)
         (default: the whole signal [0, length)).  The transpose of the
@@ -250,7 +259,8 @@ class SlicedEngine:
         count = int(length) - sample0 if count is None else int(count)
         if out is None:
             out = torch.empty(rows, count, dtype=torch.float32, device=self.eng.dev)
-        ws = self.eng.workspace(rows * S)
+        if ws is None:
+            ws = self.eng.workspace(rows * S)
         stream = int(torch.cuda.current_stream(self.eng.dev).cuda_stream)
         sig = self._signal(out, sample0, length)
         if adjoint_of_analysis:

@@ -227,6 +227,11 @@ class SlicedCQT:
         out = out[..., 2 * H:]
         return out if length is None else out[..., :length]
 
+    def streamer(self, lead, device=None):
+        """a SliceStream (one CUDA graph replay per chunk) for chunks of
+        shape [*lead, hop]"""
+        return SliceStream(self, lead, device)
+
     # streaming API, state of one half slice (sliced.py:171-209)
     #
     # With the default engine the state stays on the device: stream_fwd keeps
@@ -306,3 +311,116 @@ class SlicedCQT:
                 yield tail + y[..., :hop]
             tail = y[..., hop:]
             k += 1
+
+
+class SliceStream:
+    """The streaming transform as one CUDA graph replay per chunk.
+
+        st = sliced.streamer((B, C))
+        blocks, side = st.fwd(chunk)      # chunk [B, C, hop]; one slice per call
+        blocks, side = st.flush()         # the last slice (zeros after the end)
+        y = st.bwd(blocks, side)          # [B, C, hop], one slice behind; None first
+
+    State on the device: the two-hop input window, the overlap-add tail.
+    Slices map onto the window the same way for every k but the boundary
+    clip, so three graphs per direction cover the stream: k = 0 (samples
+    before the start read as zeros, mapped as global slice 0), odd k (as
+    slice 1) and even k >= 2 (as slice 2); the rolls follow the parity.
+    Results are bit-identical to ``stream_fwd`` / ``stream_bwd`` and to the
+    whole-buffer transform.  Inference only (graphs record no autograd);
+    returned tensors are fresh copies."""
+
+    def __init__(self, sliced, lead, device=None):
+        dev = torch.device(device) if device is not None else sliced.device
+        se = sliced._fused(dev)
+        if se is None:
+            raise RuntimeError("the graphed stream needs the default engine on a CUDA device")
+        self.sl, self.se, self.lead = sliced, se, tuple(lead)
+        rows = 1
+        for d in self.lead:
+            rows *= d
+        self.rows, self.hop = rows, sliced.hop
+        hop = self.hop
+        z = lambda *s_, dt=torch.float32: torch.zeros(*s_, dtype=dt, device=dev)
+        self.win = z(rows, 2 * hop)
+        self.chunk = z(rows, hop)
+        self.coef = z(se.coef_numel(rows, 1), dt=torch.complex64)
+        self.cin = z(se.coef_numel(rows, 1), dt=torch.complex64)
+        self.ybuf = z(rows, 2 * hop)
+        self.tail = z(rows, hop)
+        self.out = z(rows, hop)
+        self.ws = torch.empty(max(se.eng.tables.workspace_bytes(rows), 16), dtype=torch.uint8,
+                              device=dev)
+        self.kf = self.kb = 0
+
+        def fwd_body(s0):
+            self.win[:, :hop].copy_(self.win[:, hop:])
+            self.win[:, hop:].copy_(self.chunk)
+            se.analysis(self.win, 1, out=self.coef, slice0=s0, sample0=hop * (s0 - 1),
+                        length=hop * (s0 + 1), ws=self.ws)
+
+        def bwd_body(s0):
+            se.synthesis(self.cin, rows, 1, hop * (s0 + 1), out=self.ybuf, slice0=s0,
+                         sample0=hop * (s0 - 1), count=2 * hop, ws=self.ws)
+            torch.add(self.tail, self.ybuf[:, :hop], out=self.out)
+            self.tail.copy_(self.ybuf[:, hop:])
+
+        with torch.cuda.device(dev):
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side), torch.no_grad():
+                for s0 in (0, 1, 2):   # warm-up outside the captures
+                    fwd_body(s0)
+                    bwd_body(s0)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            self.gf, self.gb = [], []
+            for s0 in (0, 1, 2):
+                for body, lst in ((fwd_body, self.gf), (bwd_body, self.gb)):
+                    g = torch.cuda.CUDAGraph()
+                    with torch.no_grad(), torch.cuda.graph(g):
+                        body(s0)
+                    lst.append(g)
+        self.reset()
+
+    def reset(self):
+        """start a new stream (the state buffers are cleared)"""
+        self.win.zero_()
+        self.tail.zero_()
+        self.kf = self.kb = 0
+
+    @staticmethod
+    def _variant(k):
+        return 0 if k == 0 else (1 if k % 2 else 2)
+
+    @torch.no_grad()
+    def fwd(self, chunk):
+        """chunk [*lead, hop] -> (blocks, side) of the next slice"""
+        if tuple(chunk.shape) != self.lead + (self.hop,):
+            raise ValueError(f"chunk must be {self.lead + (self.hop,)}, got {tuple(chunk.shape)}")
+        self.chunk.copy_(chunk.reshape(self.rows, self.hop))
+        return self._run_fwd()
+
+    @torch.no_grad()
+    def flush(self):
+        """the final slice: the hop after the last chunk reads as zeros"""
+        self.chunk.zero_()
+        return self._run_fwd()
+
+    def _run_fwd(self):
+        self.gf[self._variant(self.kf)].replay()
+        self.kf += 1
+        blocks, side = self.se.group_views(self.coef.clone(), self.lead, 1)
+        return blocks, [c[:, :, 0] for c in side]
+
+    @torch.no_grad()
+    def bwd(self, blocks, side):
+        """(blocks, side) of the next slice -> the finished hop one slice
+        behind ([*lead, hop]), or None after the first slice"""
+        sd = [c.unsqueeze(2) for c in side] if side is not None else None
+        buf = self.sl._fused_buffer(self.se, blocks, sd, self.rows, 1)
+        self.cin.copy_(buf)
+        self.gb[self._variant(self.kb)].replay()
+        self.kb += 1
+        if self.kb == 1:
+            return None
+        return self.out.clone().view(*self.lead, self.hop)

@@ -376,6 +376,30 @@ def test_sliced_stream_matches_whole_buffer(dev, fused):
         assert snr_db(_np(yw[..., :n * hop]).astype(np.float64), _np(ys)) >= RT_DB
 
 
+def test_graphed_streamer_matches_whole_buffer(dev):
+    """one CUDA graph replay per chunk (SliceStream) == whole-buffer
+    transform bit for bit, across two streams on one streamer"""
+    from flash_cqt_b200 import SlicedCQT
+    sl = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
+    hop, n = sl.hop, 5
+    st = sl.streamer((2, 1))
+    g = torch.Generator(device="cpu").manual_seed(14)
+    for _ in range(2):
+        x = torch.randn(2, 1, n * hop, generator=g).to(dev)
+        wb, ws = sl.fwd(x)
+        yw = sl.bwd(wb, ws)
+        st.reset()
+        outs = [st.fwd(x[..., i * hop:(i + 1) * hop]) for i in range(n)] + [st.flush()]
+        for k, (bl, sd) in enumerate(outs):
+            for c, blk, m in zip(bl, wb, sl.size_per_oct):
+                assert torch.equal(c, blk[..., k * m:(k + 1) * m])
+            for c, whole in zip(sd, ws):
+                assert torch.equal(c, whole[:, :, k])
+        ys = [st.bwd(bl, sd) for bl, sd in outs]
+        assert ys[0] is None
+        assert torch.equal(torch.cat(ys[1:], dim=-1), yw[..., :n * hop])
+
+
 def test_sliced_stream_gradient(dev):
     """gradients through the device-state streaming path equal the
     whole-buffer transform's"""
