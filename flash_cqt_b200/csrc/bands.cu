@@ -150,6 +150,42 @@ __device__ __forceinline__ Inst locate(const BandParams& bp, int c) {
     return in;
 }
 
+#ifndef FCQT_TW3_POW
+#define FCQT_TW3_POW 1
+#endif
+
+// Last-stage twiddles W^{r k} (r < R <= 8) from W^k, W^2k and W^4k only:
+// the other powers are products of at most two of them (two roundings)
+template <int M, int T, int R, int NS, int S, int TWBASE, int P, class TW>
+__device__ __forceinline__ void stage_compute_pow(float2 (&v)[P], int t, const TW& tw) {
+    static_assert(R == 2 || R == 4 || R == 8, "power twiddles for radix 2, 4, 8");
+    static_for<0, P / R>([&](auto Bb) {
+        constexpr int b = decltype(Bb)::value;
+        const int k = (t + T * b) % NS;
+        constexpr int scale = TWBASE / (NS * R);
+        static_assert(scale * NS * R == TWBASE, "twiddle base too small");
+        float2 w[R];
+        w[1] = tw(k * scale);
+        if constexpr (R >= 4) {
+            w[2] = tw(2 * k * scale);
+            w[3] = cmul(w[1], w[2]);
+        }
+        if constexpr (R == 8) {
+            w[4] = tw(4 * k * scale);
+            w[5] = cmul(w[1], w[4]);
+            w[6] = cmul(w[2], w[4]);
+            w[7] = cmul(w[3], w[4]);
+        }
+#pragma unroll
+        for (int r = 1; r < R; ++r) {
+            float2 x = w[r];
+            if constexpr (S > 0) x.y = -x.y;
+            v[b * R + r] = cmul(v[b * R + r], x);
+        }
+        dft<R, S, b * R, 1>(v);
+    });
+}
+
 // stages 2 and 3 after stage 1's DFT; the last stage's outputs (index
 // n = j + r M / R_last, j = t + T b) go to `emit`
 struct Tw2048 {
@@ -181,6 +217,8 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const fl
             __syncthreads();
             if constexpr (FCQT_TW3_SMEM) {
                 stage_compute_rows<M, T, R3, R1 * R2, S>(v, t, tws + L::n2);
+            } else if constexpr (FCQT_TW3_POW) {
+                stage_compute_pow<M, T, R3, R1 * R2, S, 2048>(v, t, Tw2048{bp_tw});
             } else {
                 stage_compute<M, T, R3, R1 * R2, S, 2048>(v, t, Tw2048{bp_tw});
             }
