@@ -70,9 +70,20 @@ size_t ws_need(const cqt_tables* t, int batch) {
     return (size_t)batch * (size_t)t->max_planes * kPlaneStride * sizeof(float2);
 }
 
+// the band kernels split an instance index into (band, slice) with a float
+// reciprocal, exact while slices x (bands of one block length) < 2^24
+int check_slices(const cqt_tables* t, long long slices) {
+    int mx = 1;
+    for (int c = 0; c < t->ncls; ++c) mx = t->cls_nb[c] > mx ? t->cls_nb[c] : mx;
+    if (slices * mx >= (1LL << 24))
+        return fail(CQT_ERR_ARG, "too many slices in one call (split the batch)");
+    return CQT_OK;
+}
+
 int check_common(const cqt_tables* t, int batch, void* ws, size_t ws_bytes, int layout) {
     if (!t) return fail(CQT_ERR_ARG, "null tables");
     if (batch < 0) return fail(CQT_ERR_ARG, "negative batch");
+    if (int rc = check_slices(t, batch)) return rc;
     if (layout != CQT_LAYOUT_PLANAR && layout != CQT_LAYOUT_COMPLEX)
         return fail(CQT_ERR_ARG, "unknown coefficient layout");
     if (batch > 0 && (!ws || ws_bytes < ws_need(t, batch)))
@@ -174,8 +185,7 @@ int check_sliced(const cqt_tables* t, const cqt_slices* sl, const cqt_signal* si
         return fail(CQT_ERR_ARG, "bad slicing (rows >= 0, slices >= 1, slice0 >= 0)");
     if (sig->length < 0 || sig->count < 0 || sig->ld < sig->count)
         return fail(CQT_ERR_ARG, "bad signal geometry (length, count >= 0, ld >= count)");
-    if ((long long)sl->rows * sl->slices > (1LL << 30))
-        return fail(CQT_ERR_ARG, "too many slices in one call");
+    if (int rc = check_slices(t, (long long)sl->rows * sl->slices)) return rc;
     if (t->ngroups < 1) return fail(CQT_ERR_ARG, "tables carry no group layout");
     if (sl->rows > 0 && (!ws || ws_bytes < ws_need(t, sl->rows * sl->slices)))
         return fail(CQT_ERR_ARG, "workspace missing or smaller than cqt_workspace_bytes(rows * S)");

@@ -33,6 +33,10 @@
  *   - workspace: caller-owned device scratch of at least
  *     cqt_workspace_bytes(t, batch) bytes, 16-byte aligned; it may be reused
  *     between calls that are ordered on one stream.
+ *   - One call takes fewer than 2^24 / (largest number of bands sharing one
+ *     block length) slices (batch, or rows x slices); 349,525 for the default
+ *     bank, far more than fit in device memory.  Larger calls return
+ *     CQT_ERR_ARG.
  *   - All entry points are asynchronous on `stream` (a cudaStream_t, NULL =
  *     legacy default stream), allocate nothing, never synchronise, and may be
  *     captured into a CUDA graph.  One cqt_tables may serve several streams.

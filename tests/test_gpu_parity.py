@@ -245,6 +245,15 @@ def test_bad_inputs_raise(eng, dev):
         eng.synthesis(torch.zeros(1, 100, dtype=torch.complex64, device=dev))
 
 
+def test_oversized_batch_refused(eng, dev):
+    """batches past the exact (band, slice) split are refused before any
+    buffer is touched"""
+    from flash_cqt_b200 import _native
+    with pytest.raises(RuntimeError, match="too many slices"):
+        eng.tables.call("cqt_analysis", 0, 0, None, _native.CQT_LAYOUT_COMPLEX, 1 << 24,
+                        0, 0, 0)
+
+
 def test_sliced_matches_oracle(dev):
     from flash_cqt_b200 import SlicedCQT
     from fixtures import STRIDE_SLICED, chirp
