@@ -330,7 +330,7 @@ __device__ __forceinline__ int d_l(int4 d) { return d.z & 0xFFFF; }
 __device__ __forceinline__ int d_lg(int4 d) { return d.z >> 16; }
 __device__ __forceinline__ int d_plane(int4 d, int which) { return (d.w >> (4 + 4 * which)) & 15; }
 
-template <int M, bool SLICED>
+template <int M, bool SLICED, int KIND>
 __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const BandParams& bp,
                          int c, CoefPtr out, float2* smem, float2* tws,
                          unsigned long long* mbar) {
@@ -342,7 +342,13 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     float2* buf = smem + in.il * padded<kSH>(M);
     const float2* Xs = X + (long)in.slice * kPlaneStride;
     const int off = in.d.x;
-    const bool side = d_side(in.d);
+    constexpr bool side = KIND == kSide;   // every instance of the class is of one kind
+    // octave classes whose first-stage inputs r = 6..9 are outside every
+    // band's window support (checked at upload) skip them: no gather, no
+    // gain, a DFT that knows they are zero
+    constexpr unsigned kZero = KIND == kOctavePruned ? 0x3C0u : 0u;
+    static_assert(KIND != kOctavePruned || (R1 == 16 && kP / R1 == 1),
+                  "pruning assumes one radix-16 butterfly per thread in stage 1");
 
     // stage the band's contiguous spectrum segment [lo, lo + n), n <= M,
     // into shared memory with one TMA bulk load issued by the instance's
@@ -351,7 +357,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     // so bin lo + i sits at buf[i + (lo & 1)]
     int lo = 0, n = 0;
     if (in.valid) {
-        if (side) {
+        if constexpr (side) {
             const int2 sg = __ldg(tab.seg + in.d.y);
             lo = sg.x;
             n = sg.y;
@@ -383,9 +389,10 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
         for (int b = 0; b < kP / R1; ++b)
 #pragma unroll
             for (int r = 0; r < R1; ++r)
-                gain[b * R1 + r] = in.valid ? __ldg(gp + T * b + r * (M / R1)) : 0.f;
+                gain[b * R1 + r] = (in.valid && !((kZero >> r) & 1u))
+                                       ? __ldg(gp + T * b + r * (M / R1)) : 0.f;
     }
-    if (side) {   // uniform per instance: one branch, not one per tap
+    if constexpr (side) {
         const int* sp = tab.src + off + t;
 #pragma unroll
         for (int b = 0; b < kP / R1; ++b)
@@ -399,11 +406,15 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     __syncthreads();
     float2 v[kP];
     const float2* seg = buf + sh;
-    if (!side) {
+    if constexpr (!side) {
 #pragma unroll
         for (int b = 0; b < kP / R1; ++b)
 #pragma unroll
             for (int r = 0; r < R1; ++r) {
+                if ((kZero >> r) & 1u) {
+                    v[b * R1 + r] = make_float2(0.f, 0.f);
+                    continue;
+                }
                 const int i = (t + T * b + r * (M / R1) + l) & (M - 1);
                 v[b * R1 + r] = i < n ? cscale(seg[i], gain[b * R1 + r])
                                       : make_float2(0.f, 0.f);
@@ -422,7 +433,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
         }
     }
     static_for<0, kP / R1>([&](auto Bb) {
-        dft<R1, +1, decltype(Bb)::value * R1, 1>(v);
+        dftz<R1, +1, kZero, decltype(Bb)::value * R1, 1>(v);
     });
     __syncthreads();   // the staged segment is dead; stage 1 reuses the buffer
 
@@ -495,7 +506,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     }
 }
 
-template <int M, bool SLICED>
+template <int M, bool SLICED, int KIND>
 __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandParams& bp, int c,
                          float2* __restrict__ E, float2* smem, float2* tws,
                          unsigned long long* mbar) {
@@ -581,7 +592,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     __syncthreads();   // stage 1 reads done; the exchange reuses the buffer
 
     float2* Es = E + (long)in.slice * tab.nplanes * kPlaneStride;
-    const bool side = d_side(in.d);
+    constexpr bool side = KIND == kSide;   // every instance of the class is of one kind
     const int lo = in.d.y, l = d_l(in.d), lg = d_lg(in.d);
     const int pbase = d_plane(in.d, which) * kPlaneStride + lo;
 #if FCQT_PREFETCH_GAINS
@@ -600,7 +611,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     band_rest<M, -1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
         if (!in.valid) return;
-        if (side) {
+        if constexpr (side) {
 #pragma unroll
             for (int b = 0; b < kP / R; ++b)
 #pragma unroll
@@ -650,14 +661,24 @@ bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant
     float2* smem = reinterpret_cast<float2*>(smem_raw);
     float2* tws = smem + kBandData;
     const int c = find_class(bp.sc);
+    const int kind = bp.sc.kind[c];
+    auto run = [&](auto Mc) {
+        constexpr int M = decltype(Mc)::value;
+        if (kind == kSide)
+            band_fwd<M, SLICED, kSide>(X, tab, bp, c, out, smem, tws, &mbar);
+        else if (kind == kOctavePruned)
+            band_fwd<M, SLICED, kOctavePruned>(X, tab, bp, c, out, smem, tws, &mbar);
+        else
+            band_fwd<M, SLICED, kOctave>(X, tab, bp, c, out, smem, tws, &mbar);
+    };
     switch (bp.sc.M[c]) {
-    case 2048: band_fwd<2048, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
-    case 1024: band_fwd<1024, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
-    case 512:  band_fwd<512, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
-    case 256:  band_fwd<256, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
-    case 128:  band_fwd<128, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
-    case 64:   band_fwd<64, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
-    case 32:   band_fwd<32, SLICED>(X, tab, bp, c, out, smem, tws, &mbar); break;
+    case 2048: run(std::integral_constant<int, 2048>{}); break;
+    case 1024: run(std::integral_constant<int, 1024>{}); break;
+    case 512:  run(std::integral_constant<int, 512>{}); break;
+    case 256:  run(std::integral_constant<int, 256>{}); break;
+    case 128:  run(std::integral_constant<int, 128>{}); break;
+    case 64:   run(std::integral_constant<int, 64>{}); break;
+    case 32:   run(std::integral_constant<int, 32>{}); break;
     default: break;
     }
 }
@@ -671,21 +692,30 @@ bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ Band
     float2* smem = reinterpret_cast<float2*>(smem_raw);
     float2* tws = smem + kBandData;
     const int c = find_class(bp.sc);
+    const bool side = bp.sc.kind[c] == kSide;
+    auto run = [&](auto Mc) {
+        constexpr int M = decltype(Mc)::value;
+        if (side)
+            band_inv<M, SLICED, kSide>(in, tab, which, bp, c, E, smem, tws, &mbar);
+        else
+            band_inv<M, SLICED, kOctave>(in, tab, which, bp, c, E, smem, tws, &mbar);
+    };
     switch (bp.sc.M[c]) {
-    case 2048: band_inv<2048, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
-    case 1024: band_inv<1024, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
-    case 512:  band_inv<512, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
-    case 256:  band_inv<256, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
-    case 128:  band_inv<128, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
-    case 64:   band_inv<64, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
-    case 32:   band_inv<32, SLICED>(in, tab, which, bp, c, E, smem, tws, &mbar); break;
+    case 2048: run(std::integral_constant<int, 2048>{}); break;
+    case 1024: run(std::integral_constant<int, 1024>{}); break;
+    case 512:  run(std::integral_constant<int, 512>{}); break;
+    case 256:  run(std::integral_constant<int, 256>{}); break;
+    case 128:  run(std::integral_constant<int, 128>{}); break;
+    case 64:   run(std::integral_constant<int, 64>{}); break;
+    case 32:   run(std::integral_constant<int, 32>{}); break;
     default: break;
     }
 }
 
 }  // namespace
 
-BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, int batch) {
+BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, const int* kind,
+                     int batch) {
     BandSched sc{};
     sc.ncls = ncls;
     sc.batch = batch;
@@ -695,6 +725,7 @@ BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, in
         sc.M[c] = M[c];
         sc.nb[c] = nb[c];
         sc.first[c] = first[c];
+        sc.kind[c] = kind[c];
         sc.cta0[c] = cta;
         const int ipc = kBandCap / M[c];
         const long inst = (long)nb[c] * batch;

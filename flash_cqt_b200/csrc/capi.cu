@@ -23,8 +23,8 @@ struct cqt_tables {
     int device;
     int ncoef;
     int nbands;
-    int ncls;
-    int cls_M[kMaxClasses], cls_nb[kMaxClasses], cls_first[kMaxClasses];
+    int ncls;   // internal classes (see BandKind)
+    int cls_M[kMaxClasses], cls_nb[kMaxClasses], cls_first[kMaxClasses], cls_kind[kMaxClasses];
     FwdTab fwd[2];   // 0 analysis, 1 transpose of synthesis
     InvTab inv[2];   // 0 synthesis, 1 transpose of analysis
     const float2* tw2048;
@@ -106,7 +106,7 @@ int coef_ptr(const float* re, const float* im, int layout, CoefPtr* out) {
 
 BandParams band_params(const cqt_tables* t, int batch) {
     BandParams bp;
-    bp.sc = make_sched(t->ncls, t->cls_M, t->cls_nb, t->cls_first, batch);
+    bp.sc = make_sched(t->ncls, t->cls_M, t->cls_nb, t->cls_first, t->cls_kind, batch);
     bp.tw2048 = t->tw2048;
     bp.ncoef = t->ncoef;
     std::memcpy(bp.desc, t->desc, sizeof bp.desc);
@@ -232,7 +232,7 @@ size_t cqt_workspace_bytes(const cqt_tables* t, int batch) {
 int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     if (!h || !out) return fail(CQT_ERR_ARG, "null argument");
     *out = nullptr;
-    if (h->nclasses < 1 || h->nclasses > kMaxClasses)
+    if (h->nclasses < 1 || h->nclasses > kMaxHostClasses)
         return fail(CQT_ERR_ARG, "class count out of range");
     if (h->sy_nplanes < 1 || h->sy_nplanes > kMaxPlanes || h->aa_nplanes < 1 ||
         h->aa_nplanes > kMaxPlanes)
@@ -366,6 +366,40 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
             (q > kHalf && (h->sy_mask[q] | h->aa_mask[q])))
             return fail(CQT_ERR_ARG, "plane mask names a plane or bin out of range");
 
+    // internal classes: each host class's octave bands (pruned when the
+    // first-stage inputs r = 6..9 of every radix-16 butterfly lie outside
+    // every band's window support), then its side bands; the host classes
+    // must cover every band exactly once
+    std::vector<int> order;
+    std::vector<int> seen(h->nbands, 0);
+    int ncls = 0, cls_M[kMaxClasses], cls_nb[kMaxClasses], cls_first[kMaxClasses],
+        cls_kind[kMaxClasses];
+    for (int c = 0; c < h->nclasses; ++c) {
+        const int M = h->class_len[c];
+        for (int kind = 0; kind < 2; ++kind) {
+            const int first = (int)order.size();
+            bool prune = true;
+            for (int i = 0; i < h->class_count[c]; ++i) {
+                const int b = h->band_list[h->class_first[c] + i];
+                const int32_t* g = h->band_geom + 4 * b;
+                if ((int)(g[3] & 1) != kind) continue;
+                if (seen[b]++) return fail(CQT_ERR_ARG, "a band sits in two classes");
+                order.push_back(b);
+                for (int r = 6; r <= 9 && kind == 0; ++r)
+                    for (int j = 0; j < M / 16; ++j)
+                        if (((j + r * (M / 16) + g[1]) & (M - 1)) < g[2]) prune = false;
+            }
+            const int nb = (int)order.size() - first;
+            if (nb == 0) continue;
+            cls_M[ncls] = M;
+            cls_nb[ncls] = nb;
+            cls_first[ncls] = first;
+            cls_kind[ncls] = kind ? kSide : (prune ? kOctavePruned : kOctave);
+            ++ncls;
+        }
+    }
+    if ((int)order.size() != h->nbands) return fail(CQT_ERR_ARG, "classes do not cover every band");
+
     int prev = -1;
     cudaGetDevice(&prev);
     cudaError_t e = cudaSetDevice(device);
@@ -436,11 +470,12 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     t->device = device;
     t->ncoef = nc;
     t->nbands = h->nbands;
-    t->ncls = h->nclasses;
-    for (int c = 0; c < h->nclasses; ++c) {
-        t->cls_M[c] = h->class_len[c];
-        t->cls_nb[c] = h->class_count[c];
-        t->cls_first[c] = h->class_first[c];
+    t->ncls = ncls;
+    for (int c = 0; c < ncls; ++c) {
+        t->cls_M[c] = cls_M[c];
+        t->cls_nb[c] = cls_nb[c];
+        t->cls_first[c] = cls_first[c];
+        t->cls_kind[c] = cls_kind[c];
     }
     t->fwd[0] = FwdTab{(const int*)P(i_ans), (const float*)P(i_ang), (const int2*)P(i_ansg)};
     t->fwd[1] = FwdTab{(const int*)P(i_ass), (const float*)P(i_asg), (const int2*)P(i_assg)};
@@ -458,7 +493,7 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
         t->group_len[g] = band_M[group_first[g]];
     }
     for (int i = 0; i < h->nbands; ++i) {
-        const int b = h->band_list[i];
+        const int b = order[i];
         const int32_t* g = h->band_geom + 4 * b;
         const bool side = g[3] & 1;
         t->desc[i] = make_int4(h->band_off[b], side ? b : g[0], g[1] | (g[2] << 16),

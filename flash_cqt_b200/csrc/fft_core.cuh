@@ -207,3 +207,109 @@ __device__ __forceinline__ void dft(float2 (&v)[P]) {
 }
 
 }  // namespace fcqt
+
+namespace fcqt {
+
+// ------------------------------------------------------------------
+// DFT with inputs known to be zero (bit n of Z: input n is 0).  The additions
+// with a known zero are dropped; results equal dft<R, S, ...> except that a
+// zero may come out with the other sign.
+
+template <bool ZA, bool ZB>
+__device__ __forceinline__ float2 zadd(float2 a, float2 b) {
+    if constexpr (ZA && ZB) return make_float2(0.f, 0.f);
+    else if constexpr (ZA) return b;
+    else if constexpr (ZB) return a;
+    else return cadd(a, b);
+}
+template <bool ZA, bool ZB>
+__device__ __forceinline__ float2 zsub(float2 a, float2 b) {
+    if constexpr (ZA && ZB) return make_float2(0.f, 0.f);
+    else if constexpr (ZA) return make_float2(-b.x, -b.y);
+    else if constexpr (ZB) return a;
+    else return csub(a, b);
+}
+
+// the bits of Z at inputs B0 + n * STRIDE' that form sub-DFT `n2` of a split
+template <int R, unsigned Z, int R2, int n2>
+constexpr unsigned sub_mask() {
+    unsigned m = 0;
+    for (int n1 = 0; n1 < R / R2; ++n1)
+        if ((Z >> (R2 * n1 + n2)) & 1u) m |= 1u << n1;
+    return m;
+}
+
+template <int R, int S, unsigned Z, int B0 = 0, int STRIDE = 1, int P>
+__device__ __forceinline__ void dftz(float2 (&v)[P]) {
+    constexpr unsigned ALL = (R >= 32) ? 0xFFFFFFFFu : ((1u << R) - 1u);
+    if constexpr ((Z & ALL) == 0) {
+        dft<R, S, B0, STRIDE>(v);
+    } else if constexpr ((Z & ALL) == ALL) {
+#pragma unroll
+        for (int n = 0; n < R; ++n) v[B0 + n * STRIDE] = make_float2(0.f, 0.f);
+    } else if constexpr (R == 2) {
+        const float2 a = v[B0], b = v[B0 + STRIDE];
+        v[B0] = zadd<(Z & 1u) != 0, (Z & 2u) != 0>(a, b);
+        v[B0 + STRIDE] = zsub<(Z & 1u) != 0, (Z & 2u) != 0>(a, b);
+    } else if constexpr (R == 4) {
+        constexpr bool z0 = Z & 1u, z1 = Z & 2u, z2 = Z & 4u, z3 = Z & 8u;
+        const float2 x0 = v[B0], x1 = v[B0 + STRIDE], x2 = v[B0 + 2 * STRIDE],
+                     x3 = v[B0 + 3 * STRIDE];
+        const float2 t0 = zadd<z0, z2>(x0, x2), t1 = zsub<z0, z2>(x0, x2);
+        const float2 t2 = zadd<z1, z3>(x1, x3), t3 = mul_si<S>(zsub<z1, z3>(x1, x3));
+        constexpr bool zt0 = z0 && z2, zt2 = z1 && z3;
+        v[B0] = zadd<zt0, zt2>(t0, t2);
+        v[B0 + 2 * STRIDE] = zsub<zt0, zt2>(t0, t2);
+        v[B0 + STRIDE] = zadd<zt0, zt2>(t1, t3);
+        v[B0 + 3 * STRIDE] = zsub<zt0, zt2>(t1, t3);
+    } else {
+        constexpr int R1 = Split<R>::R1, R2 = Split<R>::R2;
+        static_assert(R1 * R2 == R && R1 > 1, "unsupported radix");
+        // step 1: length-R1 DFTs over n1 for each n2, with their zero inputs
+        static_for<0, R2>([&](auto N2) {
+            constexpr int n2 = decltype(N2)::value;
+            dftz<R1, S, sub_mask<R, Z, R2, n2>(), B0 + n2 * STRIDE, R2 * STRIDE>(v);
+        });
+        // a sub-DFT whose inputs were all zero gives zeros: no twiddle
+        static_for<1, R2>([&](auto N2) {
+            constexpr int n2 = decltype(N2)::value;
+            constexpr bool dead = sub_mask<R, Z, R2, n2>() == ((1u << R1) - 1u);
+            if constexpr (!dead) {
+                static_for<1, R1>([&](auto K1) {
+                    constexpr int k1 = decltype(K1)::value;
+                    constexpr int slot = B0 + (R2 * k1 + n2) * STRIDE;
+                    v[slot] = twc<R, n2 * k1, S>(v[slot]);
+                });
+            }
+        });
+        // step 2: length-R2 DFTs over n2, zero where a whole sub-DFT was
+        constexpr unsigned Z2 = [] {
+            unsigned m = 0;
+            for (int n2 = 0; n2 < R2; ++n2) {
+                unsigned s = 0;
+                for (int n1 = 0; n1 < R1; ++n1)
+                    if ((Z >> (R2 * n1 + n2)) & 1u) s |= 1u << n1;
+                if (s == ((1u << R1) - 1u)) m |= 1u << n2;
+            }
+            return m;
+        }();
+        static_for<0, R1>([&](auto K1) {
+            constexpr int k1 = decltype(K1)::value;
+            dftz<R2, S, Z2, B0 + R2 * k1 * STRIDE, STRIDE>(v);
+        });
+        float2 t[R];
+        static_for<0, R1>([&](auto K1) {
+            constexpr int k1 = decltype(K1)::value;
+            static_for<0, R2>([&](auto K2) {
+                constexpr int k2 = decltype(K2)::value;
+                t[k1 + R1 * k2] = v[B0 + (R2 * k1 + k2) * STRIDE];
+            });
+        });
+        static_for<0, R>([&](auto K) {
+            constexpr int k = decltype(K)::value;
+            v[B0 + k * STRIDE] = t[k];
+        });
+    }
+}
+
+}  // namespace fcqt

@@ -22,7 +22,11 @@ struct InvTab {            // synthesis-engine tap table (one per use)
     int nplanes;
 };
 
-constexpr int kMaxClasses = 8;
+constexpr int kMaxHostClasses = 8;   // block-length classes of the host tables
+// internal classes: each host class splits into its octave bands and its
+// side (per-tap table) bands, so a CTA holds one kind only
+constexpr int kMaxClasses = 2 * kMaxHostClasses;
+enum BandKind { kOctave = 0, kOctavePruned = 1, kSide = 2 };
 
 struct BandSched {         // CTA ranges of the block-length classes for one launch
     int ncls;
@@ -30,6 +34,7 @@ struct BandSched {         // CTA ranges of the block-length classes for one lau
     int nb[kMaxClasses];       // bands in the class
     int first[kMaxClasses];    // first entry of the class in band_list
     int cta0[kMaxClasses + 1]; // first CTA of each class, cta0[ncls] = grid
+    int kind[kMaxClasses];     // BandKind of the class
     int batch;
     float inv_batch;           // 1 / batch, for the instance -> (band, slice) split
 };
@@ -105,7 +110,8 @@ constexpr int kBandP = FCQT_BAND_P;
 constexpr int kBandThreads = FCQT_BAND_THREADS;
 constexpr int kBandCap = kBandThreads * kBandP;   // points per band CTA
 
-BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, int batch);
+BandSched make_sched(int ncls, const int* M, const int* nb, const int* first, const int* kind,
+                     int batch);
 
 cudaError_t init_kernel_attributes();
 struct SpecTables {        // packed-spectrum engine twiddles (device)
