@@ -595,18 +595,26 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     constexpr bool side = KIND == kSide;   // every instance of the class is of one kind
     const int lo = in.d.y, l = d_l(in.d), lg = d_lg(in.d);
     const int pbase = d_plane(in.d, which) * kPlaneStride + lo;
+    // last-stage outputs r of a pruned octave class that lie outside every
+    // band's window support (taps [6M/16, 10M/16), checked at upload): for
+    // M = 2048 the radix-8 outputs 3 and 4 -- no gain, no index, no store
+    constexpr int RL = TwLayout<M>::R3 > 1 ? TwLayout<M>::R3
+                       : TwLayout<M>::R2 > 1 ? TwLayout<M>::R2 : TwLayout<M>::R1;
+    constexpr unsigned kDeadOut = (KIND == kOctavePruned && M == 2048) ? 0x18u : 0u;
+    static_assert(kDeadOut == 0 || RL == 8, "dead outputs assume a radix-8 last stage");
 #if FCQT_PREFETCH_GAINS
     // the gains of this thread's final-stage outputs, loaded before the
     // stages so the scatter does not wait on them
-    constexpr int RL = TwLayout<M>::R3 > 1 ? TwLayout<M>::R3
-                       : TwLayout<M>::R2 > 1 ? TwLayout<M>::R2 : TwLayout<M>::R1;
     constexpr int NSL = M / RL;
     float gpre[kP];
+    if constexpr (!side) {
 #pragma unroll
-    for (int b = 0; b < kP / RL; ++b)
+        for (int b = 0; b < kP / RL; ++b)
 #pragma unroll
-        for (int r = 0; r < RL; ++r)
-            gpre[b * RL + r] = in.valid ? __ldg(tab.gre + off + t + T * b + r * NSL) : 0.f;
+            for (int r = 0; r < RL; ++r)
+                gpre[b * RL + r] = (in.valid && !((kDeadOut >> r) & 1u))
+                                       ? __ldg(tab.gre + off + t + T * b + r * NSL) : 0.f;
+    }
 #endif
     band_rest<M, -1>(v, buf, tws, bp.tw2048, t, [&](float2 (&w)[kP], auto Rc, auto NSc) {
         constexpr int R = decltype(Rc)::value, NS = decltype(NSc)::value;
@@ -629,6 +637,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
             for (int b = 0; b < kP / R; ++b)
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
+                    if ((kDeadOut >> r) & 1u) continue;
                     const int m = t + T * b + r * NS;
                     const int i = (m + l) & (M - 1);
 #if FCQT_PREFETCH_GAINS
@@ -693,10 +702,13 @@ bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ Band
     float2* tws = smem + kBandData;
     const int c = find_class(bp.sc);
     const bool side = bp.sc.kind[c] == kSide;
+    const bool pruned = bp.sc.kind[c] == kOctavePruned;
     auto run = [&](auto Mc) {
         constexpr int M = decltype(Mc)::value;
         if (side)
             band_inv<M, SLICED, kSide>(in, tab, which, bp, c, E, smem, tws, &mbar);
+        else if (M == 2048 && pruned)
+            band_inv<M, SLICED, kOctavePruned>(in, tab, which, bp, c, E, smem, tws, &mbar);
         else
             band_inv<M, SLICED, kOctave>(in, tab, which, bp, c, E, smem, tws, &mbar);
     };
