@@ -113,3 +113,33 @@ def test_adjoint_models_vs_oracle(heap, tabs):
     gk = km.bands_fwd(km.spectrum_fwd(gy), {"src": src, "gain": gain},
                       heap.bands)
     assert snr_db(o.heap(o.adj_bwd(gy)), gk) > 140
+
+
+@pytest.mark.parametrize("bank", [([3, 4, 2], [8, 16, 32]), ([4, 4, 1], [8, 16, 32]),
+                                  ([2, 2, 2, 3], [8, 12, 16, 32]), ([3, 4, 2], [8, 64, 64])])
+def test_pruned_taps_are_dead(bank):
+    """The band kernels skip the first-stage inputs r = 6..9 of a block-length
+    class (and, at M = 2048, the last-stage outputs 3 and 4 of the
+    synthesis) when the closed-form geometry puts taps [6M/16, 10M/16) outside
+    every octave band's window (the upload's check).  The per-tap tables must
+    agree: no gather and no scatter tap in that range carries a gain."""
+    tabs = build_tables(HeapLayout(Filterbank(bank[0], bank[1], 44100, 65536)))
+    geom, blen, boff = tabs["band_geom"], tabs["band_len"], tabs["band_off"]
+    sets = [tabs["fwd"]["analysis"][1], tabs["fwd"]["adj_synth"][1],
+            tabs["inv"]["synth"][1], tabs["inv"]["adj_an"][1]]
+    pruned = 0
+    for M in sorted(set(blen.tolist())):
+        octave = [b for b in range(len(blen)) if blen[b] == M and not geom[b, 3] & 1]
+        if not octave:
+            continue
+        m = np.arange(6 * M // 16, 10 * M // 16)
+        # the upload's criterion, from the closed-form geometry alone
+        if not all((((m + geom[b, 1]) & (M - 1)) >= geom[b, 2]).all() for b in octave):
+            continue
+        pruned += 1
+        for b in octave:
+            for gains in sets:
+                assert not gains[boff[b] + m].any(), (M, b)
+        if M == 2048:   # last stage radix 8, span 256: outputs 3, 4 = taps 768..1279
+            assert 3 * 256 == 6 * M // 16 and 5 * 256 == 10 * M // 16
+    assert pruned > 0
