@@ -402,8 +402,10 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
                 src[b * R1 + r] = sv < 0 ? -1 : (((sv & 0xFFFF) - lo) | (sv & 0x10000));
             }
     }
+    // each thread's completed wait makes the bulk-loaded segment visible to
+    // it; the twiddle rows filled above are first read in stage 2, behind the
+    // stage-1 exchange barrier, so no CTA barrier is needed here
     mbar_wait(mbar, 0);
-    __syncthreads();
     float2 v[kP];
     const float2* seg = buf + sh;
     if constexpr (!side) {
