@@ -50,7 +50,8 @@ constexpr int kBandData = padded<kSH>(kBandCap);         // float2 per CTA
 #endif
 constexpr int kBandTw = FCQT_TW3_SMEM ? 2048 : 1024;     // >= largest twiddle set
 constexpr int kBandSmem = (kBandData + kBandTw) * 8;
-constexpr int kBandMinBlocks = kP == 32 ? 2 : 4;        // 128 / 64 registers a thread
+// resident CTAs per SM at 128 (P = 32) or 64 (P = 16) registers a thread
+constexpr int kBandMinBlocks = (kP == 32 ? 2 : 4) * 256 / kBandThreads;
 
 template <int M, int P = kP> struct Sched;   // stage radices per block length
 template <> struct Sched<32, 32>   { static constexpr int R1 = 32, R2 = 1,  R3 = 1; };

@@ -104,8 +104,10 @@ struct CoefPtr {           // coefficient heap addressing
 #define FCQT_BAND_P 16
 #endif
 constexpr int kBandP = FCQT_BAND_P;
+// 128 threads of 16 points: 2048 points per band CTA, eight CTAs per SM (the
+// fastest of 128 / 256 / 512 measured; 128 is the least a 2048-point band needs)
 #ifndef FCQT_BAND_THREADS
-#define FCQT_BAND_THREADS 256
+#define FCQT_BAND_THREADS 128
 #endif
 constexpr int kBandThreads = FCQT_BAND_THREADS;
 constexpr int kBandCap = kBandThreads * kBandP;   // points per band CTA
