@@ -101,3 +101,43 @@ def test_slice_ranges_cover_and_balance():
             assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
             n = [b - a for a, b in r]
             assert max(n) - min(n) <= 1
+
+
+def _dropping_worker(rank, world, port, q):
+    """rank 1 fails before the halo exchange (it never sends); rank 0 must
+    get an error from its bounded wait, not hang"""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    part = Partition(4 * 32768, 4, rank, world)
+    lo, hi = part.synthesis_window()
+    local = torch.zeros(2, hi - lo)
+    try:
+        if rank == 1:
+            q.put((rank, "dropped"))
+            return                      # leaves without sending its first hop
+        try:
+            exchange_halo(local, part)
+            q.put((rank, "no error"))
+        except Exception as e:          # the bounded wait gave up
+            q.put((rank, type(e).__name__))
+    finally:
+        if rank == 0:
+            dist.destroy_process_group()
+
+
+def test_dropped_halo_times_out():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dropping_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert got[1] == "dropped"
+    assert got[0] not in ("no error",), got
+    assert all(p.exitcode is not None for p in procs)
