@@ -45,7 +45,10 @@ def parse():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of SM clock and throttle reasons."""
+    """nvidia-smi samples (every 20 ms) of SM clock and throttle reasons,
+    read on a thread as they arrive.  Entering waits (up to 3 s) for the first
+    sample, so a short timed region still has samples: the first is taken
+    right before it, with the GPU still at load clocks from the warm-up."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,"
@@ -54,27 +57,39 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.lines = []
+        self._first = threading.Event()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.lines.append(ln)
+                self._first.set()
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+        self._first.wait(timeout=3.0)
         return self
 
     def __exit__(self, *a):
-        self.lines = []
         if self.proc is not None:
+            time.sleep(0.03)   # one more sample at the end of the region
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+                self.proc.wait()
+            self._thread.join(timeout=5)
 
     def summary(self):
         sm, smax, reasons = [], None, set()
