@@ -221,3 +221,57 @@ def _cplx32(z):
     out[..., 0] = z.real
     out[..., 1] = z.imag
     return out
+
+
+# ---------------------------------------------------------------- C export
+# Field order of the binary table file: the pointer fields of
+# cqt_host_tables (include/flash_cqt_b200.h) in declaration order, with the
+# two plane counts as one-element int32 arrays after their masks.
+HOST_FIELDS = [
+    ("band_off", np.int32), ("band_list", np.int32), ("band_geom", np.int32),
+    ("group_count", np.int32), ("group_roll", np.int32),
+    ("class_len", np.int32), ("class_count", np.int32), ("class_first", np.int32),
+    ("an_src", np.int32), ("an_gain", np.float32), ("an_seg", np.int32),
+    ("as_src", np.int32), ("as_gain", np.float32), ("as_seg", np.int32),
+    ("sy_dest", np.int32), ("sy_gre", np.float32), ("sy_gim", np.float32),
+    ("sy_mask", np.uint8), ("sy_nplanes", np.int32),
+    ("aa_dest", np.int32), ("aa_gre", np.float32), ("aa_gim", np.float32),
+    ("aa_mask", np.uint8), ("aa_nplanes", np.int32),
+    ("tw2048", np.float32), ("tw_hi", np.float32), ("tw_lo", np.float32),
+]
+
+
+def host_arrays(tabs):
+    """the cqt_host_tables arrays of `tabs` by field name"""
+    cls = tabs["classes"]
+    a = {
+        "band_off": tabs["band_off"], "band_list": tabs["band_list"],
+        "band_geom": tabs["band_geom"], "group_count": tabs["group_count"],
+        "group_roll": tabs["group_roll"],
+        "class_len": [c[0] for c in cls], "class_count": [c[1] for c in cls],
+        "class_first": [c[2] for c in cls],
+        "an_src": tabs["fwd"]["analysis"][0], "an_gain": tabs["fwd"]["analysis"][1],
+        "an_seg": tabs["seg"]["analysis"],
+        "as_src": tabs["fwd"]["adj_synth"][0], "as_gain": tabs["fwd"]["adj_synth"][1],
+        "as_seg": tabs["seg"]["adj_synth"],
+        "tw2048": tabs["tw2048"], "tw_hi": tabs["tw_hi"], "tw_lo": tabs["tw_lo"],
+    }
+    for pre, key in (("sy", "synth"), ("aa", "adj_an")):
+        d, gr, gi, mk, npl = tabs["inv"][key]
+        a.update({pre + "_dest": d, pre + "_gre": gr, pre + "_gim": gi,
+                  pre + "_mask": mk, pre + "_nplanes": [npl]})
+    return {k: np.ascontiguousarray(np.asarray(v), dtype=dt).reshape(-1)
+            for (k, dt), v in ((f, a[f[0]]) for f in HOST_FIELDS)}
+
+
+def save_host_tables(tabs, path):
+    """Write the host tables for C consumers of the library: for every field
+    of HOST_FIELDS in order, an int64 element count and the raw
+    little-endian elements.  nbands, ncoef, ngroups and nclasses are the
+    counts of band_off, an_src, group_count and class_len."""
+    arrs = host_arrays(tabs)
+    with open(path, "wb") as f:
+        for name, _ in HOST_FIELDS:
+            a = arrs[name]
+            f.write(np.int64(a.size).tobytes())
+            f.write(a.tobytes())
