@@ -196,13 +196,22 @@ class DeviceTables:
     def workspace_bytes(self, batch):
         return int(lib().cqt_workspace_bytes(self.handle, int(batch)))
 
+    _SIG_FIRST = ("cqt_analysis", "cqt_adj_synthesis")
+
     def call(self, name, a, b, c, layout, batch, ws, ws_bytes, stream):
-        fn = getattr(lib(), name)
-        if name in ("cqt_analysis", "cqt_adj_synthesis"):
+        fns = self.__dict__.get("_fns")
+        if fns is None:   # bound once: no library lock on the per-call path
+            L = lib()
+            fns = self._fns = {n: getattr(L, n) for n in
+                               ("cqt_analysis", "cqt_synthesis", "cqt_adj_analysis",
+                                "cqt_adj_synthesis")}
+        fn = fns[name]
+        if name in self._SIG_FIRST:
             rc = fn(self.handle, a, b, c, layout, int(batch), ws, ws_bytes, stream)
         else:
             rc = fn(self.handle, a, b, layout, c, int(batch), ws, ws_bytes, stream)
-        _check(rc, name)
+        if rc != 0:
+            _check(rc, name)
 
     def stage(self, stage, sig_in, sig_out, c_re, c_im, layout, batch, ws,
               ws_bytes, stream):

@@ -15,9 +15,8 @@
 // (m + l) mod M < Lg (the window support, oct_cqt.py:44-58), no conjugation,
 // one colour plane per band -- so they need one gain load per tap and no
 // index tables.  The two side bands take the table path (src / dest tables,
-// conjugated mirror taps).  Band descriptors travel in the kernel parameters
-// (constant bank), so a CTA starts its memory traffic without any dependent
-// global loads.
+// conjugated mirror taps).  Band descriptors come from the kernel
+// parameters (the first 160) or the table blob.
 //
 // Replaces the reference's radix band engine (radix_impl.cuh:146-443: warp
 // shuffle radix-8/16/32 butterflies, one CTA per (band, slice), atomics in
@@ -131,7 +130,7 @@ struct Inst {
     int4 d;       // band descriptor
 };
 
-template <int M>
+template <int M, bool EXT>
 __device__ __forceinline__ Inst locate(const BandParams& bp, int c) {
     constexpr int T = M / kP;
     constexpr int IPC = kBandThreads / T;
@@ -147,7 +146,12 @@ __device__ __forceinline__ Inst locate(const BandParams& bp, int c) {
     if (rem >= B) { ++q; rem -= B; }
     if (rem < 0) { --q; rem += B; }
     in.slice = in.valid ? rem : 0;
-    in.d = bp.desc[bp.sc.first[c] + (in.valid ? q : 0)];
+    const int di = bp.sc.first[c] + (in.valid ? q : 0);
+    // banks within kInlineBands read the parameters, larger ones device memory
+    if constexpr (EXT)
+        in.d = __ldg(bp.desc + di);
+    else
+        in.d = bp.desc_inline[di];
     return in;
 }
 
@@ -331,14 +335,14 @@ __device__ __forceinline__ int d_l(int4 d) { return d.z & 0xFFFF; }
 __device__ __forceinline__ int d_lg(int4 d) { return d.z >> 16; }
 __device__ __forceinline__ int d_plane(int4 d, int which) { return (d.w >> (4 + 4 * which)) & 15; }
 
-template <int M, bool SLICED, int KIND>
+template <int M, bool SLICED, int KIND, bool EXT>
 __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const BandParams& bp,
                          int c, CoefPtr out, float2* smem, float2* tws,
                          unsigned long long* mbar) {
     constexpr int T = M / kP;
     constexpr int R1 = Sched<M>::R1;
     constexpr int IPC = kBandThreads / T;
-    const Inst in = locate<M>(bp, c);
+    const Inst in = locate<M, EXT>(bp, c);
     const int t = in.t;
     float2* buf = smem + in.il * padded<kSH>(M);
     const float2* Xs = X + (long)in.slice * kPlaneStride;
@@ -509,14 +513,14 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     }
 }
 
-template <int M, bool SLICED, int KIND>
+template <int M, bool SLICED, int KIND, bool EXT>
 __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandParams& bp, int c,
                          float2* __restrict__ E, float2* smem, float2* tws,
                          unsigned long long* mbar) {
     constexpr int T = M / kP;
     constexpr int R1 = Sched<M>::R1;
     constexpr int IPC = kBandThreads / T;
-    const Inst in = locate<M>(bp, c);
+    const Inst in = locate<M, EXT>(bp, c);
     const int t = in.t;
     float2* buf = smem + in.il * padded<kSH>(M);
     const int off = in.d.x;
@@ -664,7 +668,7 @@ __device__ __forceinline__ int find_class(const BandSched& sc) {
     return c;
 }
 
-template <bool SLICED>
+template <bool SLICED, bool EXT>
 __global__ void __launch_bounds__(kBandThreads, kBandMinBlocks)
 bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant__ BandParams bp,
                  CoefPtr out) {
@@ -677,11 +681,11 @@ bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant
     auto run = [&](auto Mc) {
         constexpr int M = decltype(Mc)::value;
         if (kind == kSide)
-            band_fwd<M, SLICED, kSide>(X, tab, bp, c, out, smem, tws, &mbar);
+            band_fwd<M, SLICED, kSide, EXT>(X, tab, bp, c, out, smem, tws, &mbar);
         else if (kind == kOctavePruned)
-            band_fwd<M, SLICED, kOctavePruned>(X, tab, bp, c, out, smem, tws, &mbar);
+            band_fwd<M, SLICED, kOctavePruned, EXT>(X, tab, bp, c, out, smem, tws, &mbar);
         else
-            band_fwd<M, SLICED, kOctave>(X, tab, bp, c, out, smem, tws, &mbar);
+            band_fwd<M, SLICED, kOctave, EXT>(X, tab, bp, c, out, smem, tws, &mbar);
     };
     switch (bp.sc.M[c]) {
     case 2048: run(std::integral_constant<int, 2048>{}); break;
@@ -695,7 +699,7 @@ bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant
     }
 }
 
-template <bool SLICED>
+template <bool SLICED, bool EXT>
 __global__ void __launch_bounds__(kBandThreads, kBandMinBlocks)
 bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ BandParams bp,
                  float2* __restrict__ E) {
@@ -709,11 +713,11 @@ bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ Band
     auto run = [&](auto Mc) {
         constexpr int M = decltype(Mc)::value;
         if (side)
-            band_inv<M, SLICED, kSide>(in, tab, which, bp, c, E, smem, tws, &mbar);
+            band_inv<M, SLICED, kSide, EXT>(in, tab, which, bp, c, E, smem, tws, &mbar);
         else if (M == 2048 && pruned)
-            band_inv<M, SLICED, kOctavePruned>(in, tab, which, bp, c, E, smem, tws, &mbar);
+            band_inv<M, SLICED, kOctavePruned, EXT>(in, tab, which, bp, c, E, smem, tws, &mbar);
         else
-            band_inv<M, SLICED, kOctave>(in, tab, which, bp, c, E, smem, tws, &mbar);
+            band_inv<M, SLICED, kOctave, EXT>(in, tab, which, bp, c, E, smem, tws, &mbar);
     };
     switch (bp.sc.M[c]) {
     case 2048: run(std::integral_constant<int, 2048>{}); break;
@@ -754,10 +758,11 @@ cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParam
                              CoefPtr out, cudaStream_t s) {
     const int grid = bp.sc.cta0[bp.sc.ncls];
     if (grid <= 0) return cudaSuccess;
+    auto go = [&](auto kern) { kern<<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bp, out); };
     if (bp.sl.S > 0)
-        bands_fwd_kernel<true><<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bp, out);
+        bp.ext ? go(bands_fwd_kernel<true, true>) : go(bands_fwd_kernel<true, false>);
     else
-        bands_fwd_kernel<false><<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bp, out);
+        bp.ext ? go(bands_fwd_kernel<false, true>) : go(bands_fwd_kernel<false, false>);
     return cudaGetLastError();
 }
 
@@ -765,10 +770,11 @@ cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const Ban
                              float2* E, cudaStream_t s) {
     const int grid = bp.sc.cta0[bp.sc.ncls];
     if (grid <= 0) return cudaSuccess;
+    auto go = [&](auto kern) { kern<<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E); };
     if (bp.sl.S > 0)
-        bands_inv_kernel<true><<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E);
+        bp.ext ? go(bands_inv_kernel<true, true>) : go(bands_inv_kernel<true, false>);
     else
-        bands_inv_kernel<false><<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E);
+        bp.ext ? go(bands_inv_kernel<false, true>) : go(bands_inv_kernel<false, false>);
     return cudaGetLastError();
 }
 
@@ -777,8 +783,14 @@ cudaError_t read_wait_timeouts(unsigned* count) {
 }
 
 cudaError_t init_band_attributes() {
-    const void* fns[] = {(const void*)bands_fwd_kernel<false>, (const void*)bands_fwd_kernel<true>,
-                         (const void*)bands_inv_kernel<false>, (const void*)bands_inv_kernel<true>};
+    const void* fns[] = {(const void*)bands_fwd_kernel<false, false>,
+                         (const void*)bands_fwd_kernel<true, false>,
+                         (const void*)bands_inv_kernel<false, false>,
+                         (const void*)bands_inv_kernel<true, false>,
+                         (const void*)bands_fwd_kernel<false, true>,
+                         (const void*)bands_fwd_kernel<true, true>,
+                         (const void*)bands_inv_kernel<false, true>,
+                         (const void*)bands_inv_kernel<true, true>};
     for (const void* f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kBandSmem);

@@ -28,7 +28,8 @@ struct cqt_tables {
     FwdTab fwd[2];   // 0 analysis, 1 transpose of synthesis
     InvTab inv[2];   // 0 synthesis, 1 transpose of analysis
     const float2* tw2048;
-    int4 desc[kMaxBands];   // class order, see BandParams
+    const int4* desc;       // device copy in the blob, class order, see BandParams
+    int4 desc_host[kInlineBands];   // the inline head of the same array
     int ngroups;
     int group_count[kMaxGroups], group_len[kMaxGroups], group_roll[kMaxGroups];
     SpecTables spec;
@@ -109,7 +110,10 @@ BandParams band_params(const cqt_tables* t, int batch) {
     bp.sc = make_sched(t->ncls, t->cls_M, t->cls_nb, t->cls_first, t->cls_kind, batch);
     bp.tw2048 = t->tw2048;
     bp.ncoef = t->ncoef;
-    std::memcpy(bp.desc, t->desc, sizeof bp.desc);
+    bp.desc = t->desc;
+    bp.ext = t->nbands > kInlineBands;
+    std::memcpy(bp.desc_inline, t->desc_host,
+                sizeof(int4) * (t->nbands < kInlineBands ? t->nbands : kInlineBands));
     bp.sl = SliceLayout{};
     return bp;
 }
@@ -438,6 +442,16 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
         qm_aa[n] = b;
     }
     size_t i_qsy = add(qm_sy.data(), qm_sy.size() * 2), i_qaa = add(qm_aa.data(), qm_aa.size() * 2);
+    // band descriptors in class order (see BandParams)
+    std::vector<int4> desc(h->nbands);
+    for (int i = 0; i < h->nbands; ++i) {
+        const int b = order[i];
+        const int32_t* g = h->band_geom + 4 * b;
+        const bool side = g[3] & 1;
+        desc[i] = make_int4(h->band_off[b], side ? b : g[0], g[1] | (g[2] << 16),
+                            (g[3] & 0xFFF) | (band_group[b] << 12) | (band_row[b] << 16));
+    }
+    size_t i_desc = add(desc.data(), desc.size() * sizeof(int4));
     size_t i_tw = add(h->tw2048, 2048 * 8), i_hi = add(h->tw_hi, 256 * 8), i_lo = add(h->tw_lo, 256 * 8);
     std::vector<float2> rows(spectrum_twiddle_count());
     spectrum_twiddle_rows(rows.data());
@@ -492,13 +506,8 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
         t->group_roll[g] = h->group_roll[g] ? 1 : 0;
         t->group_len[g] = band_M[group_first[g]];
     }
-    for (int i = 0; i < h->nbands; ++i) {
-        const int b = order[i];
-        const int32_t* g = h->band_geom + 4 * b;
-        const bool side = g[3] & 1;
-        t->desc[i] = make_int4(h->band_off[b], side ? b : g[0], g[1] | (g[2] << 16),
-                               (g[3] & 0xFFF) | (band_group[b] << 12) | (band_row[b] << 16));
-    }
+    t->desc = (const int4*)P(i_desc);
+    for (int i = 0; i < h->nbands && i < kInlineBands; ++i) t->desc_host[i] = desc[i];
     t->spec = SpecTables{(const float2*)P(i_hi), (const float2*)P(i_lo), (const float2*)P(i_rows)};
     t->max_planes = h->sy_nplanes > h->aa_nplanes ? h->sy_nplanes : h->aa_nplanes;
     t->blob = blob;

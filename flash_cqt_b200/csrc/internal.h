@@ -39,9 +39,8 @@ struct BandSched {         // CTA ranges of the block-length classes for one lau
     float inv_batch;           // 1 / batch, for the instance -> (band, slice) split
 };
 
-// band descriptors travel in the kernel parameters (8 KB at 512 bands; the
-// limit for kernel parameters is 32,764 bytes)
 constexpr int kMaxBands = 512;
+constexpr int kInlineBands = 160;
 constexpr int kMaxGroups = 16;
 
 // Coefficient layout of the sliced transform: one interleaved complex buffer
@@ -86,9 +85,16 @@ struct BandParams {
     const float2* tw2048;  // W_2048^e, forward sign
     int ncoef;
     // per band in class order: {heap offset, lo (octave) | band id (side),
-    // l | Lg << 16, flags: bit 0 side band, bits 4-7 synthesis plane,
-    // bits 8-11 adjoint plane, bits 12-15 group, bits 16-23 row in group}
-    int4 desc[kMaxBands];
+    // l | Lg << 16, flags: bit 0 side band, bits 4-7 synthesis plane, bits
+    // 8-11 adjoint plane, bits 12-15 group, bits 16-23 row in group}.  The
+    // descriptors of a bank of at most kInlineBands bands ride in the kernel
+    // parameters (constant bank, no dependent global load before a CTA's
+    // first copy); larger banks run a kernel instantiation that reads them
+    // from device memory (desc).  2.5 KB of parameters rather than 8 KB keeps
+    // eager launches cheap.
+    int4 desc_inline[kInlineBands];
+    const int4* desc;
+    int ext;               // more than kInlineBands bands: read desc
     SliceLayout sl;
 };
 

@@ -43,6 +43,7 @@ class Engine:
         assert self.tables.ncoef == self.ncoef
         self._ws = None
         self._ws_retired = []   # outgrown workspaces, kept alive (see workspace())
+        self._ws_need = {}      # batch -> bytes
 
     @classmethod
     def from_params(cls, num_octs, bins_per_oct, fs, audio_len, device=None):
@@ -54,7 +55,9 @@ class Engine:
         """grow-only scratch shared by the calls on this engine.  An outgrown
         buffer is retired, not freed: a CUDA graph captured earlier may still
         address it (Graphed, HostPipeline, the streaming graphs)."""
-        need = self.tables.workspace_bytes(batch)
+        need = self._ws_need.get(batch)
+        if need is None:
+            need = self._ws_need[batch] = self.tables.workspace_bytes(batch)
         if self._ws is None or self._ws.numel() < need:
             if self._ws is not None:
                 self._ws_retired.append(self._ws)
@@ -95,10 +98,12 @@ class Engine:
         return re.contiguous(), im.contiguous()
 
     def _run(self, name, a, b, c, layout, batch):
-        with torch.cuda.device(self.dev):
-            ws = self.workspace(batch)
-            self.tables.call(name, a, b, c, layout, batch, ws.data_ptr(), ws.numel(),
-                             self._stream())
+        if torch.cuda.current_device() != self.dev.index:
+            with torch.cuda.device(self.dev):
+                return self._run(name, a, b, c, layout, batch)
+        ws = self.workspace(batch)
+        self.tables.call(name, a, b, c, layout, batch, ws.data_ptr(), ws.numel(),
+                         torch.cuda.current_stream().cuda_stream)
 
     # ----------------------------------------------------------------- complex
     def analysis(self, x, out=None):
