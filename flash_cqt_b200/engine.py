@@ -103,7 +103,7 @@ class Engine:
                 return self._run(name, a, b, c, layout, batch)
         ws = self.workspace(batch)
         self.tables.call(name, a, b, c, layout, batch, ws.data_ptr(), ws.numel(),
-                         torch.cuda.current_stream().cuda_stream)
+                         _raw_stream_of(self.dev.index))
 
     # ----------------------------------------------------------------- complex
     def analysis(self, x, out=None):
@@ -163,6 +163,17 @@ class Engine:
 
 def ctypes_stream(stream):
     return int(stream.cuda_stream)
+
+
+def _raw_stream_of(index):
+    """cudaStream_t of the current stream on device `index` (the fast torch
+    accessor where present)"""
+    return torch.cuda.current_stream(index).cuda_stream
+
+
+_raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+if _raw is not None:
+    _raw_stream_of = _raw   # noqa: F811 -- same result, without a Stream object
 
 
 class SlicedEngine:

@@ -72,10 +72,12 @@ class TrainableCQT:
         self.gspec = cqt.heap.gspec
         self.ncoef = cqt.heap.ncoef
         self.ngroups = len(cqt.heap.groups)
+        self._sizes = [b * M for b, M, _ in self.gspec]
 
     def split(self, h, lead):
         """heap [B, ncoef] complex -> (blocks, side) views with leading dims."""
-        vs = [h[:, off:off + b * M].view(*lead, b, M) for b, M, off in self.gspec]
+        vs = [p.view(*lead, b, M)
+              for p, (b, M, _) in zip(h.split(self._sizes, dim=1), self.gspec)]
         # remembered (weakly: no tensor is kept alive) so that heap_of can
         # recognise them by identity
         self._last = (weakref.ref(h), tuple(weakref.ref(v) for v in vs))
