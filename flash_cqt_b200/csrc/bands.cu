@@ -41,9 +41,11 @@ namespace {
 constexpr int kP = kBandP;
 constexpr int kSH = kP == 32 ? 5 : 4;                    // shared padding shift
 constexpr int kBandData = padded<kSH>(kBandCap);         // float2 per CTA
-// stage-3 twiddles (only M = 2048 has a third radix-2 stage with P = 32) come
-// from the global W_2048 table when FCQT_TW3_SMEM is 0, which keeps a CTA at
-// 75 KB of shared memory so two CTAs fit the 168 KB carveout
+// Build-time tuning switches (defaults are the measured best):
+//   FCQT_TW3_SMEM   stage-3 twiddles as shared rows (1) or from the global
+//                   W_2048 table (0: less shared memory per CTA, faster);
+//   FCQT_TW3_POW    stage-3 twiddles W^k, W^2k, W^4k and their products (1);
+//   FCQT_PREFETCH_GAINS  bands_inv loads its scatter gains before the stages (1).
 #ifndef FCQT_TW3_SMEM
 #define FCQT_TW3_SMEM 0
 #endif
