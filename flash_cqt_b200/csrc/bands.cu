@@ -376,6 +376,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     const int sh = lo & 1;
     if (threadIdx.x == 0) mbar_init(mbar, IPC);
     __syncthreads();
+    pdl_wait();   // the previous kernel of the stream has completed
     if (t == 0) {
         const int a = lo - sh, bytes = n > 0 ? (((lo + n + 1) & ~1) - a) * 8 : 0;
         mbar_arrive_expect(mbar, (unsigned)bytes);
@@ -541,6 +542,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     float* bim = bre + M;
     if (threadIdx.x == 0) mbar_init(mbar, IPC);
     __syncthreads();
+    pdl_wait();   // the previous kernel of the stream has completed
     if (t == 0) {
         mbar_arrive_expect(mbar, bulk ? M * 8 : 0);
         if (bulk) {
@@ -678,6 +680,7 @@ bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant
     __shared__ unsigned long long mbar;
     float2* smem = reinterpret_cast<float2*>(smem_raw);
     float2* tws = smem + kBandData;
+    pdl_launch_dependents();
     const int c = find_class(bp.sc);
     const int kind = bp.sc.kind[c];
     auto run = [&](auto Mc) {
@@ -709,6 +712,7 @@ bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ Band
     __shared__ unsigned long long mbar;
     float2* smem = reinterpret_cast<float2*>(smem_raw);
     float2* tws = smem + kBandData;
+    pdl_launch_dependents();
     const int c = find_class(bp.sc);
     const bool side = bp.sc.kind[c] == kSide;
     const bool pruned = bp.sc.kind[c] == kOctavePruned;
@@ -760,24 +764,26 @@ cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParam
                              CoefPtr out, cudaStream_t s) {
     const int grid = bp.sc.cta0[bp.sc.ncls];
     if (grid <= 0) return cudaSuccess;
-    auto go = [&](auto kern) { kern<<<grid, kBandThreads, kBandSmem, s>>>(X, tab, bp, out); };
+    auto go = [&](auto kern) {
+        return launch_pdl(bp.sc.batch <= kPdlMaxBatch, kern, dim3(grid), dim3(kBandThreads),
+                          kBandSmem, s, X, tab, bp, out);
+    };
     if (bp.sl.S > 0)
-        bp.ext ? go(bands_fwd_kernel<true, true>) : go(bands_fwd_kernel<true, false>);
-    else
-        bp.ext ? go(bands_fwd_kernel<false, true>) : go(bands_fwd_kernel<false, false>);
-    return cudaGetLastError();
+        return bp.ext ? go(bands_fwd_kernel<true, true>) : go(bands_fwd_kernel<true, false>);
+    return bp.ext ? go(bands_fwd_kernel<false, true>) : go(bands_fwd_kernel<false, false>);
 }
 
 cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const BandParams& bp,
                              float2* E, cudaStream_t s) {
     const int grid = bp.sc.cta0[bp.sc.ncls];
     if (grid <= 0) return cudaSuccess;
-    auto go = [&](auto kern) { kern<<<grid, kBandThreads, kBandSmem, s>>>(in, tab, which, bp, E); };
+    auto go = [&](auto kern) {
+        return launch_pdl(bp.sc.batch <= kPdlMaxBatch, kern, dim3(grid), dim3(kBandThreads),
+                          kBandSmem, s, in, tab, which, bp, E);
+    };
     if (bp.sl.S > 0)
-        bp.ext ? go(bands_inv_kernel<true, true>) : go(bands_inv_kernel<true, false>);
-    else
-        bp.ext ? go(bands_inv_kernel<false, true>) : go(bands_inv_kernel<false, false>);
-    return cudaGetLastError();
+        return bp.ext ? go(bands_inv_kernel<true, true>) : go(bands_inv_kernel<true, false>);
+    return bp.ext ? go(bands_inv_kernel<false, true>) : go(bands_inv_kernel<false, false>);
 }
 
 cudaError_t read_wait_timeouts(unsigned* count) {

@@ -271,8 +271,10 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     const int h = blockIdx.x & 1;
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
+    pdl_launch_dependents();
     load_tables<C>(hl, tws, ghi, glo, gtw);
     __syncthreads();
+    pdl_wait();   // the previous kernel of the stream has completed
     const Tw64k tw{hl, hl + 256};
 
     // stage 1 inputs straight from global: the radix-2 DIF split of z
@@ -371,8 +373,10 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     float2* peer = cl.map_shared_rank(buf, h ^ 1);
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
+    pdl_launch_dependents();
     load_tables<C>(hl, tws, ghi, glo, gtw);
     cl.sync();   // tables staged, and the partner is running (its buffer may be written)
+    pdl_wait();  // the previous kernel of the stream has completed
     const Tw64k tw{hl, hl + 256};
     const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
     const bool two = nplanes > 1;
@@ -562,12 +566,10 @@ cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& s
     if (batch <= 0) return cudaSuccess;
     const int ahead = wave_ctas();
     if (in.S > 0)
-        spectrum_fwd_kernel<true><<<2 * batch, CF::T, smemOf<CF>(), s>>>(
-            in, X, st.hi, st.lo, st.rows, ahead);
-    else
-        spectrum_fwd_kernel<false><<<2 * batch, CF::T, smemOf<CF>(), s>>>(
-            in, X, st.hi, st.lo, st.rows, ahead);
-    return cudaGetLastError();
+        return launch_pdl(batch <= kPdlMaxBatch, spectrum_fwd_kernel<true>, dim3(2 * batch), dim3(CF::T), smemOf<CF>(), s,
+                          in, X, st.hi, st.lo, st.rows, ahead);
+    return launch_pdl(batch <= kPdlMaxBatch, spectrum_fwd_kernel<false>, dim3(2 * batch), dim3(CF::T), smemOf<CF>(), s,
+                      in, X, st.hi, st.lo, st.rows, ahead);
 }
 
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
@@ -575,12 +577,10 @@ cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap
     if (batch <= 0) return cudaSuccess;
     const int ahead = wave_ctas();
     if (out.S > 0)
-        spectrum_inv_kernel<true><<<2 * batch, CI::T, smemOf<CI>(), s>>>(
-            E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
-    else
-        spectrum_inv_kernel<false><<<2 * batch, CI::T, smemOf<CI>(), s>>>(
-            E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
-    return cudaGetLastError();
+        return launch_pdl(batch <= kPdlMaxBatch, spectrum_inv_kernel<true>, dim3(2 * batch), dim3(CI::T), smemOf<CI>(), s,
+                          E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
+    return launch_pdl(batch <= kPdlMaxBatch, spectrum_inv_kernel<false>, dim3(2 * batch), dim3(CI::T), smemOf<CI>(), s,
+                      E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
 }
 
 cudaError_t init_spectrum_attributes() {
