@@ -220,7 +220,15 @@ class DeviceTables:
                                       ws_bytes, stream), "cqt_launch_stage")
 
     def sliced(self, name, *args):
-        _check(getattr(lib(), name)(self.handle, *args), name)
+        fns = self.__dict__.get("_sfns")
+        if fns is None:   # bound once: no library lock on the per-call path
+            L = lib()
+            fns = self._sfns = {n: getattr(L, n) for n in
+                                ("cqt_sliced_analysis", "cqt_sliced_synthesis",
+                                 "cqt_sliced_adj_analysis", "cqt_sliced_adj_synthesis")}
+        rc = fns[name](self.handle, *args)
+        if rc != 0:
+            _check(rc, name)
 
     def __del__(self):
         h = getattr(self, "handle", None)

@@ -154,27 +154,46 @@ __device__ __forceinline__ void spec_stages(float2 (&v)[C::P], float2* buf, cons
 
 // one packed input pair z[n] = (sample 2n, sample 2n + 1) of slice g
 struct SliceReader {
-    const float* row;      // buffer row (sliced) or slice base (contiguous)
-    long long p0;          // global sample of slice position 0 (sliced)
-    long long lo, hi;      // readable global samples [lo, hi)
-    long long sample0;     // global sample of row[0]
+    const float* at;       // sliced: row element of slice position 0 (may lie
+                           // outside the row; only [jl, jh) is read); else the slice
+    int jl, jh;            // readable slice positions [jl, jh) (sliced)
     int shift;             // +-H
     const float* window;
     bool sliced;
+    bool whole;            // sliced, every position readable, row and window
+                           // 8-byte aligned at even positions: float2 loads
     __device__ __forceinline__ float2 operator()(int n) const {
-        if (!sliced) return __ldg(reinterpret_cast<const float2*>(row) + n);
+        if (!sliced) return __ldg(reinterpret_cast<const float2*>(at) + n);
         const int j = (2 * n + shift) & (kSlice - 1);
-        const long long p = p0 + j;
         float2 v;
-        v.x = (p >= lo && p < hi) ? __ldg(row + (p - sample0)) : 0.f;
-        v.y = (p + 1 >= lo && p + 1 < hi) ? __ldg(row + (p + 1 - sample0)) : 0.f;
+        v.x = (j >= jl && j < jh) ? __ldg(at + j) : 0.f;
+        v.y = (j + 1 >= jl && j + 1 < jh) ? __ldg(at + j + 1) : 0.f;
         if (window) {
             v.x *= __ldg(window + j);
             v.y *= __ldg(window + j + 1);
         }
         return v;
     }
+    // the same value when `whole` holds
+    __device__ __forceinline__ float2 pair(int n) const {
+        const int j = (2 * n + shift) & (kSlice - 1);
+        float2 v = __ldg(reinterpret_cast<const float2*>(at + j));
+        if (window) {
+            const float2 w = __ldg(reinterpret_cast<const float2*>(window + j));
+            v.x *= w.x;
+            v.y *= w.y;
+        }
+        return v;
+    }
 };
+
+// a float row indexed by global sample (row base - sample0) and the window
+// both 8-byte aligned, so that even global samples start float2 pairs
+__device__ __forceinline__ bool pairs_aligned(const float* row, long long sample0,
+                                              const float* window) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(row) - (uintptr_t)(sample0 * 4);
+    return ((a | reinterpret_cast<uintptr_t>(window)) & 7u) == 0;
+}
 
 // global sample range a buffer row can hold: [max(0, sample0), min(length, sample0 + count))
 __device__ __forceinline__ void sample_range(const SigMap& m, long long& lo, long long& hi) {
@@ -182,24 +201,32 @@ __device__ __forceinline__ void sample_range(const SigMap& m, long long& lo, lon
     hi = m.sample0 + m.count < m.length ? m.sample0 + m.count : m.length;
 }
 
+__device__ __forceinline__ int clamp_slice(long long v) {
+    return v < 0 ? 0 : (v > kSlice ? kSlice : (int)v);
+}
+
 template <bool SLICED>
 __device__ __forceinline__ SliceReader make_reader(const SigMap& m, long long g) {
     SliceReader r;
     r.sliced = SLICED;
     r.window = m.window;
+    r.whole = false;
     if constexpr (!SLICED) {
-        r.row = m.x + g * kSlice;
-        r.p0 = 0;
-        r.lo = r.hi = r.sample0 = 0;
+        r.at = m.x + g * kSlice;
+        r.jl = r.jh = 0;
         r.shift = 0;
     } else {
         const long long row = g / m.S;
         const int sg = m.slice0 + (int)(g % m.S);
-        r.row = m.x + row * m.ld;
-        r.p0 = 2LL * kQuarter * (sg - 1);
-        sample_range(m, r.lo, r.hi);
-        r.sample0 = m.sample0;
+        const float* rp = m.x + row * m.ld;
+        const long long p0 = 2LL * kQuarter * (sg - 1);   // global sample of position 0
+        long long lo, hi;
+        sample_range(m, lo, hi);
+        r.jl = clamp_slice(lo - p0);
+        r.jh = clamp_slice(hi - p0);
+        r.at = rp + (p0 - m.sample0);
         r.shift = (sg & 1) ? -kQuarter : kQuarter;
+        r.whole = r.jl == 0 && r.jh == kSlice && pairs_aligned(rp, m.sample0, r.window);
     }
     return r;
 }
@@ -280,15 +307,22 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     // stage 1 inputs straight from global: the radix-2 DIF split of z
     const SliceReader z = make_reader<SLICED>(in, slice);
     float2 v[P];
+    auto load = [&](auto&& zf) {
 #pragma unroll
-    for (int b = 0; b < P / C::R1; ++b)
+        for (int b = 0; b < P / C::R1; ++b)
 #pragma unroll
-        for (int r = 0; r < C::R1; ++r) {
-            const int n = t + T * b + r * (kQuarter / C::R1);
-            const float2 a = z(n);
-            const float2 c = z(n + kQuarter);
-            v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
-        }
+            for (int r = 0; r < C::R1; ++r) {
+                const int n = t + T * b + r * (kQuarter / C::R1);
+                const float2 a = zf(n);
+                const float2 c = zf(n + kQuarter);
+                v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
+            }
+    };
+    // one uniform branch, each side a straight run of loads
+    if (SLICED && z.whole)
+        load([&](int n) { return z.pair(n); });
+    else
+        load(z);
     spec_compute<C, 1, -1>(v, t, tws);   // consumes the loads
     if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
         const long nb = blockIdx.x + (long)ahead;
@@ -483,6 +517,9 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
         const float* wnd = out.window;
         long long lo, hi;
         sample_range(out, lo, hi);
+        // aligned rows take one two-lane vector atomic per pair (each lane
+        // still receives exactly two terms)
+        const bool vec = pairs_aligned(out.y + row * out.ld, out.sample0, wnd);
         spec_stages<C, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
             constexpr int R = sR<C>(C::NST), NS = sNS<C>(C::NST);
 #pragma unroll
@@ -493,12 +530,18 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
                     float2 val = cscale(w[b * R + r], inv);
                     const int j = (2 * (2 * nn + h) + shift) & (kSlice - 1);
                     if (wnd) {
-                        val.x *= __ldg(wnd + j);
-                        val.y *= __ldg(wnd + j + 1);
+                        const float2 wj = vec ? __ldg(reinterpret_cast<const float2*>(wnd + j))
+                                              : make_float2(__ldg(wnd + j), __ldg(wnd + j + 1));
+                        val.x *= wj.x;
+                        val.y *= wj.y;
                     }
                     const long long p = p0 + j;
-                    if (p >= lo && p < hi) atomicAdd(yr + p, val.x);
-                    if (p + 1 >= lo && p + 1 < hi) atomicAdd(yr + p + 1, val.y);
+                    if (vec && p >= lo && p + 1 < hi) {
+                        atomicAdd(reinterpret_cast<float2*>(yr + p), val);
+                    } else {
+                        if (p >= lo && p < hi) atomicAdd(yr + p, val.x);
+                        if (p + 1 >= lo && p + 1 < hi) atomicAdd(yr + p + 1, val.y);
+                    }
                 }
         });
     }

@@ -207,13 +207,10 @@ class SlicedEngine:
         rows = 1
         for d in lead:
             rows *= d
-        out, off = [], 0
         ngo = len(self.eng.heap.groups)
-        for gi, (b, M, _) in enumerate(self.gspec):
-            n = rows * S * b * M
-            v = buf[off:off + n]
-            out.append(v.view(*lead, b, S * M) if gi < ngo else v.view(*lead, S, 1, M))
-            off += n
+        sizes = [rows * S * b * M for b, M, _ in self.gspec]
+        out = [v.view(*lead, b, S * M) if gi < ngo else v.view(*lead, S, 1, M)
+               for gi, (v, (b, M, _)) in enumerate(zip(buf.split(sizes), self.gspec))]
         return out[:ngo], out[ngo:]
 
     def _sig(self, x, name):
@@ -224,8 +221,10 @@ class SlicedEngine:
         return x
 
     def _call(self, name, *args):
-        with torch.cuda.device(self.eng.dev):
-            self.eng.tables.sliced(name, *args)
+        if torch.cuda.current_device() != self.eng.dev.index:
+            with torch.cuda.device(self.eng.dev):
+                return self.eng.tables.sliced(name, *args)
+        self.eng.tables.sliced(name, *args)
 
     def _slices(self, rows, slice0, S, window):
         return self.N.CqtSlices(rows, slice0, S, window.data_ptr() if window is not None else None)
@@ -249,7 +248,7 @@ class SlicedEngine:
                               device=self.eng.dev)
         if ws is None:
             ws = self.eng.workspace(rows * S)
-        stream = int(torch.cuda.current_stream(self.eng.dev).cuda_stream)
+        stream = _raw_stream_of(self.eng.dev.index)
         sig = self._signal(x, sample0, length)
         if adjoint_of_synthesis:
             sl = self._slices(rows, slice0, S, None)
@@ -277,7 +276,7 @@ class SlicedEngine:
             out = torch.empty(rows, count, dtype=torch.float32, device=self.eng.dev)
         if ws is None:
             ws = self.eng.workspace(rows * S)
-        stream = int(torch.cuda.current_stream(self.eng.dev).cuda_stream)
+        stream = _raw_stream_of(self.eng.dev.index)
         sig = self._signal(out, sample0, length)
         if adjoint_of_analysis:
             sl = self._slices(rows, slice0, S, self.window)

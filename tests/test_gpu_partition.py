@@ -119,3 +119,41 @@ def test_nccl_ranks_match_whole_stream(dev):
     x = _signal(dev)
     want = sl.bwd(*sl.fwd(x), length=L).cpu().numpy()
     np.testing.assert_array_equal(y, want)
+
+
+def test_unaligned_rows_and_offsets_agree_bitwise(dev):
+    """Rows whose global sample 0 is not 8-byte aligned (odd sample0, odd row
+    stride, odd element offset) take the scalar loads and single-lane atomics;
+    aligned rows take float2 loads and two-lane atomics.  Both must give the
+    same bits for the same slices."""
+    from flash_cqt_b200 import SlicedCQT
+    sl = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
+    se = sl._fused(dev)
+    H2 = sl.hop
+    x = _signal(dev).view(2, L)
+    S = se.count(L)
+    ref = se.analysis(x, S)
+    rb, rs = se.group_views(ref, (2,), S)
+    s0, n = 3, 4
+    a, b = H2 * (s0 - 1) - 1, H2 * (s0 + n + 1) + 1      # odd first sample
+    ld = (b - a) + 3                                       # odd row stride
+    store = torch.zeros(2 * ld + 4, device=dev)
+    xw = store[1:1 + 2 * ld].view(2, ld)[:, :b - a]        # row 0 misaligned, row 1 not
+    xw.copy_(x[:, a:b])
+    buf = se.analysis(xw, n, slice0=s0, sample0=a, length=L)
+    bb, bs = se.group_views(buf, (2,), n)
+    for c, full, m in zip(bb, rb, sl.size_per_oct):
+        assert torch.equal(c, full[..., s0 * m:(s0 + n) * m])
+    for c, full in zip(bs, rs):
+        assert torch.equal(c, full[:, s0:s0 + n])
+    # synthesis and the windowed adjoint into aligned and misaligned rows
+    lo, hi = H2 * (s0 - 1), H2 * (s0 + n)
+    for adj in (False, True):
+        ya = se.synthesis(buf, 2, n, L, slice0=s0, sample0=lo, count=hi - lo,
+                          adjoint_of_analysis=adj)
+        outs = torch.full((2 * ld + 4,), 7.0, device=dev)
+        yu = outs[1:1 + 2 * ld].view(2, ld)[:, :hi - lo + 2]
+        se.synthesis(buf, 2, n, L, out=yu, slice0=s0, sample0=lo - 1,
+                     count=hi - lo + 2, adjoint_of_analysis=adj)
+        assert torch.equal(yu[:, 1:1 + hi - lo], ya)
+        assert torch.all(yu[:, 0] == 0) and torch.all(yu[:, -1] == 0)
