@@ -92,8 +92,22 @@ __device__ __forceinline__ void static_for(F&& f) {
     }
 }
 
+// Complex add and subtract as sm_100 packed two-lane fp32 instructions (one
+// instruction for both components; each lane rounds as the scalar operation,
+// and a - b is formed exactly as b * -1 + a).  FCQT_F32X2=0 builds the scalar
+// forms.
+#ifndef FCQT_F32X2
+#define FCQT_F32X2 1
+#endif
+#if FCQT_F32X2
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) {
+    return __ffma2_rn(b, make_float2(-1.f, -1.f), a);
+}
+#else
 __device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
 __device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+#endif
 __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
     return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
 }
@@ -109,6 +123,19 @@ template <int S>
 __device__ __forceinline__ float2 mul_si(float2 a) {
     if constexpr (S < 0) return make_float2(a.y, -a.x);
     else return make_float2(-a.y, a.x);
+}
+
+// y1 = t + S i d and y3 = t - S i d, per component (the swap and the signs
+// fold into scalar adds)
+template <int S>
+__device__ __forceinline__ void rot_pair(float2 t, float2 d, float2& y1, float2& y3) {
+    if constexpr (S < 0) {
+        y1 = make_float2(t.x + d.y, t.y - d.x);
+        y3 = make_float2(t.x - d.y, t.y + d.x);
+    } else {
+        y1 = make_float2(t.x - d.y, t.y + d.x);
+        y3 = make_float2(t.x + d.y, t.y - d.x);
+    }
 }
 
 // multiply by the compile-time twiddle W_R^E = exp(S 2 pi i E / R)
@@ -162,11 +189,10 @@ __device__ __forceinline__ void dft(float2 (&v)[P]) {
     } else if constexpr (R == 4) {
         float2 x0 = v[B0], x1 = v[B0 + STRIDE], x2 = v[B0 + 2 * STRIDE], x3 = v[B0 + 3 * STRIDE];
         float2 t0 = cadd(x0, x2), t1 = csub(x0, x2);
-        float2 t2 = cadd(x1, x3), t3 = mul_si<S>(csub(x1, x3));
+        float2 t2 = cadd(x1, x3), d = csub(x1, x3);
         v[B0] = cadd(t0, t2);
         v[B0 + 2 * STRIDE] = csub(t0, t2);
-        v[B0 + STRIDE] = cadd(t1, t3);
-        v[B0 + 3 * STRIDE] = csub(t1, t3);
+        rot_pair<S>(t1, d, v[B0 + STRIDE], v[B0 + 3 * STRIDE]);
     } else {
         // R = R1 * R2, input n = R2 n1 + n2, output k = k1 + R1 k2
         constexpr int R1 = Split<R>::R1, R2 = Split<R>::R2;
@@ -256,12 +282,17 @@ __device__ __forceinline__ void dftz(float2 (&v)[P]) {
         const float2 x0 = v[B0], x1 = v[B0 + STRIDE], x2 = v[B0 + 2 * STRIDE],
                      x3 = v[B0 + 3 * STRIDE];
         const float2 t0 = zadd<z0, z2>(x0, x2), t1 = zsub<z0, z2>(x0, x2);
-        const float2 t2 = zadd<z1, z3>(x1, x3), t3 = mul_si<S>(zsub<z1, z3>(x1, x3));
+        const float2 t2 = zadd<z1, z3>(x1, x3), d = zsub<z1, z3>(x1, x3);
         constexpr bool zt0 = z0 && z2, zt2 = z1 && z3;
         v[B0] = zadd<zt0, zt2>(t0, t2);
         v[B0 + 2 * STRIDE] = zsub<zt0, zt2>(t0, t2);
-        v[B0 + STRIDE] = zadd<zt0, zt2>(t1, t3);
-        v[B0 + 3 * STRIDE] = zsub<zt0, zt2>(t1, t3);
+        if constexpr (!zt0 && !zt2) {
+            rot_pair<S>(t1, d, v[B0 + STRIDE], v[B0 + 3 * STRIDE]);
+        } else {
+            const float2 t3 = mul_si<S>(d);
+            v[B0 + STRIDE] = zadd<zt0, zt2>(t1, t3);
+            v[B0 + 3 * STRIDE] = zsub<zt0, zt2>(t1, t3);
+        }
     } else {
         constexpr int R1 = Split<R>::R1, R2 = Split<R>::R2;
         static_assert(R1 * R2 == R && R1 > 1, "unsupported radix");
