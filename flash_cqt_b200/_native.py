@@ -127,6 +127,42 @@ def wait_timeouts():
     return int(n.value)
 
 
+_torchops = None
+_torchops_tried = False
+
+
+def torch_ops():
+    """The torch fast path (``_lib/_torchops*.so``, built from
+    ``csrc/torch_ops.cpp`` by ``flash_cqt_b200.build``): the whole-slice entry
+    points and TrainableCQT's autograd functions in C++, calling this
+    library's entry points.  None when it is not built or
+    ``FLASH_CQT_B200_TORCH_OPS=0``; the ctypes path then serves every call
+    (the same CUDA kernels either way)."""
+    global _torchops, _torchops_tried
+    if _torchops_tried:
+        return _torchops
+    with _lock:
+        if not _torchops_tried:
+            _torchops_tried = True
+            if os.environ.get("FLASH_CQT_B200_TORCH_OPS", "1") != "0":
+                import importlib.util
+                import sysconfig
+                import torch  # noqa: F401  (its libraries resolve the module's)
+                path = LIB_PATH.parent / ("_torchops" + sysconfig.get_config_var("EXT_SUFFIX"))
+                if path.exists():
+                    spec = importlib.util.spec_from_file_location("flash_cqt_b200._torchops",
+                                                                  str(path))
+                    mod = importlib.util.module_from_spec(spec)
+                    spec.loader.exec_module(mod)
+                    _torchops = mod
+    return _torchops
+
+
+def fn_address(name):
+    """address of an exported entry point of the library"""
+    return ctypes.cast(getattr(lib(), name), ctypes.c_void_p).value
+
+
 def _check(rc, what):
     if rc != 0:
         msg = lib().cqt_last_error().decode(errors="replace")

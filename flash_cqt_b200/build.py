@@ -73,6 +73,43 @@ def build(force=False, verbose=False, ptxas_info=False, defines=(), lib=None,
     return LIB
 
 
+TORCH_OPS_SRC = CSRC / "torch_ops.cpp"
+
+
+def torch_ops_path():
+    import sysconfig
+    return PKG / "_lib" / ("_torchops" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_torch_ops(force=False, verbose=False):
+    """Compile the torch fast path (``csrc/torch_ops.cpp``, host C++ only)
+    against the installed torch; it calls the CUDA library through function
+    pointers, so it links nothing of ours."""
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension as ce
+    out = torch_ops_path()
+    out.parent.mkdir(parents=True, exist_ok=True)
+    if not force and out.exists() and out.stat().st_mtime >= TORCH_OPS_SRC.stat().st_mtime:
+        return out
+    inc = ce.include_paths(device_type="cuda") + [sysconfig.get_paths()["include"]]
+    libdirs = ce.library_paths(device_type="cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    # the system g++ (not $CXX): exceptions thrown here unwind through torch's
+    # libraries and must share their C++ runtime
+    cxx = shutil.which("g++", path="/usr/bin:/bin") or "g++"
+    cmd = [cxx, "-O3", "-std=c++17", "-fPIC", "-shared",
+           "-DTORCH_EXTENSION_NAME=_torchops", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}",   # default visibility: c10 exception types must match
+           *[f"-I{d}" for d in inc], str(TORCH_OPS_SRC), "-o", str(out),
+           *[f"-L{d}" for d in libdirs], *[f"-Wl,-rpath,{d}" for d in libdirs[:1]],
+           "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python"]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -80,8 +117,12 @@ def main(argv=None):
     ap.add_argument("--ptxas-info", action="store_true")
     ap.add_argument("-D", dest="defines", action="append", default=[])
     ap.add_argument("--lib", default=None)
+    ap.add_argument("--no-torch-ops", action="store_true",
+                    help="skip the torch fast path (host C++)")
     a = ap.parse_args(argv)
     print(build(a.force, a.verbose, a.ptxas_info, a.defines, a.lib))
+    if not a.no_torch_ops and a.lib is None:
+        print(build_torch_ops(a.force, a.verbose))
 
 
 if __name__ == "__main__":

@@ -1,0 +1,312 @@
+// Torch-facing fast path of the CUDA engines: the four whole-slice entry
+// points of the C ABI (cqt_analysis, cqt_synthesis, cqt_adj_analysis,
+// cqt_adj_synthesis) called from C++ with torch's current stream, and
+// TrainableCQT's fwd / bwd as C++ autograd functions whose backward nodes run
+// the transposes without entering Python.  The C-ABI library stays the only
+// place with device code; this module receives its function pointers from the
+// Python loader (no link-time dependency) and only moves tensors in and out.
+//
+// Mirrors trainable.py:141-191 of the reference (TrainableCQT.fwd / bwd: the
+// forward returns per-group complex views, the backward of the analysis is
+// the transpose of the analysis, that of the synthesis the transpose of the
+// synthesis, nothing saved for backward).
+#include <torch/extension.h>
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <cstdint>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace {
+
+constexpr int64_t kN = 65536;
+constexpr int kLayoutComplex = 1;   // CQT_LAYOUT_COMPLEX
+
+// cqt_analysis / cqt_adj_synthesis: signal first
+using FnSignalFirst = int (*)(const void*, const float*, float*, float*, int, int, void*,
+                              size_t, void*);
+// cqt_synthesis / cqt_adj_analysis: coefficients first
+using FnCoefFirst = int (*)(const void*, const float*, const float*, int, float*, int, void*,
+                            size_t, void*);
+using FnWorkspace = size_t (*)(const void*, int);
+using FnLastError = const char* (*)();
+
+// One filterbank's device tables on one device, with a grow-only workspace.
+// Held by intrusive pointer from Python and from every autograd node that
+// may still call it; it keeps the Python owner of the tables alive.
+struct Ops : torch::CustomClassHolder {
+    const void* tables = nullptr;
+    c10::DeviceIndex device = 0;
+    int64_t ncoef = 0;
+    FnSignalFirst an = nullptr, adj_syn = nullptr;
+    FnCoefFirst syn = nullptr, adj_an = nullptr;
+    FnWorkspace ws_bytes = nullptr;
+    FnLastError last_error = nullptr;
+    PyObject* owner = nullptr;         // Python object owning `tables` (strong ref)
+    at::Tensor ws;
+    std::vector<at::Tensor> retired;   // outgrown workspaces: captured graphs may address them
+    std::unordered_map<int64_t, size_t> need;
+    std::vector<int64_t> sizes, bins, lens;   // per group: b * M, b, M
+    int64_t ngroups = 0;                       // octave groups (the rest are side groups)
+    // the heap and views of the last fwd, held weakly, so that bwd can
+    // recognise untouched views by identity
+    c10::weak_intrusive_ptr<c10::TensorImpl, c10::UndefinedTensorImpl> last_h{
+        c10::intrusive_ptr<c10::TensorImpl, c10::UndefinedTensorImpl>()};
+    std::vector<c10::weak_intrusive_ptr<c10::TensorImpl, c10::UndefinedTensorImpl>> last_v;
+
+    ~Ops() override {
+        if (owner && Py_IsInitialized()) {
+            pybind11::gil_scoped_acquire gil;
+            Py_DECREF(owner);
+        }
+    }
+
+    void check(int rc, const char* what) const {
+        if (rc != 0)
+            TORCH_CHECK(false, what, " failed (", rc, "): ", last_error ? last_error() : "");
+    }
+
+    void* workspace(int64_t batch, size_t* bytes) {
+        auto it = need.find(batch);
+        size_t n;
+        if (it == need.end()) {
+            n = ws_bytes(tables, (int)batch);
+            need.emplace(batch, n);
+        } else {
+            n = it->second;
+        }
+        if (!ws.defined() || (size_t)ws.numel() < n) {
+            if (ws.defined()) retired.push_back(ws);
+            ws = at::empty({(int64_t)std::max<size_t>(n, 16)},
+                           at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device));
+        }
+        *bytes = (size_t)ws.numel();
+        return ws.data_ptr();
+    }
+
+    void* stream() const { return at::cuda::getCurrentCUDAStream(device).stream(); }
+
+    at::Tensor signal(const at::Tensor& t, const char* name) const {
+        TORCH_CHECK_VALUE(t.defined() && t.is_cuda() && t.get_device() == device, name,
+                          " must be a tensor on cuda:", (int)device);
+        TORCH_CHECK_TYPE(t.scalar_type() == at::kFloat, name, " must be float32, got ",
+                         t.scalar_type());
+        TORCH_CHECK_VALUE(t.dim() == 2 && t.size(1) == kN, name, " must be [B, ", kN,
+                          "], got ", t.sizes());
+        at::Tensor c = t.contiguous();
+        // the engines move signals as float2 / float4 vectors
+        return (reinterpret_cast<uintptr_t>(c.data_ptr()) & 15u) ? c.clone() : c;
+    }
+
+    at::Tensor coef(const at::Tensor& t, const char* name) const {
+        TORCH_CHECK_VALUE(t.defined() && t.is_cuda() && t.get_device() == device, name,
+                          " must be a tensor on cuda:", (int)device);
+        TORCH_CHECK_TYPE(t.scalar_type() == at::kComplexFloat, name,
+                         " must be complex64, got ", t.scalar_type());
+        TORCH_CHECK_VALUE(t.dim() == 2 && t.size(1) == ncoef, name, " must be [B, ", ncoef,
+                          "], got ", t.sizes());
+        return t.resolve_conj().contiguous();
+    }
+
+    struct DeviceSwitch {   // switches only when the current device differs
+        c10::optional<c10::cuda::CUDAGuard> g;
+        explicit DeviceSwitch(c10::DeviceIndex d) {
+            if (c10::cuda::current_device() != d) g.emplace(d);
+        }
+    };
+
+    at::Tensor analysis(const at::Tensor& x_) {
+        at::Tensor x = signal(x_, "x");
+        DeviceSwitch sw(device);
+        const int64_t B = x.size(0);
+        at::Tensor out = at::empty({B, ncoef}, x.options().dtype(at::kComplexFloat));
+        size_t wb;
+        void* w = workspace(B, &wb);
+        check(an(tables, x.data_ptr<float>(), reinterpret_cast<float*>(out.data_ptr()), nullptr,
+                 kLayoutComplex, (int)B, w, wb, stream()),
+              "cqt_analysis");
+        return out;
+    }
+
+    at::Tensor synthesis(const at::Tensor& c_) {
+        at::Tensor c = coef(c_, "coefficients");
+        DeviceSwitch sw(device);
+        const int64_t B = c.size(0);
+        at::Tensor out = at::empty({B, kN}, c.options().dtype(at::kFloat));
+        size_t wb;
+        void* w = workspace(B, &wb);
+        check(syn(tables, reinterpret_cast<const float*>(c.data_ptr()), nullptr, kLayoutComplex,
+                  out.data_ptr<float>(), (int)B, w, wb, stream()),
+              "cqt_synthesis");
+        return out;
+    }
+
+    at::Tensor adj_analysis(const at::Tensor& g_) {
+        at::Tensor g = coef(g_, "coefficient gradient");
+        DeviceSwitch sw(device);
+        const int64_t B = g.size(0);
+        at::Tensor out = at::empty({B, kN}, g.options().dtype(at::kFloat));
+        size_t wb;
+        void* w = workspace(B, &wb);
+        check(adj_an(tables, reinterpret_cast<const float*>(g.data_ptr()), nullptr,
+                     kLayoutComplex, out.data_ptr<float>(), (int)B, w, wb, stream()),
+              "cqt_adj_analysis");
+        return out;
+    }
+
+    at::Tensor adj_synthesis(const at::Tensor& gy_) {
+        at::Tensor gy = signal(gy_, "signal gradient");
+        DeviceSwitch sw(device);
+        const int64_t B = gy.size(0);
+        at::Tensor out = at::empty({B, ncoef}, gy.options().dtype(at::kComplexFloat));
+        size_t wb;
+        void* w = workspace(B, &wb);
+        check(adj_syn(tables, gy.data_ptr<float>(), reinterpret_cast<float*>(out.data_ptr()),
+                      nullptr, kLayoutComplex, (int)B, w, wb, stream()),
+              "cqt_adj_synthesis");
+        return out;
+    }
+};
+
+Ops* ops_of(const torch::autograd::AutogradContext* ctx) {
+    return static_cast<Ops*>(ctx->saved_data.at("ops").toCapsule().get());
+}
+
+// analysis with the transpose of the analysis as its backward
+struct AnalysisFn : public torch::autograd::Function<AnalysisFn> {
+    static at::Tensor forward(torch::autograd::AutogradContext* ctx, const at::Tensor& x,
+                              const c10::intrusive_ptr<Ops>& ops) {
+        ctx->saved_data["ops"] = c10::IValue::make_capsule(ops);
+        return ops->analysis(x);
+    }
+    static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                   torch::autograd::variable_list g) {
+        if (!g[0].defined()) return {at::Tensor(), at::Tensor()};
+        return {ops_of(ctx)->adj_analysis(g[0]), at::Tensor()};
+    }
+};
+
+// synthesis with the transpose of the synthesis as its backward
+struct SynthesisFn : public torch::autograd::Function<SynthesisFn> {
+    static at::Tensor forward(torch::autograd::AutogradContext* ctx, const at::Tensor& c,
+                              const c10::intrusive_ptr<Ops>& ops) {
+        ctx->saved_data["ops"] = c10::IValue::make_capsule(ops);
+        return ops->synthesis(c);
+    }
+    static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                   torch::autograd::variable_list g) {
+        if (!g[0].defined()) return {at::Tensor(), at::Tensor()};
+        return {ops_of(ctx)->adj_synthesis(g[0]), at::Tensor()};
+    }
+};
+
+// Python handle of an Ops
+struct Handle {
+    c10::intrusive_ptr<Ops> ops;
+
+    Handle(uintptr_t tables, int device, int64_t ncoef, uintptr_t an, uintptr_t syn,
+           uintptr_t adj_an, uintptr_t adj_syn, uintptr_t ws_bytes, uintptr_t last_error,
+           pybind11::object owner, std::vector<int64_t> bins, std::vector<int64_t> lens,
+           int64_t ngroups)
+        : ops(c10::make_intrusive<Ops>()) {
+        TORCH_CHECK(bins.size() == lens.size() && ngroups <= (int64_t)bins.size(),
+                    "bad group layout");
+        Ops& o = *ops;
+        o.tables = reinterpret_cast<const void*>(tables);
+        o.device = (c10::DeviceIndex)device;
+        o.ncoef = ncoef;
+        o.an = reinterpret_cast<FnSignalFirst>(an);
+        o.syn = reinterpret_cast<FnCoefFirst>(syn);
+        o.adj_an = reinterpret_cast<FnCoefFirst>(adj_an);
+        o.adj_syn = reinterpret_cast<FnSignalFirst>(adj_syn);
+        o.ws_bytes = reinterpret_cast<FnWorkspace>(ws_bytes);
+        o.last_error = reinterpret_cast<FnLastError>(last_error);
+        o.owner = owner.release().ptr();   // the strong reference moves into Ops
+        int64_t total = 0;
+        for (size_t i = 0; i < bins.size(); ++i) {
+            o.sizes.push_back(bins[i] * lens[i]);
+            total += bins[i] * lens[i];
+        }
+        TORCH_CHECK(total == ncoef, "group layout does not cover the heap");
+        o.bins = std::move(bins);
+        o.lens = std::move(lens);
+        o.ngroups = ngroups;
+    }
+
+    // the grow-only scratch for `batch` slices (shared with ctypes callers)
+    at::Tensor workspace(int64_t batch) {
+        size_t b;
+        ops->workspace(batch, &b);
+        return ops->ws;
+    }
+
+    at::Tensor analysis(const at::Tensor& x) { return ops->analysis(x); }
+    at::Tensor synthesis(const at::Tensor& c) { return ops->synthesis(c); }
+    at::Tensor adj_analysis(const at::Tensor& g) { return ops->adj_analysis(g); }
+    at::Tensor adj_synthesis(const at::Tensor& gy) { return ops->adj_synthesis(gy); }
+
+    // differentiable heap <-> signal, no per-group views
+    at::Tensor analysis_heap(const at::Tensor& x) { return AnalysisFn::apply(x, ops); }
+    at::Tensor synthesis_heap(const at::Tensor& h) { return SynthesisFn::apply(h, ops); }
+
+    // TrainableCQT.fwd: x [..., 65536] -> (blocks [..., b, M], side [..., 1, M])
+    pybind11::tuple fwd(const at::Tensor& x) {
+        Ops& o = *ops;
+        TORCH_CHECK(x.dim() >= 1 && x.size(-1) == kN, "x must be [..., ", kN, "]");
+        std::vector<int64_t> lead(x.sizes().begin(), x.sizes().end() - 1);
+        at::Tensor h = AnalysisFn::apply(x.reshape({-1, kN}), ops);
+        std::vector<at::Tensor> parts = h.split_with_sizes(o.sizes, 1);
+        pybind11::list blocks, side;
+        o.last_v.clear();
+        std::vector<int64_t> shape(lead);
+        shape.push_back(0);
+        shape.push_back(0);
+        for (size_t i = 0; i < parts.size(); ++i) {
+            shape[shape.size() - 2] = o.bins[i];
+            shape[shape.size() - 1] = o.lens[i];
+            at::Tensor v = parts[i].view(shape);
+            o.last_v.emplace_back(v.getIntrusivePtr());
+            if ((int64_t)i < o.ngroups) blocks.append(v);
+            else side.append(v);
+        }
+        o.last_h = c10::weak_intrusive_ptr<c10::TensorImpl, c10::UndefinedTensorImpl>(
+            h.getIntrusivePtr());
+        return pybind11::make_tuple(blocks, side);
+    }
+
+    // the heap behind (blocks, side) when they are the untouched views the last
+    // fwd returned (same tensor objects, the heap still alive), else None
+    pybind11::object last_heap(const std::vector<at::Tensor>& all) {
+        Ops& o = *ops;
+        if (all.size() != o.last_v.size() || o.last_h.expired()) return pybind11::none();
+        for (size_t i = 0; i < all.size(); ++i)
+            if (o.last_v[i].expired() ||
+                all[i].unsafeGetTensorImpl() != o.last_v[i]._unsafe_get_target())
+                return pybind11::none();
+        auto hp = o.last_h.lock();
+        if (!hp) return pybind11::none();
+        return pybind11::cast(at::Tensor(std::move(hp)));
+    }
+};
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.doc() = "torch fast path of the flash_cqt_b200 C ABI";
+    pybind11::class_<Handle>(m, "Handle")
+        .def(pybind11::init<uintptr_t, int, int64_t, uintptr_t, uintptr_t, uintptr_t, uintptr_t,
+                            uintptr_t, uintptr_t, pybind11::object, std::vector<int64_t>,
+                            std::vector<int64_t>, int64_t>())
+        .def("workspace", &Handle::workspace)
+        .def("analysis", &Handle::analysis)
+        .def("synthesis", &Handle::synthesis)
+        .def("adj_analysis", &Handle::adj_analysis)
+        .def("adj_synthesis", &Handle::adj_synthesis)
+        .def("analysis_heap", &Handle::analysis_heap)
+        .def("synthesis_heap", &Handle::synthesis_heap)
+        .def("fwd", &Handle::fwd)
+        .def("last_heap", &Handle::last_heap);
+}

@@ -44,6 +44,19 @@ class Engine:
         self._ws = None
         self._ws_retired = []   # outgrown workspaces, kept alive (see workspace())
         self._ws_need = {}      # batch -> bytes
+        # the C++ fast path over the same entry points (None: ctypes only);
+        # it owns the workspace and keeps the tables alive
+        self._ops = None
+        mod = _native.torch_ops()
+        if mod is not None:
+            ngo = len(heap.groups)
+            self._ops = mod.Handle(
+                self.tables.handle.value, self.dev.index, self.ncoef,
+                *[_native.fn_address(n) for n in (
+                    "cqt_analysis", "cqt_synthesis", "cqt_adj_analysis",
+                    "cqt_adj_synthesis", "cqt_workspace_bytes", "cqt_last_error")],
+                self.tables, [b for b, _, _ in heap.gspec], [M for _, M, _ in heap.gspec],
+                ngo)
 
     @classmethod
     def from_params(cls, num_octs, bins_per_oct, fs, audio_len, device=None):
@@ -55,6 +68,8 @@ class Engine:
         """grow-only scratch shared by the calls on this engine.  An outgrown
         buffer is retired, not freed: a CUDA graph captured earlier may still
         address it (Graphed, HostPipeline, the streaming graphs)."""
+        if self._ops is not None:
+            return self._ops.workspace(batch)
         need = self._ws_need.get(batch)
         if need is None:
             need = self._ws_need[batch] = self.tables.workspace_bytes(batch)
@@ -108,6 +123,8 @@ class Engine:
     # ----------------------------------------------------------------- complex
     def analysis(self, x, out=None):
         """x [B, 65536] float32 -> coefficient heap complex64 [B, ncoef]."""
+        if out is None and self._ops is not None:
+            return self._ops.analysis(x)
         x = self._signal(x, "x")
         B = x.shape[0]
         if out is None:
@@ -118,6 +135,8 @@ class Engine:
 
     def synthesis(self, c, out=None):
         """coefficient heap complex64 [B, ncoef] -> y [B, 65536] float32."""
+        if out is None and self._ops is not None:
+            return self._ops.synthesis(c)
         c = self._coef(c, "coefficients")
         B = c.shape[0]
         if out is None:
@@ -128,6 +147,8 @@ class Engine:
 
     def adj_analysis(self, g, out=None):
         """transpose of analysis: complex64 grads [B, ncoef] -> [B, 65536]."""
+        if out is None and self._ops is not None:
+            return self._ops.adj_analysis(g)
         g = self._coef(g, "coefficient gradient")
         B = g.shape[0]
         if out is None:
@@ -138,6 +159,8 @@ class Engine:
 
     def adj_synthesis(self, gy, out=None):
         """transpose of synthesis: [B, 65536] -> complex64 grads [B, ncoef]."""
+        if out is None and self._ops is not None:
+            return self._ops.adj_synthesis(gy)
         gy = self._signal(gy, "signal gradient")
         B = gy.shape[0]
         if out is None:

@@ -7,6 +7,10 @@ the backward of the synthesis is the transpose of the synthesis (analysis
 engine with the dual window, ``cqt_adj_synthesis``).  Nothing is saved for
 backward.
 
+When the torch fast path (``csrc/torch_ops.cpp``) is built, ``fwd`` / ``bwd``
+and the two autograd functions run in C++ (same kernels, same results, no
+Python in the backward); the Python classes below serve otherwise.
+
 Differences from the reference, all in the data path, none in the interface:
 the coefficients come out of the kernel already interleaved, so the blocks
 returned by ``fwd`` are zero-copy views of one complex64 heap (the reference
@@ -85,6 +89,9 @@ class TrainableCQT:
 
     def fwd(self, x):
         """x [..., 65536] real -> (blocks, side), complex64, gradients flow."""
+        ops = self.eng._ops
+        if ops is not None:   # the same, from C++ (autograd nodes included)
+            return ops.fwd(x)
         lead = x.shape[:-1]
         h = _Analysis.apply(x.reshape(-1, N).contiguous(), self.eng)
         return self.split(h, lead)
@@ -122,12 +129,20 @@ class TrainableCQT:
     def bwd(self, blocks, side=None):
         """inverse of fwd (side None drops the DC and Nyquist bands)."""
         lead = blocks[0].shape[:-2]
+        ops = self.eng._ops
+        if ops is not None:
+            h = ops.last_heap(list(blocks) + list(side)) if side is not None else None
+            if h is None:
+                h = self.heap_of(blocks, side)
+            return ops.synthesis_heap(h).reshape(*lead, N)
         h = self.heap_of(blocks, side)
         return _Synthesis.apply(h, self.eng).reshape(*lead, N)
 
     # flat-heap entry points (no per-group views), used by the fused sliced path
     def analysis_heap(self, x):
-        return _Analysis.apply(x, self.eng)
+        ops = self.eng._ops
+        return ops.analysis_heap(x) if ops is not None else _Analysis.apply(x, self.eng)
 
     def synthesis_heap(self, h):
-        return _Synthesis.apply(h, self.eng)
+        ops = self.eng._ops
+        return ops.synthesis_heap(h) if ops is not None else _Synthesis.apply(h, self.eng)

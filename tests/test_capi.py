@@ -85,3 +85,42 @@ def test_inconsistent_geometry_rejected():
     tabs["band_geom"] = g
     with pytest.raises(RuntimeError, match="disagrees with geometry"):
         _native.DeviceTables(tabs, 0)
+
+
+def test_torch_fast_path_loads():
+    """the host C++ torch fast path (built beside the library) imports and
+    exposes its handle; it holds no device code of its own"""
+    from flash_cqt_b200 import build
+    if not build.torch_ops_path().exists():
+        pytest.skip("torch fast path not built")
+    mod = _native.torch_ops()
+    assert mod is not None
+    for m in ("analysis", "synthesis", "adj_analysis", "adj_synthesis", "analysis_heap",
+              "synthesis_heap", "fwd", "last_heap", "workspace"):
+        assert hasattr(mod.Handle, m), m
+    for n in ("cqt_analysis", "cqt_synthesis", "cqt_adj_analysis", "cqt_adj_synthesis",
+              "cqt_workspace_bytes", "cqt_last_error"):
+        assert _native.fn_address(n)
+
+
+def test_torch_fast_path_raises_python_errors():
+    """argument errors from the C++ fast path arrive as Python exceptions
+    (ValueError here: tensors not on the handle's device), before any entry
+    point is called -- the pointers handed over below are never used"""
+    from flash_cqt_b200 import build
+    if not build.torch_ops_path().exists():
+        pytest.skip("torch fast path not built")
+    mod = _native.torch_ops()
+
+    class Owner:
+        pass
+
+    h = mod.Handle(0, 0, 10, 1, 1, 1, 1, 1, _native.fn_address("cqt_last_error"), Owner(),
+                   [2, 2], [3, 2], 1)
+    cases = ((h.analysis, torch.zeros(1, 65536)),
+             (h.synthesis, torch.zeros(1, 10, dtype=torch.complex64)),
+             (h.adj_analysis, torch.zeros(1, 10, dtype=torch.complex64)),
+             (h.adj_synthesis, torch.zeros(2, 65536)))
+    for fn, t in cases:
+        with pytest.raises(ValueError, match="must be a tensor on cuda:0"):
+            fn(t)

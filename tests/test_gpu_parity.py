@@ -4,6 +4,8 @@ Tolerances (from the north star): coefficients >= 120 dB relative SNR against
 the oracle, reconstruction >= 125 dB, gradients >= 120 dB against the oracle's
 exact adjoints (which are pinned to torch autograd through the reference).
 """
+import pathlib
+
 import numpy as np
 import pytest
 import torch
@@ -479,3 +481,45 @@ def test_no_bounded_wait_expired(eng, dev):
     from flash_cqt_b200._native import wait_timeouts
     torch.cuda.synchronize()
     assert wait_timeouts() == 0
+
+
+_TRAIN_STEP = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[2])
+from flash_cqt_b200 import OctCQT, TrainableCQT, _native
+dev = torch.device("cuda:0")
+cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=65536, device=dev)
+t = TrainableCQT(cqt, dev)
+g = torch.Generator(device="cpu").manual_seed(11)
+x = torch.randn(3, 65536, generator=g).to(dev).requires_grad_(True)
+tgt = torch.randn(3, 65536, generator=g).to(dev)
+blocks, side = t.fwd(x)
+y = t.bwd(blocks, side)
+((y - tgt) ** 2).mean().backward()
+torch.save({"fast": _native.torch_ops() is not None, "y": y.detach().cpu(),
+            "b0": blocks[0].detach().cpu(), "gx": x.grad.cpu()}, sys.argv[1])
+"""
+
+
+def test_torch_fast_path_matches_ctypes_path(tmp_path):
+    """TrainableCQT through the C++ fast path and through the Python autograd
+    functions over ctypes run the same kernels: bit-identical outputs and
+    gradients"""
+    import os
+    import subprocess
+    import sys
+    root = str(pathlib.Path(__file__).resolve().parents[1])
+    script = tmp_path / "step.py"
+    script.write_text(_TRAIN_STEP)
+    out = {}
+    for flag in ("1", "0"):
+        f = tmp_path / f"r{flag}.pt"
+        env = dict(os.environ, FLASH_CQT_B200_TORCH_OPS=flag)
+        subprocess.run([sys.executable, str(script), str(f), root], check=True, env=env,
+                       timeout=600)
+        out[flag] = torch.load(f)
+    if not out["1"]["fast"]:
+        pytest.skip("torch fast path not built")
+    assert not out["0"]["fast"]
+    for k in ("y", "b0", "gx"):
+        assert torch.equal(out["1"][k], out["0"][k]), k
