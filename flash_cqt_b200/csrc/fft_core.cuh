@@ -94,8 +94,11 @@ __device__ __forceinline__ void static_for(F&& f) {
 
 // Complex add and subtract as sm_100 packed two-lane fp32 instructions (one
 // instruction for both components; each lane rounds as the scalar operation,
-// and a - b is formed exactly as b * -1 + a).  FCQT_F32X2=0 builds the scalar
-// forms.
+// and a - b is formed exactly as b * -1 + a).  The complex product is
+// a.x (b.x, b.y) + a.y (-b.y, b.x) as one packed multiply and one packed
+// fused multiply-add (one rounding after the multiply, one after the add, as
+// the scalar form, with the roles of the two products swapped).
+// FCQT_F32X2=0 builds the scalar forms.
 #ifndef FCQT_F32X2
 #define FCQT_F32X2 1
 #endif
@@ -109,7 +112,12 @@ __device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(
 __device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
 #endif
 __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+#if FCQT_F32X2
+    const float2 t = __fmul2_rn(make_float2(a.x, a.x), b);
+    return __ffma2_rn(make_float2(a.y, a.y), make_float2(-b.y, b.x), t);
+#else
     return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
+#endif
 }
 // a * conj(b)
 __device__ __forceinline__ float2 cmulc(float2 a, float2 b) {
