@@ -23,6 +23,7 @@
 namespace {
 
 constexpr int64_t kN = 65536;
+constexpr int kLayoutPlanar = 0;    // CQT_LAYOUT_PLANAR
 constexpr int kLayoutComplex = 1;   // CQT_LAYOUT_COMPLEX
 
 // cqt_analysis / cqt_adj_synthesis: signal first
@@ -111,6 +112,23 @@ struct Ops : torch::CustomClassHolder {
         return t.resolve_conj().contiguous();
     }
 
+    // a float32 [B, ncoef] coefficient plane on this device; `out` planes
+    // are written in place, so they must already be contiguous
+    at::Tensor plane(const at::Tensor& t, const char* name, int64_t B, bool out) const {
+        TORCH_CHECK_VALUE(t.defined() && t.is_cuda() && t.get_device() == device,
+                          "coefficient plane ", name, " must be float32 on cuda:", (int)device);
+        TORCH_CHECK_VALUE(t.scalar_type() == at::kFloat, "coefficient plane ", name,
+                          " must be float32 on cuda:", (int)device);
+        TORCH_CHECK_VALUE(t.dim() == 2 && t.size(1) == ncoef && (B < 0 || t.size(0) == B),
+                          "coefficient plane ", name, " must be [B, ", ncoef, "]");
+        if (out) {
+            TORCH_CHECK_VALUE(t.is_contiguous(), "coefficient plane ", name,
+                              " must be contiguous");
+            return t;
+        }
+        return t.contiguous();
+    }
+
     struct DeviceSwitch {   // switches only when the current device differs
         c10::optional<c10::cuda::CUDAGuard> g;
         explicit DeviceSwitch(c10::DeviceIndex d) {
@@ -129,6 +147,36 @@ struct Ops : torch::CustomClassHolder {
                  kLayoutComplex, (int)B, w, wb, stream()),
               "cqt_analysis");
         return out;
+    }
+
+    // planar layout (FusedOctCQT): results go into the caller's tensors
+    void analysis_planar(const at::Tensor& x_, const at::Tensor& kr_, const at::Tensor& ki_) {
+        at::Tensor x = signal(x_, "x");
+        const int64_t B = x.size(0);
+        at::Tensor kr = plane(kr_, "re", B, true), ki = plane(ki_, "im", B, true);
+        DeviceSwitch sw(device);
+        size_t wb;
+        void* w = workspace(B, &wb);
+        check(an(tables, x.data_ptr<float>(), kr.data_ptr<float>(), ki.data_ptr<float>(),
+                 kLayoutPlanar, (int)B, w, wb, stream()),
+              "cqt_analysis");
+    }
+
+    void synthesis_planar(const at::Tensor& kr_, const at::Tensor& ki_, const at::Tensor& y) {
+        at::Tensor kr = plane(kr_, "re", -1, false);
+        const int64_t B = kr.size(0);
+        at::Tensor ki = plane(ki_, "im", B, false);
+        TORCH_CHECK_VALUE(y.defined() && y.is_cuda() && y.get_device() == device &&
+                              y.scalar_type() == at::kFloat && y.dim() == 2 &&
+                              y.size(0) == B && y.size(1) == kN && y.is_contiguous(),
+                          "y must be a contiguous float32 [B, ", kN, "] tensor on cuda:",
+                          (int)device);
+        DeviceSwitch sw(device);
+        size_t wb;
+        void* w = workspace(B, &wb);
+        check(syn(tables, kr.data_ptr<float>(), ki.data_ptr<float>(), kLayoutPlanar,
+                  y.data_ptr<float>(), (int)B, w, wb, stream()),
+              "cqt_synthesis");
     }
 
     at::Tensor synthesis(const at::Tensor& c_) {
@@ -244,6 +292,12 @@ struct Handle {
     }
 
     at::Tensor analysis(const at::Tensor& x) { return ops->analysis(x); }
+    void analysis_planar(const at::Tensor& x, const at::Tensor& kr, const at::Tensor& ki) {
+        ops->analysis_planar(x, kr, ki);
+    }
+    void synthesis_planar(const at::Tensor& kr, const at::Tensor& ki, const at::Tensor& y) {
+        ops->synthesis_planar(kr, ki, y);
+    }
     at::Tensor synthesis(const at::Tensor& c) { return ops->synthesis(c); }
     at::Tensor adj_analysis(const at::Tensor& g) { return ops->adj_analysis(g); }
     at::Tensor adj_synthesis(const at::Tensor& gy) { return ops->adj_synthesis(gy); }
@@ -302,6 +356,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                             std::vector<int64_t>, int64_t>())
         .def("workspace", &Handle::workspace)
         .def("analysis", &Handle::analysis)
+        .def("analysis_planar", &Handle::analysis_planar)
+        .def("synthesis_planar", &Handle::synthesis_planar)
         .def("synthesis", &Handle::synthesis)
         .def("adj_analysis", &Handle::adj_analysis)
         .def("adj_synthesis", &Handle::adj_synthesis)

@@ -102,6 +102,14 @@ class Engine:
             raise ValueError(f"{name} must be [B, {self.ncoef}], got {tuple(c.shape)}")
         return c.resolve_conj().contiguous()
 
+    def _out(self, t, shape, dtype, name):
+        """a caller-supplied output: written in place, so it must match exactly"""
+        if (not torch.is_tensor(t) or t.device != self.dev or t.dtype != dtype
+                or tuple(t.shape) != tuple(shape) or not t.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous {dtype} tensor of shape "
+                             f"{tuple(shape)} on {self.dev}")
+        return t
+
     def _planes(self, re, im):
         for t, nm in ((re, "re"), (im, "im")):
             if not torch.is_tensor(t) or t.device != self.dev or t.dtype != torch.float32:
@@ -129,6 +137,7 @@ class Engine:
         B = x.shape[0]
         if out is None:
             out = torch.empty(B, self.ncoef, dtype=torch.complex64, device=self.dev)
+        self._out(out, (B, self.ncoef), torch.complex64, "out")
         self._run("cqt_analysis", x.data_ptr(), out.data_ptr(), None,
                   _native.CQT_LAYOUT_COMPLEX, B)
         return out
@@ -141,6 +150,7 @@ class Engine:
         B = c.shape[0]
         if out is None:
             out = torch.empty(B, N, dtype=torch.float32, device=self.dev)
+        self._out(out, (B, N), torch.float32, "out")
         self._run("cqt_synthesis", c.data_ptr(), None, out.data_ptr(),
                   _native.CQT_LAYOUT_COMPLEX, B)
         return out
@@ -153,6 +163,7 @@ class Engine:
         B = g.shape[0]
         if out is None:
             out = torch.empty(B, N, dtype=torch.float32, device=self.dev)
+        self._out(out, (B, N), torch.float32, "out")
         self._run("cqt_adj_analysis", g.data_ptr(), None, out.data_ptr(),
                   _native.CQT_LAYOUT_COMPLEX, B)
         return out
@@ -165,20 +176,32 @@ class Engine:
         B = gy.shape[0]
         if out is None:
             out = torch.empty(B, self.ncoef, dtype=torch.complex64, device=self.dev)
+        self._out(out, (B, self.ncoef), torch.complex64, "out")
         self._run("cqt_adj_synthesis", gy.data_ptr(), out.data_ptr(), None,
                   _native.CQT_LAYOUT_COMPLEX, B)
         return out
 
     # ------------------------------------------------------------------ planar
     def analysis_planar(self, x, kr, ki):
+        """x [B, 65536] -> the planes kr, ki [B, ncoef] (written in place)"""
+        if self._ops is not None:
+            self._ops.analysis_planar(x, kr, ki)
+            return kr, ki
         x = self._signal(x, "x")
-        kr, ki = self._planes(kr, ki)
+        B = x.shape[0]
+        self._out(kr, (B, self.ncoef), torch.float32, "coefficient plane re")
+        self._out(ki, (B, self.ncoef), torch.float32, "coefficient plane im")
         self._run("cqt_analysis", x.data_ptr(), kr.data_ptr(), ki.data_ptr(),
-                  _native.CQT_LAYOUT_PLANAR, x.shape[0])
+                  _native.CQT_LAYOUT_PLANAR, B)
         return kr, ki
 
     def synthesis_planar(self, kr, ki, y):
+        """planes kr, ki [B, ncoef] -> y [B, 65536] (written in place)"""
+        if self._ops is not None:
+            self._ops.synthesis_planar(kr, ki, y)
+            return y
         kr, ki = self._planes(kr, ki)
+        self._out(y, (kr.shape[0], N), torch.float32, "y")
         self._run("cqt_synthesis", kr.data_ptr(), ki.data_ptr(), y.data_ptr(),
                   _native.CQT_LAYOUT_PLANAR, kr.shape[0])
         return y

@@ -95,8 +95,9 @@ def test_torch_fast_path_loads():
         pytest.skip("torch fast path not built")
     mod = _native.torch_ops()
     assert mod is not None
-    for m in ("analysis", "synthesis", "adj_analysis", "adj_synthesis", "analysis_heap",
-              "synthesis_heap", "fwd", "last_heap", "workspace"):
+    for m in ("analysis", "synthesis", "adj_analysis", "adj_synthesis", "analysis_planar",
+              "synthesis_planar", "analysis_heap", "synthesis_heap", "fwd", "last_heap",
+              "workspace"):
         assert hasattr(mod.Handle, m), m
     for n in ("cqt_analysis", "cqt_synthesis", "cqt_adj_analysis", "cqt_adj_synthesis",
               "cqt_workspace_bytes", "cqt_last_error"):
@@ -124,3 +125,8 @@ def test_torch_fast_path_raises_python_errors():
     for fn, t in cases:
         with pytest.raises(ValueError, match="must be a tensor on cuda:0"):
             fn(t)
+    p = torch.zeros(1, 10)
+    with pytest.raises(ValueError, match="must be a tensor on cuda:0"):
+        h.analysis_planar(torch.zeros(1, 65536), p, p)
+    with pytest.raises(ValueError, match="must be float32 on cuda:0"):
+        h.synthesis_planar(p, p, torch.zeros(1, 65536))

@@ -245,6 +245,15 @@ def test_bad_inputs_raise(eng, dev):
         eng.analysis(torch.zeros(1, 65536))
     with pytest.raises(ValueError):
         eng.synthesis(torch.zeros(1, 100, dtype=torch.complex64, device=dev))
+    # outputs written in place must match the batch exactly (no short buffers)
+    x2 = torch.zeros(2, 65536, device=dev)
+    kr = torch.zeros(1, eng.ncoef, device=dev)
+    with pytest.raises(ValueError):
+        eng.analysis_planar(x2, kr, kr.clone())
+    with pytest.raises(ValueError):
+        eng.synthesis_planar(kr, kr.clone(), torch.zeros(1, 4096, device=dev))
+    with pytest.raises(ValueError):
+        eng.analysis(x2, out=torch.zeros(1, eng.ncoef, dtype=torch.complex64, device=dev))
 
 
 def test_oversized_batch_refused(eng, dev):
