@@ -311,7 +311,9 @@ struct Handle {
         Ops& o = *ops;
         TORCH_CHECK(x.dim() >= 1 && x.size(-1) == kN, "x must be [..., ", kN, "]");
         std::vector<int64_t> lead(x.sizes().begin(), x.sizes().end() - 1);
-        at::Tensor h = AnalysisFn::apply(x.reshape({-1, kN}), ops);
+        int64_t B = 1;   // explicit: reshape cannot infer -1 for an empty batch
+        for (int64_t d : lead) B *= d;
+        at::Tensor h = AnalysisFn::apply(x.reshape({B, kN}), ops);
         std::vector<at::Tensor> parts = h.split_with_sizes(o.sizes, 1);
         pybind11::list blocks, side;
         o.last_v.clear();

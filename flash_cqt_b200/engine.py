@@ -292,6 +292,11 @@ class SlicedEngine:
         if out is None:
             out = torch.empty(self.coef_numel(rows, S), dtype=torch.complex64,
                               device=self.eng.dev)
+        elif (not torch.is_tensor(out) or out.device != self.eng.dev
+              or out.dtype != torch.complex64 or not out.is_contiguous()
+              or out.numel() != self.coef_numel(rows, S)):
+            raise ValueError("out must be a contiguous complex64 buffer of rows * S * ncoef "
+                             f"values on {self.eng.dev}")
         if ws is None:
             ws = self.eng.workspace(rows * S)
         stream = _raw_stream_of(self.eng.dev.index)
@@ -320,6 +325,12 @@ class SlicedEngine:
         count = int(length) - sample0 if count is None else int(count)
         if out is None:
             out = torch.empty(rows, count, dtype=torch.float32, device=self.eng.dev)
+        elif (not torch.is_tensor(out) or out.device != self.eng.dev
+              or out.dtype != torch.float32 or tuple(out.shape) != (rows, count)
+              or out.stride(-1) != 1):
+            # written in place: no copy may stand in for it
+            raise ValueError(f"out must be float32 [rows, count] = [{rows}, {count}] with "
+                             f"unit sample stride on {self.eng.dev}")
         if ws is None:
             ws = self.eng.workspace(rows * S)
         stream = _raw_stream_of(self.eng.dev.index)

@@ -93,7 +93,10 @@ class TrainableCQT:
         if ops is not None:   # the same, from C++ (autograd nodes included)
             return ops.fwd(x)
         lead = x.shape[:-1]
-        h = _Analysis.apply(x.reshape(-1, N).contiguous(), self.eng)
+        B = 1
+        for d in lead:   # explicit: reshape cannot infer -1 for an empty batch
+            B *= d
+        h = _Analysis.apply(x.reshape(B, N).contiguous(), self.eng)
         return self.split(h, lead)
 
     def heap_of(self, blocks, side=None):
@@ -119,7 +122,7 @@ class TrainableCQT:
                         and c.stride()[-1] == 1 and c.stride()[-2] == M
                         for c, (b, M, off) in zip(allb, self.gspec))):
             return base
-        parts = [c.reshape(B, -1).to(torch.complex64) for c in allb]
+        parts = [c.reshape(B, c.shape[-2] * c.shape[-1]).to(torch.complex64) for c in allb]
         if side is None:
             nside = sum(b * M for b, M, _ in self.gspec[self.ngroups:])
             parts.append(torch.zeros(B, nside, dtype=torch.complex64,

@@ -505,15 +505,21 @@ tgt = torch.randn(3, 65536, generator=g).to(dev)
 blocks, side = t.fwd(x)
 y = t.bwd(blocks, side)
 ((y - tgt) ** 2).mean().backward()
+from flash_cqt_b200 import FusedOctCQT
+f = FusedOctCQT(cqt, dev)
+kr, ki = f.fwd(x.detach())
+kr, ki = kr.clone(), ki.clone()
+yf = f.bwd(kr, ki).clone()
 torch.save({"fast": _native.torch_ops() is not None, "y": y.detach().cpu(),
-            "b0": blocks[0].detach().cpu(), "gx": x.grad.cpu()}, sys.argv[1])
+            "b0": blocks[0].detach().cpu(), "gx": x.grad.cpu(), "kr": kr.cpu(),
+            "ki": ki.cpu(), "yf": yf.cpu()}, sys.argv[1])
 """
 
 
 def test_torch_fast_path_matches_ctypes_path(tmp_path):
-    """TrainableCQT through the C++ fast path and through the Python autograd
-    functions over ctypes run the same kernels: bit-identical outputs and
-    gradients"""
+    """TrainableCQT and FusedOctCQT through the C++ fast path and through the
+    Python autograd functions / launchers over ctypes run the same kernels:
+    bit-identical outputs and gradients"""
     import os
     import subprocess
     import sys
@@ -530,5 +536,25 @@ def test_torch_fast_path_matches_ctypes_path(tmp_path):
     if not out["1"]["fast"]:
         pytest.skip("torch fast path not built")
     assert not out["0"]["fast"]
-    for k in ("y", "b0", "gx"):
+    for k in ("y", "b0", "gx", "kr", "ki", "yf"):
         assert torch.equal(out["1"][k], out["0"][k]), k
+
+
+def test_empty_batch(eng, dev):
+    """a batch of zero slices launches nothing and returns empty results of
+    the right shapes on every entry point"""
+    from flash_cqt_b200 import FusedOctCQT, OctCQT, TrainableCQT
+    x0 = torch.zeros(0, 65536, device=dev)
+    h = eng.analysis(x0)
+    assert h.shape == (0, eng.ncoef) and h.dtype == torch.complex64
+    assert eng.synthesis(h).shape == (0, 65536)
+    assert eng.adj_analysis(h).shape == (0, 65536)
+    assert eng.adj_synthesis(x0).shape == (0, eng.ncoef)
+    cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=65536, device=dev)
+    t = TrainableCQT(cqt, dev)
+    blocks, side = t.fwd(x0)
+    assert all(c.shape[0] == 0 for c in list(blocks) + list(side))
+    assert t.bwd(blocks, side).shape == (0, 65536)
+    f = FusedOctCQT(cqt, dev)
+    kr, ki = f.fwd(x0)
+    assert kr.shape == (0, eng.ncoef) and f.bwd(kr, ki).shape == (0, 65536)
