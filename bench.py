@@ -496,6 +496,49 @@ def extras(args, eng, t, dev, world, rank, barrier, W, K, hbm=6549.1):
         sweep[str(Bs)] = {"ms": med, "round_trips_per_s": Bs / (med / 1e3)}
         del gg
     out["sweep_per_gpu"] = sweep
+    # ---- config 2: one slice of 8 seeded sinusoids (log-uniform 43 Hz - 20 kHz,
+    # amplitudes U(0.1, 1), phases U(0, 2 pi)) + N(0, 0.01^2) noise, graphed
+    # round trip and its reconstruction SNR
+    g1 = torch.Generator().manual_seed(1)
+    fr = torch.exp(torch.empty(8, dtype=torch.float64).uniform_(math.log(43.0),
+                                                                 math.log(20000.0),
+                                                                 generator=g1))
+    am = torch.empty(8, dtype=torch.float64).uniform_(0.1, 1.0, generator=g1)
+    ph = torch.empty(8, dtype=torch.float64).uniform_(0.0, 2 * math.pi, generator=g1)
+    tt = torch.arange(N, dtype=torch.float64) / 44100.0
+    x1 = (am[:, None] * torch.sin(2 * math.pi * fr[:, None] * tt + ph[:, None])).sum(0)
+    x1 = x1 + 0.01 * torch.randn(N, dtype=torch.float64, generator=g1)
+    x1 = x1.float().view(1, N).to(dev)
+    c1 = torch.empty(1, eng.ncoef, dtype=torch.complex64, device=dev)
+    y1 = torch.empty(1, N, device=dev)
+
+    def rt1():
+        eng.analysis(x1, out=c1)
+        eng.synthesis(c1, out=y1)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            rt1()
+    torch.cuda.current_stream().wait_stream(s)
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2):
+        rt1()
+    ts = []
+    for _ in range(50):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g2.replay()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    xd, yd = x1.double(), y1.double()
+    out["config2_b1_sinusoids"] = {
+        "ms": statistics.median(ts),
+        "snr_db": float(10 * torch.log10((xd ** 2).sum() / ((yd - xd) ** 2).sum())),
+        "input": "8 seeded sinusoids + N(0, 0.01^2), seed 1, graph replay"}
+    del g2
     # ---- train step, batch 16: analysis -> synthesis -> MSE -> backward
     Bt = 16
     gx = torch.Generator(device=dev).manual_seed(2)
