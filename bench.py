@@ -40,6 +40,9 @@ def parse():
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the batch sweep, train step, e2e and CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--sliced-only", action="store_true",
+                    help="run only the config-5 long-stream measurement and print its "
+                         "result (for profiling the sliced kernels)")
     return ap.parse_args()
 
 
@@ -191,6 +194,16 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.sliced_only:
+        pk = ROOT / "MEASURED_PEAKS.json"
+        hbm = (json.loads(pk.read_text()).get("hbm_gbs") if pk.exists() else None) or 6650.0
+        r = sliced_stream(dev, world, rank, max(args.warmup, 3), args.steps, hbm)
+        if rank == 0:
+            print(json.dumps({"sliced_stream": r}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     B = args.batch
     W = max(args.warmup, 3)
     K = args.steps
