@@ -313,7 +313,9 @@ struct Handle {
         std::vector<int64_t> lead(x.sizes().begin(), x.sizes().end() - 1);
         int64_t B = 1;   // explicit: reshape cannot infer -1 for an empty batch
         for (int64_t d : lead) B *= d;
-        at::Tensor h = AnalysisFn::apply(x.reshape({B, kN}), ops);
+        // a [B, 65536] input goes in as it is: a no-op reshape would still
+        // add a view node to the autograd graph
+        at::Tensor h = AnalysisFn::apply(x.dim() == 2 ? x : x.reshape({B, kN}), ops);
         std::vector<at::Tensor> parts = h.split_with_sizes(o.sizes, 1);
         pybind11::list blocks, side;
         o.last_v.clear();

@@ -137,7 +137,9 @@ class TrainableCQT:
             h = ops.last_heap(list(blocks) + list(side)) if side is not None else None
             if h is None:
                 h = self.heap_of(blocks, side)
-            return ops.synthesis_heap(h).reshape(*lead, N)
+            y = ops.synthesis_heap(h)
+            # a one-dimensional lead is the heap's batch already: no view node
+            return y if len(lead) == 1 else y.reshape(*lead, N)
         h = self.heap_of(blocks, side)
         return _Synthesis.apply(h, self.eng).reshape(*lead, N)
 
