@@ -304,7 +304,8 @@ def _flat(blocks, side):
     return torch.cat([c.reshape(-1) for c in list(blocks) + list(side)])
 
 
-@pytest.mark.parametrize("shape", [(1, 1, 150000), (2, 2, 65537), (1, 3, 262144)])
+@pytest.mark.parametrize("shape", [(1, 1, 150000), (2, 2, 65537), (1, 3, 262144),
+                                   (1, 1, 1000), (2, 1, 32768)])
 def test_sliced_fused_equals_generic_path(dev, shape):
     from flash_cqt_b200 import SlicedCQT
     g = torch.Generator(device="cpu").manual_seed(sum(shape))
