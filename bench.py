@@ -28,6 +28,9 @@ N = 65536
 METRIC = "65536-sample CQT round trips/s"
 # algorithmic bytes per slice (x in, coefficients out, coefficients in, y out)
 RT_BYTES = 262144 + 1063936 + 1063936 + 262144
+# train step per sample: round trip + target in + y re-read + coefficient
+# gradients out and in + dL/dx out
+TRAIN_BYTES = RT_BYTES + 262144 + 262144 + 1063936 + 1063936 + 262144
 
 
 def parse():
@@ -576,6 +579,68 @@ def extras(args, eng, t, dev, world, rank, barrier, W, K, hbm=6549.1):
         b.synchronize()
         ts.append(a.elapsed_time(b))
     out["train_step_ms_b16"] = statistics.median(ts)
+    # the same step with the loss folded into the engines (TrainableCQT.mse_loss:
+    # squared-error sum in the synthesis epilogue, 2 (y - t) / n formed in the
+    # transposed synthesis' load)
+    def step_fused(xg):
+        t.mse_loss(*t.fwd(xg), tgt).backward()
+
+    def fused_eager():
+        xg = xt.clone().requires_grad_(True)
+        step_fused(xg)
+        return xg.grad
+
+    for _ in range(W):
+        fused_eager()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(max(K, 20)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fused_eager()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    fused_ms = statistics.median(ts)
+    # device time of the fused step alone: forward and backward captured in one
+    # CUDA graph (static input, gradient in the graph's pool) and replayed
+    xs = xt.clone().requires_grad_(True)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            xs.grad = None
+            step_fused(xs)
+    torch.cuda.current_stream().wait_stream(s)
+    xs.grad = None
+    gstep = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gstep):
+        step_fused(xs)
+    for _ in range(3):
+        gstep.replay()
+    torch.cuda.synchronize()
+    reps = max(K, 50)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        gstep.replay()
+    b.record()
+    b.synchronize()
+    gpu_ms = a.elapsed_time(b) / reps
+    del gstep
+    step_bytes = TRAIN_BYTES * Bt
+    out["train_step"] = {
+        "batch": Bt, "eager_ms": out["train_step_ms_b16"], "fused_loss_eager_ms": fused_ms,
+        "fused_loss_gpu_ms": gpu_ms,
+        "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes,
+                     "achieved": step_bytes / (gpu_ms / 1e3) / 1e9, "peak": hbm,
+                     "unit": "GB/s", "frac": step_bytes / (gpu_ms / 1e3) / 1e9 / hbm,
+                     "time": "fused_loss_gpu_ms (device time of the graph-replayed step)"},
+        "eager_frac_of_hbm": step_bytes / (out["train_step_ms_b16"] / 1e3) / 1e9 / hbm,
+        "what": "analysis -> synthesis -> MSE vs a seeded target -> backward, B = 16 "
+                "(x seed 2, target seed 3); eager = the reference's "
+                "((bwd(*fwd(x)) - t) ** 2).mean().backward(), fused_loss = "
+                "TrainableCQT.mse_loss(...).backward()"}
     return out
 
 

@@ -90,6 +90,11 @@ def lib():
                 else:
                     fn.argtypes = [vp, vp, vp, ci, vp, ci, vp, sz, vp]
                 fn.restype = ci
+            fl = ctypes.c_float
+            L.cqt_synthesis_sqerr.argtypes = [vp, vp, vp, ci, vp, vp, vp, fl, ci, vp, sz, vp]
+            L.cqt_synthesis_sqerr.restype = ci
+            L.cqt_adj_synthesis_sqerr.argtypes = [vp, vp, vp, fl, vp, vp, vp, ci, ci, vp, sz, vp]
+            L.cqt_adj_synthesis_sqerr.restype = ci
             L.cqt_launch_stage.argtypes = [vp, ci, vp, vp, vp, vp, ci, ci, vp, sz, vp]
             L.cqt_launch_stage.restype = ci
             L.cqt_analysis_noalloc.argtypes = [vp, vp, vp, vp, ci, ci, vp]
@@ -113,7 +118,8 @@ def exported_symbols():
     """Names the C header declares (checked by the CPU tests)."""
     return ["cqt_tables_upload", "cqt_tables_free", "cqt_ncoef",
             "cqt_workspace_bytes", "cqt_analysis", "cqt_synthesis",
-            "cqt_adj_analysis", "cqt_adj_synthesis", "cqt_launch_stage",
+            "cqt_adj_analysis", "cqt_adj_synthesis", "cqt_synthesis_sqerr",
+            "cqt_adj_synthesis_sqerr", "cqt_launch_stage",
             "cqt_analysis_noalloc", "cqt_sliced_count", "cqt_sliced_analysis",
             "cqt_sliced_synthesis", "cqt_sliced_adj_analysis",
             "cqt_sliced_adj_synthesis", "cqt_wait_timeouts", "cqt_last_error",

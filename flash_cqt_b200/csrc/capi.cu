@@ -2,6 +2,7 @@
 // entry points.  Each entry point validates its arguments, launches two
 // kernels on the caller's stream and reports launch errors; none allocates
 // or synchronises.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -67,8 +68,17 @@ int check_device(const cqt_tables* t) {
     return CQT_OK;
 }
 
-size_t ws_need(const cqt_tables* t, int batch) {
+// workspace: the spectrum rows / colour planes, then the per-CTA partial sums
+// of the squared-error entry points (16-byte aligned: the planes are)
+size_t ws_planes(const cqt_tables* t, int batch) {
     return (size_t)batch * (size_t)t->max_planes * kPlaneStride * sizeof(float2);
+}
+size_t ws_need(const cqt_tables* t, int batch) {
+    const size_t partials = ((size_t)spectrum_ctas(batch) * sizeof(float) + 15) & ~(size_t)15;
+    return ws_planes(t, batch) + partials;
+}
+float* ws_partials(const cqt_tables* t, int batch, void* ws) {
+    return reinterpret_cast<float*>(static_cast<char*>(ws) + ws_planes(t, batch));
 }
 
 // the band kernels split an instance index into (band, slice) with a float
@@ -567,6 +577,49 @@ int cqt_adj_analysis(const cqt_tables* t, const float* g_re, const float* g_im, 
     return run_inv_engine(t, 1, in, gx, batch, ws, static_cast<cudaStream_t>(stream));
 }
 
+int cqt_synthesis_sqerr(const cqt_tables* t, const float* c_re, const float* c_im, int layout,
+                        float* y, const float* target, float* loss, float loss_scale,
+                        int batch, void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_common(t, batch, ws, ws_bytes, layout);
+    if (rc) return rc;
+    if (!loss) return fail(CQT_ERR_ARG, "null loss");
+    if (((uintptr_t)loss & 3u) != 0) return fail(CQT_ERR_ARG, "loss not 4-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (batch > 0) {
+        if ((rc = check_signal(y, false))) return rc;
+        if ((rc = check_signal(target, true))) return rc;
+        CoefPtr in;
+        if ((rc = coef_ptr(c_re, c_im, layout, &in))) return rc;
+        SigMap out = contiguous_out(y);
+        out.target = target;
+        out.partial = ws_partials(t, batch, ws);
+        if ((rc = run_inv(t, 0, in, out, band_params(t, batch), batch, ws, s))) return rc;
+    }
+    // an empty batch still defines the loss: the sum of nothing
+    cudaError_t e = launch_sqerr_finish(batch > 0 ? ws_partials(t, batch, ws) : nullptr,
+                                        spectrum_ctas(batch), loss_scale, loss, s);
+    return e == cudaSuccess ? CQT_OK : cuda_fail(e, "squared-error sum launch");
+}
+
+int cqt_adj_synthesis_sqerr(const cqt_tables* t, const float* y, const float* target,
+                            float scale, const float* scale_dev, float* g_re, float* g_im,
+                            int layout, int batch, void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_common(t, batch, ws, ws_bytes, layout);
+    if (rc) return rc;
+    if (batch == 0) return CQT_OK;
+    if ((rc = check_signal(y, true))) return rc;
+    if ((rc = check_signal(target, true))) return rc;
+    if (((uintptr_t)scale_dev & 3u) != 0) return fail(CQT_ERR_ARG, "scale_dev not 4-byte aligned");
+    CoefPtr out;
+    if ((rc = coef_ptr(g_re, g_im, layout, &out))) return rc;
+    SigMap in = contiguous_in(y);
+    in.target = target;
+    in.scale_dev = scale_dev;
+    in.scale = scale;
+    return run_fwd(t, 1, in, out, band_params(t, batch), batch, ws,
+                   static_cast<cudaStream_t>(stream));
+}
+
 int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float* sig_out,
                      float* c_re, float* c_im, int layout, int batch, void* ws,
                      size_t ws_bytes, void* stream) {
@@ -619,8 +672,13 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
 // * The array holds at most kNoAllocMaxBatch = 8 slices (2,097,664 bytes);
 //   every GPU that loads this library keeps it until the process exits.
 // * The first call on a device, with that device current, looks up the
-//   array's device address with cudaGetSymbolAddress and caches it; make that
-//   first call before any stream capture.
+//   array's device address with cudaGetSymbolAddress and caches it.  That
+//   lookup may make the CUDA runtime load this library's device code (lazy
+//   module loading), which can itself allocate and synchronise; so make one
+//   warm-up call per device at start-up, off the real-time thread and before
+//   any stream capture (batch 0 is enough: the lookup comes before the
+//   empty-batch return).  Later calls take the cached address with one atomic
+//   load, no lock, and allocate nothing.
 // * All calls on a device share the array and it keeps the last call's
 //   contents.  Nothing in it needs clearing (the spectrum kernel writes every
 //   bin the band kernel later reads), but calls that overlap on the GPU --
@@ -632,8 +690,8 @@ constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) float2 g_noalloc_scratch[kNoAllocMaxBatch * kPlaneStride];
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;                              // first lookup per device only
+std::atomic<void*> g_noalloc_ptr[kNoAllocMaxDevices];
 
 }  // namespace
 
@@ -651,14 +709,14 @@ extern "C" int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* 
     if (rc) return rc;
     if (t->device < 0 || t->device >= kNoAllocMaxDevices)
         return fail(CQT_ERR_DEVICE, "device index beyond the no-allocation address cache");
-    void* scratch = nullptr;
-    {
+    void* scratch = g_noalloc_ptr[t->device].load(std::memory_order_acquire);
+    if (!scratch) {
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
-        scratch = g_noalloc_ptr[t->device];
+        scratch = g_noalloc_ptr[t->device].load(std::memory_order_relaxed);
         if (!scratch) {
             cudaError_t e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
             if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
-            g_noalloc_ptr[t->device] = scratch;
+            g_noalloc_ptr[t->device].store(scratch, std::memory_order_release);
         }
     }
     if (batch == 0) return CQT_OK;

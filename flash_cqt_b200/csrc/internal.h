@@ -77,7 +77,18 @@ struct SigMap {
     int S;
     int slice0;
     const float* window;   // [65536] or null
+    // squared-error mode of the contiguous layout (S == 0), for an MSE loss:
+    // the analysis engine reads s * (x - target) with s = scale (times
+    // *scale_dev when not null); the synthesis engine stores y and writes one
+    // partial sum of (y - target)^2 per CTA into partial[CTA]
+    const float* target;
+    const float* scale_dev;
+    float scale;
+    float* partial;
 };
+
+// input / output mode of the spectrum kernels
+enum SigMode { kSigPlain = 0, kSigSliced = 1, kSigSqErr = 2 };
 
 // everything a band kernel needs besides the per-tap tables, passed by value
 // (kernel parameters live in the constant bank: no dependent global loads)
@@ -175,6 +186,12 @@ cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& s
                                 cudaStream_t s);
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
                                 const SpecTables& st, int batch, cudaStream_t s);
+// CTAs of one spectrum launch over `batch` slices (partial sums of the
+// squared-error mode: one per CTA)
+inline int spectrum_ctas(int batch) { return 2 * batch; }
+// loss = scale * sum of the n partials, in a fixed order (one CTA)
+cudaError_t launch_sqerr_finish(const float* partial, int n, float scale, float* loss,
+                                cudaStream_t s);
 cudaError_t read_wait_timeouts(unsigned* count);   // expired bounded waits (device)
 cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParams& bp,
                              CoefPtr out, cudaStream_t s);

@@ -290,12 +290,13 @@ __device__ __forceinline__ void prefetch_signal_part(const SigMap& m, long g, in
     }
 }
 
-template <bool SLICED>
+template <int MODE>
 __global__ void __launch_bounds__(CF::T, 1)
 spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                     const float2* __restrict__ ghi, const float2* __restrict__ glo,
                     const float2* __restrict__ gtw, int ahead) {
     using C = CF;
+    constexpr bool SLICED = MODE == kSigSliced;
     constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
@@ -324,15 +325,29 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                 v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
             }
     };
-    // one uniform branch, each side a straight run of loads
-    if (SLICED && z.whole)
+    if constexpr (MODE == kSigSqErr) {
+        // the MSE gradient s (y - target) formed on load (s = 2 dL/dloss / n)
+        const float2* yp = reinterpret_cast<const float2*>(in.x) + slice * (long)kHalf;
+        const float2* tp = reinterpret_cast<const float2*>(in.target) + slice * (long)kHalf;
+        const float sc = in.scale_dev ? in.scale * __ldg(in.scale_dev) : in.scale;
+        load([&](int n) {
+            const float2 a = __ldg(yp + n), b = __ldg(tp + n);
+            return make_float2(sc * (a.x - b.x), sc * (a.y - b.y));
+        });
+    } else if (SLICED && z.whole) {   // one uniform branch, each side a straight run of loads
         load([&](int n) { return z.pair(n); });
-    else
+    } else {
         load(z);
+    }
     spec_compute<C, 1, -1>(v, t, tws);   // consumes the loads
     if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
         const long nb = blockIdx.x + (long)ahead;
         prefetch_signal_part<SLICED, T>(in, nb >> 1, (int)(nb & 1), 2, t);
+        if constexpr (MODE == kSigSqErr) {
+            SigMap tm = in;
+            tm.x = in.target;
+            prefetch_signal_part<false, T>(tm, nb >> 1, (int)(nb & 1), 2, t);
+        }
     }
     spec_stages<C, 2, -1>(v, buf, tws, t, [&](float2 (&w)[P]) {
         stage_store<kQuarter, T, sR<C>(C::NST), sNS<C>(C::NST), SH>(w, buf, t);
@@ -395,13 +410,14 @@ __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
 // shared memory, so every plane value is loaded once.  After that exchange
 // the CTAs work alone: CTA h stores z[2m + h] into y (swapping halves through
 // distributed shared memory for whole-sector stores measured slower).
-template <bool SLICED>
+template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CI::T, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restrict__ qmask,
                     const SigMap out, const float2* __restrict__ ghi,
                     const float2* __restrict__ glo, const float2* __restrict__ gtw,
                     int nplanes, int ahead) {
     using C = CI;
+    constexpr bool SLICED = MODE == kSigSliced;
     constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
     namespace cg = cooperative_groups;
     extern __shared__ float4 smem_raw[];
@@ -498,7 +514,7 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     __syncthreads();
     spec_compute<C, 1, +1>(v, t, tws);
     const float inv = 1.0f / (float)kHalf;
-    if constexpr (!SLICED) {
+    if constexpr (MODE == kSigPlain) {
         // z[2m + h] -> samples 4m + 2h, 4m + 2h + 1
         float2* ys = reinterpret_cast<float2*>(out.y + slice * kSlice);
         spec_stages<C, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
@@ -511,6 +527,38 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
                     ys[2 * nn + h] = cscale(w[b * R + r], inv);
                 }
         });
+    } else if constexpr (MODE == kSigSqErr) {
+        // the same stores, and the squared error against the target summed
+        // in a fixed order: per thread, then a warp butterfly, then the warps
+        // in index order -> one partial per CTA
+        float2* ys = reinterpret_cast<float2*>(out.y + slice * kSlice);
+        const float2* ts = reinterpret_cast<const float2*>(out.target + slice * kSlice);
+        float acc = 0.f;
+        spec_stages<C, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
+            constexpr int R = sR<C>(C::NST), NS = sNS<C>(C::NST);
+#pragma unroll
+            for (int b = 0; b < P / R; ++b)
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int nn = t + T * b + NS * r;
+                    const float2 val = cscale(w[b * R + r], inv);
+                    ys[2 * nn + h] = val;
+                    const float2 tv = __ldg(ts + 2 * nn + h);
+                    const float dx = val.x - tv.x, dy = val.y - tv.y;
+                    acc = fmaf(dx, dx, acc);
+                    acc = fmaf(dy, dy, acc);
+                }
+        });
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+        __shared__ float warp_sum[T / 32];
+        if ((t & 31) == 0) warp_sum[t >> 5] = acc;
+        __syncthreads();
+        if (t == 0) {
+            float sum = 0.f;
+            for (int w = 0; w < T / 32; ++w) sum += warp_sum[w];
+            out.partial[blockIdx.x] = sum;
+        }
     } else {
         // un-roll by +-H and overlap-add into the zeroed output: every output
         // sample receives exactly two terms, and a + b == b + a, so the
@@ -610,33 +658,68 @@ int wave_ctas() {
 }
 }  // namespace
 
+namespace {
+// loss = scale * sum of n partial sums: thread i adds partials i, i + 256, ...
+// in order, then a fixed halving tree (one CTA, deterministic)
+__global__ void __launch_bounds__(256, 1)
+sqerr_finish_kernel(const float* __restrict__ partial, int n, float scale, float* loss) {
+    pdl_launch_dependents();
+    __shared__ float red[256];
+    pdl_wait();   // the partials of the previous kernel are complete
+    const int t = threadIdx.x;
+    float a = 0.f;
+    for (int i = t; i < n; i += 256) a += partial[i];
+    red[t] = a;
+    __syncthreads();
+#pragma unroll
+    for (int w = 128; w > 0; w >>= 1) {
+        if (t < w) red[t] += red[t + w];
+        __syncthreads();
+    }
+    if (t == 0) *loss = scale * red[0];
+}
+}  // namespace
+
+cudaError_t launch_sqerr_finish(const float* partial, int n, float scale, float* loss,
+                                cudaStream_t s) {
+    return launch_pdl(n / 2 <= kPdlMaxBatch, sqerr_finish_kernel, dim3(1), dim3(256), 0, s,
+                      partial, n, scale, loss);
+}
+
 cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& st, int batch,
                                 cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
     const int ahead = wave_ctas();
-    if (in.S > 0)
-        return launch_pdl(batch <= kPdlMaxBatch, spectrum_fwd_kernel<true>, dim3(2 * batch), dim3(CF::T), smemOf<CF>(), s,
-                          in, X, st.hi, st.lo, st.rows, ahead);
-    return launch_pdl(batch <= kPdlMaxBatch, spectrum_fwd_kernel<false>, dim3(2 * batch), dim3(CF::T), smemOf<CF>(), s,
-                      in, X, st.hi, st.lo, st.rows, ahead);
+    auto go = [&](auto kern) {
+        return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_ctas(batch)), dim3(CF::T),
+                          smemOf<CF>(), s, in, X, st.hi, st.lo, st.rows, ahead);
+    };
+    if (in.S > 0) return go(spectrum_fwd_kernel<kSigSliced>);
+    if (in.target) return go(spectrum_fwd_kernel<kSigSqErr>);
+    return go(spectrum_fwd_kernel<kSigPlain>);
 }
 
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
                                 const SpecTables& st, int batch, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
     const int ahead = wave_ctas();
-    if (out.S > 0)
-        return launch_pdl(batch <= kPdlMaxBatch, spectrum_inv_kernel<true>, dim3(2 * batch), dim3(CI::T), smemOf<CI>(), s,
-                          E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
-    return launch_pdl(batch <= kPdlMaxBatch, spectrum_inv_kernel<false>, dim3(2 * batch), dim3(CI::T), smemOf<CI>(), s,
-                      E, tab.qmask, out, st.hi, st.lo, st.rows, tab.nplanes, ahead);
+    auto go = [&](auto kern) {
+        return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_ctas(batch)), dim3(CI::T),
+                          smemOf<CI>(), s, E, tab.qmask, out, st.hi, st.lo, st.rows,
+                          tab.nplanes, ahead);
+    };
+    if (out.S > 0) return go(spectrum_inv_kernel<kSigSliced>);
+    if (out.partial) return go(spectrum_inv_kernel<kSigSqErr>);
+    return go(spectrum_inv_kernel<kSigPlain>);
 }
 
 cudaError_t init_spectrum_attributes() {
-    const void* fwd[] = {(const void*)spectrum_fwd_kernel<false>,
-                         (const void*)spectrum_fwd_kernel<true>};
-    const void* inv[] = {(const void*)spectrum_inv_kernel<false>,
-                         (const void*)spectrum_inv_kernel<true>};
+    const void* fwd[] = {(const void*)spectrum_fwd_kernel<kSigPlain>,
+                         (const void*)spectrum_fwd_kernel<kSigSliced>,
+                         (const void*)spectrum_fwd_kernel<kSigSqErr>};
+    const void* inv[] = {(const void*)spectrum_inv_kernel<kSigPlain>,
+                         (const void*)spectrum_inv_kernel<kSigSliced>,
+                         (const void*)spectrum_inv_kernel<kSigSqErr>};
     for (const void* f : fwd) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              smemOf<CF>());

@@ -33,6 +33,11 @@ using FnSignalFirst = int (*)(const void*, const float*, float*, float*, int, in
 using FnCoefFirst = int (*)(const void*, const float*, const float*, int, float*, int, void*,
                             size_t, void*);
 using FnWorkspace = size_t (*)(const void*, int);
+// cqt_synthesis_sqerr / cqt_adj_synthesis_sqerr (the fused MSE loss)
+using FnSynSqErr = int (*)(const void*, const float*, const float*, int, float*, const float*,
+                           float*, float, int, void*, size_t, void*);
+using FnAdjSynSqErr = int (*)(const void*, const float*, const float*, float, const float*,
+                              float*, float*, int, int, void*, size_t, void*);
 using FnLastError = const char* (*)();
 
 // One filterbank's device tables on one device, with a grow-only workspace.
@@ -46,6 +51,8 @@ struct Ops : torch::CustomClassHolder {
     FnCoefFirst syn = nullptr, adj_an = nullptr;
     FnWorkspace ws_bytes = nullptr;
     FnLastError last_error = nullptr;
+    FnSynSqErr syn_sqerr = nullptr;
+    FnAdjSynSqErr adj_syn_sqerr = nullptr;
     PyObject* owner = nullptr;         // Python object owning `tables` (strong ref)
     at::Tensor ws;
     std::vector<at::Tensor> retired;   // outgrown workspaces: captured graphs may address them
@@ -205,6 +212,42 @@ struct Ops : torch::CustomClassHolder {
         return out;
     }
 
+    // synthesis + the squared-error sum against `target`: (loss = mean of
+    // (y - target)^2 as a 0-dim float32 tensor, y)
+    std::vector<at::Tensor> synthesis_sqerr(const at::Tensor& c_, const at::Tensor& target_) {
+        at::Tensor c = coef(c_, "coefficients");
+        const int64_t B = c.size(0);
+        at::Tensor tgt = signal(target_, "target");
+        TORCH_CHECK_VALUE(tgt.size(0) == B, "target must be [", B, ", ", kN, "], got ",
+                          tgt.sizes());
+        DeviceSwitch sw(device);
+        at::Tensor y = at::empty({B, kN}, c.options().dtype(at::kFloat));
+        at::Tensor loss = at::empty({}, c.options().dtype(at::kFloat));
+        size_t wb;
+        void* w = workspace(B, &wb);
+        const float scale = B > 0 ? (float)(1.0 / ((double)B * (double)kN)) : 0.f;
+        check(syn_sqerr(tables, reinterpret_cast<const float*>(c.data_ptr()), nullptr,
+                        kLayoutComplex, y.data_ptr<float>(), tgt.data_ptr<float>(),
+                        loss.data_ptr<float>(), scale, (int)B, w, wb, stream()),
+              "cqt_synthesis_sqerr");
+        return {loss, y, tgt};
+    }
+
+    // transpose of the synthesis applied to scale * (*g) * (y - target)
+    at::Tensor adj_synthesis_sqerr(const at::Tensor& y, const at::Tensor& tgt, float scale,
+                                   const at::Tensor& g) {
+        DeviceSwitch sw(device);
+        const int64_t B = y.size(0);
+        at::Tensor out = at::empty({B, ncoef}, y.options().dtype(at::kComplexFloat));
+        size_t wb;
+        void* w = workspace(B, &wb);
+        check(adj_syn_sqerr(tables, y.data_ptr<float>(), tgt.data_ptr<float>(), scale,
+                            g.data_ptr<float>(), reinterpret_cast<float*>(out.data_ptr()),
+                            nullptr, kLayoutComplex, (int)B, w, wb, stream()),
+              "cqt_adj_synthesis_sqerr");
+        return out;
+    }
+
     at::Tensor adj_synthesis(const at::Tensor& gy_) {
         at::Tensor gy = signal(gy_, "signal gradient");
         DeviceSwitch sw(device);
@@ -251,13 +294,43 @@ struct SynthesisFn : public torch::autograd::Function<SynthesisFn> {
     }
 };
 
+// synthesis + mean squared error against a target: outputs (loss, y), y not
+// differentiable (it is a by-product for the caller); the backward runs the
+// transpose of the synthesis with dL/dy = 2 dL/dloss (y - target) / n formed
+// inside the kernel's load -- no elementwise loss kernels between the engines
+struct SynthesisMSEFn : public torch::autograd::Function<SynthesisMSEFn> {
+    static torch::autograd::variable_list forward(torch::autograd::AutogradContext* ctx,
+                                                  const at::Tensor& c, const at::Tensor& target,
+                                                  const c10::intrusive_ptr<Ops>& ops) {
+        ctx->saved_data["ops"] = c10::IValue::make_capsule(ops);
+        std::vector<at::Tensor> r = ops->synthesis_sqerr(c, target);
+        ctx->saved_data["y"] = r[1];
+        ctx->saved_data["t"] = r[2];
+        ctx->mark_non_differentiable({r[1]});
+        return {r[0], r[1]};
+    }
+    static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                   torch::autograd::variable_list g) {
+        if (!g[0].defined()) return {at::Tensor(), at::Tensor(), at::Tensor()};
+        Ops* o = ops_of(ctx);
+        at::Tensor y = ctx->saved_data.at("y").toTensor();
+        at::Tensor t = ctx->saved_data.at("t").toTensor();
+        at::Tensor gl = g[0].to(y.options()).contiguous();
+        const float scale = y.numel() > 0 ? (float)(2.0 / (double)y.numel()) : 0.f;
+        at::Tensor gc = o->adj_synthesis_sqerr(y, t, scale, gl);
+        at::Tensor gt;
+        if (ctx->needs_input_grad(1)) gt = (y - t) * (gl * -scale);
+        return {gc, gt, at::Tensor()};
+    }
+};
+
 // Python handle of an Ops
 struct Handle {
     c10::intrusive_ptr<Ops> ops;
 
     Handle(uintptr_t tables, int device, int64_t ncoef, uintptr_t an, uintptr_t syn,
            uintptr_t adj_an, uintptr_t adj_syn, uintptr_t ws_bytes, uintptr_t last_error,
-           pybind11::object owner, std::vector<int64_t> bins, std::vector<int64_t> lens,
+           uintptr_t syn_sqerr, uintptr_t adj_syn_sqerr, pybind11::object owner, std::vector<int64_t> bins, std::vector<int64_t> lens,
            int64_t ngroups)
         : ops(c10::make_intrusive<Ops>()) {
         TORCH_CHECK(bins.size() == lens.size() && ngroups <= (int64_t)bins.size(),
@@ -272,6 +345,8 @@ struct Handle {
         o.adj_syn = reinterpret_cast<FnSignalFirst>(adj_syn);
         o.ws_bytes = reinterpret_cast<FnWorkspace>(ws_bytes);
         o.last_error = reinterpret_cast<FnLastError>(last_error);
+        o.syn_sqerr = reinterpret_cast<FnSynSqErr>(syn_sqerr);
+        o.adj_syn_sqerr = reinterpret_cast<FnAdjSynSqErr>(adj_syn_sqerr);
         o.owner = owner.release().ptr();   // the strong reference moves into Ops
         int64_t total = 0;
         for (size_t i = 0; i < bins.size(); ++i) {
@@ -305,6 +380,11 @@ struct Handle {
     // differentiable heap <-> signal, no per-group views
     at::Tensor analysis_heap(const at::Tensor& x) { return AnalysisFn::apply(x, ops); }
     at::Tensor synthesis_heap(const at::Tensor& h) { return SynthesisFn::apply(h, ops); }
+    // heap [B, ncoef] and target [B, 65536] -> (mean squared error, y)
+    pybind11::tuple mse(const at::Tensor& h, const at::Tensor& target) {
+        torch::autograd::variable_list r = SynthesisMSEFn::apply(h, target, ops);
+        return pybind11::make_tuple(r[0], r[1]);
+    }
 
     // TrainableCQT.fwd: x [..., 65536] -> (blocks [..., b, M], side [..., 1, M])
     pybind11::tuple fwd(const at::Tensor& x) {
@@ -356,8 +436,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "torch fast path of the flash_cqt_b200 C ABI";
     pybind11::class_<Handle>(m, "Handle")
         .def(pybind11::init<uintptr_t, int, int64_t, uintptr_t, uintptr_t, uintptr_t, uintptr_t,
-                            uintptr_t, uintptr_t, pybind11::object, std::vector<int64_t>,
-                            std::vector<int64_t>, int64_t>())
+                            uintptr_t, uintptr_t, uintptr_t, uintptr_t, pybind11::object,
+                            std::vector<int64_t>, std::vector<int64_t>, int64_t>())
         .def("workspace", &Handle::workspace)
         .def("analysis", &Handle::analysis)
         .def("analysis_planar", &Handle::analysis_planar)
@@ -367,6 +447,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("adj_synthesis", &Handle::adj_synthesis)
         .def("analysis_heap", &Handle::analysis_heap)
         .def("synthesis_heap", &Handle::synthesis_heap)
+        .def("mse", &Handle::mse)
         .def("fwd", &Handle::fwd)
         .def("last_heap", &Handle::last_heap);
 }

@@ -38,8 +38,14 @@ class Partition:
 
     def __init__(self, length, S, rank, world, hop=32768):
         self.length, self.S, self.rank, self.world, self.hop = length, S, rank, world, hop
-        self.s0, self.s1 = slice_ranges(S, world)[rank]
+        ranges = slice_ranges(S, world)
+        self.s0, self.s1 = ranges[rank]
         self.nslices = self.s1 - self.s0
+        # with fewer slices than ranks the trailing ranks own nothing; the
+        # halo exchange pairs a rank with its right neighbour only when that
+        # neighbour has slices (it alone sends), so both sides agree
+        self.right_nslices = (ranges[rank + 1][1] - ranges[rank + 1][0]
+                              if rank + 1 < world else 0)
 
     def input_window(self):
         """global input samples the rank's slices read: [start, stop)"""
@@ -51,8 +57,9 @@ class Partition:
         return self.hop * (self.s0 - 1), self.hop * self.s1
 
     def owned(self):
-        """global output samples the rank owns after the halo exchange"""
-        lo = self.hop * self.s0
+        """global output samples the rank owns after the halo exchange
+        (empty, at the signal's end, for a rank whose slices start past it)"""
+        lo = min(self.hop * self.s0, self.length)
         hi = min(self.hop * self.s1, self.length)
         return lo, max(lo, hi)
 
@@ -62,14 +69,17 @@ def exchange_halo(local, part, group=None):
     ``part.synthesis_window()``.  Sends the first hop to rank - 1, adds the
     hop received from rank + 1 into the last owned hop, and returns the owned
     part (a view of `local`).  Every rank makes the same calls in the same
-    order (ranks with no neighbour skip the matching side)."""
+    order.  A rank sends only if it owns slices, and receives only from a right
+    neighbour that owns slices, so a stream of fewer slices than ranks leaves
+    no receive without its send (the trailing ranks own nothing and take no
+    part)."""
     H2 = part.hop
     ops = []
     recv = None
     if part.rank > 0 and part.nslices > 0:
         ops.append(dist.P2POp(dist.isend, local[:, :H2].contiguous(), part.rank - 1,
                               group=group))
-    if part.rank + 1 < part.world:
+    if part.right_nslices > 0:
         recv = torch.empty(local.shape[0], H2, dtype=local.dtype, device=local.device)
         ops.append(dist.P2POp(dist.irecv, recv, part.rank + 1, group=group))
     if ops:
@@ -107,8 +117,11 @@ class PartitionedSlicedCQT:
         se = self.sl._fused(x.device)
         if se is None:
             raise RuntimeError("the partitioned transform needs the default CUDA engine")
-        buf = se.analysis(x.reshape(B * C, -1), p.nslices, slice0=p.s0,
-                          sample0=sample0, length=length)
+        if p.nslices == 0:   # a trailing rank of a stream shorter than the world
+            buf = torch.empty(0, dtype=torch.complex64, device=x.device)
+        else:
+            buf = se.analysis(x.reshape(B * C, -1), p.nslices, slice0=p.s0,
+                              sample0=sample0, length=length)
         return se.group_views(buf, (B, C), p.nslices)
 
     def bwd(self, blocks, side, length):
@@ -116,10 +129,13 @@ class PartitionedSlicedCQT:
         output samples [B, C, owned]"""
         B, C = blocks[0].shape[:2]
         p = self.partition(length)
-        se = self.sl._fused(blocks[0].device)
-        buf = self.sl._fused_buffer(se, blocks, side, B * C, p.nslices)
         lo, hi = p.synthesis_window()
-        local = se.synthesis(buf, B * C, p.nslices, length, slice0=p.s0, sample0=lo,
-                             count=hi - lo)
+        if p.nslices == 0:   # nothing to synthesise; still takes its (empty) part
+            local = torch.zeros(B * C, hi - lo, device=blocks[0].device)
+        else:
+            se = self.sl._fused(blocks[0].device)
+            buf = self.sl._fused_buffer(se, blocks, side, B * C, p.nslices)
+            local = se.synthesis(buf, B * C, p.nslices, length, slice0=p.s0, sample0=lo,
+                                 count=hi - lo)
         own = exchange_halo(local, p, self.group)
         return own.reshape(B, C, -1)

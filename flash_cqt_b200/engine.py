@@ -54,7 +54,8 @@ class Engine:
                 self.tables.handle.value, self.dev.index, self.ncoef,
                 *[_native.fn_address(n) for n in (
                     "cqt_analysis", "cqt_synthesis", "cqt_adj_analysis",
-                    "cqt_adj_synthesis", "cqt_workspace_bytes", "cqt_last_error")],
+                    "cqt_adj_synthesis", "cqt_workspace_bytes", "cqt_last_error",
+                    "cqt_synthesis_sqerr", "cqt_adj_synthesis_sqerr")],
                 self.tables, [b for b, _, _ in heap.gspec], [M for _, M, _ in heap.gspec],
                 ngo)
 
@@ -180,6 +181,48 @@ class Engine:
         self._run("cqt_adj_synthesis", gy.data_ptr(), out.data_ptr(), None,
                   _native.CQT_LAYOUT_COMPLEX, B)
         return out
+
+    # -------------------------------------------------------- squared error
+    def synthesis_sqerr(self, c, target):
+        """coefficient heap [B, ncoef] and target [B, 65536] -> (loss, y):
+        y = synthesis(c), loss = mean((y - target)^2) as a 0-dim float32
+        tensor, summed in a fixed order inside the engines."""
+        c = self._coef(c, "coefficients")
+        B = c.shape[0]
+        target = self._signal(target, "target")
+        if target.shape[0] != B:
+            raise ValueError(f"target must be [{B}, {N}], got {tuple(target.shape)}")
+        y = torch.empty(B, N, dtype=torch.float32, device=self.dev)
+        loss = torch.empty((), dtype=torch.float32, device=self.dev)
+        self._run_sqerr(c.data_ptr(), y.data_ptr(), target.data_ptr(), loss.data_ptr(),
+                        1.0 / (B * N) if B else 0.0, B)
+        return loss, y, target
+
+    def adj_synthesis_sqerr(self, y, target, scale, g):
+        """transpose of the synthesis applied to scale * g * (y - target), g a
+        device float32 scalar tensor (e.g. dL/dloss)"""
+        B = y.shape[0]
+        out = torch.empty(B, self.ncoef, dtype=torch.complex64, device=self.dev)
+        if torch.cuda.current_device() != self.dev.index:
+            with torch.cuda.device(self.dev):
+                return self.adj_synthesis_sqerr(y, target, scale, g)
+        ws = self.workspace(B)
+        rc = _native.lib().cqt_adj_synthesis_sqerr(
+            self.tables.handle, y.data_ptr(), target.data_ptr(), float(scale), g.data_ptr(),
+            out.data_ptr(), None, _native.CQT_LAYOUT_COMPLEX, B, ws.data_ptr(), ws.numel(),
+            _raw_stream_of(self.dev.index))
+        _native._check(rc, "cqt_adj_synthesis_sqerr")
+        return out
+
+    def _run_sqerr(self, c, y, target, loss, scale, B):
+        if torch.cuda.current_device() != self.dev.index:
+            with torch.cuda.device(self.dev):
+                return self._run_sqerr(c, y, target, loss, scale, B)
+        ws = self.workspace(B)
+        rc = _native.lib().cqt_synthesis_sqerr(
+            self.tables.handle, c, None, _native.CQT_LAYOUT_COMPLEX, y, target, loss,
+            float(scale), B, ws.data_ptr(), ws.numel(), _raw_stream_of(self.dev.index))
+        _native._check(rc, "cqt_synthesis_sqerr")
 
     # ------------------------------------------------------------------ planar
     def analysis_planar(self, x, kr, ki):

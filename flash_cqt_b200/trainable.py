@@ -47,6 +47,29 @@ class _Synthesis(torch.autograd.Function):
         return ctx.eng.adj_synthesis(gy.contiguous()), None
 
 
+class _SynthesisMSE(torch.autograd.Function):
+    """synthesis + mean squared error: (loss, y), y not differentiable; the
+    backward folds dL/dy = 2 dL/dloss (y - target) / n into the load of the
+    transposed synthesis (cqt_adj_synthesis_sqerr)"""
+
+    @staticmethod
+    def forward(ctx, c, target, eng):
+        ctx.eng = eng
+        loss, y, t = eng.synthesis_sqerr(c, target)
+        ctx.y, ctx.t = y, t
+        ctx.mark_non_differentiable(y)
+        return loss, y
+
+    @staticmethod
+    def backward(ctx, gl, _gy):
+        y, t = ctx.y, ctx.t
+        scale = 2.0 / y.numel() if y.numel() else 0.0
+        gl = gl.to(device=y.device, dtype=torch.float32).contiguous()
+        gc = ctx.eng.adj_synthesis_sqerr(y, t, scale, gl)
+        gt = (y - t) * (gl * -scale) if ctx.needs_input_grad[1] else None
+        return gc, gt, None
+
+
 def _engine_for(cqt, device):
     """One Engine per (filterbank, device), cached on the OctCQT object."""
     dev = torch.device(device) if device is not None else None
@@ -142,6 +165,35 @@ class TrainableCQT:
             return y if len(lead) == 1 else y.reshape(*lead, N)
         h = self.heap_of(blocks, side)
         return _Synthesis.apply(h, self.eng).reshape(*lead, N)
+
+    def mse_loss(self, blocks, side, target, return_output=False):
+        """``((self.bwd(blocks, side) - target) ** 2).mean()`` -- the loss of the
+        reference's train step -- with the loss and its gradient folded into
+        the engines: the synthesis sums the squared error as it stores y, and
+        the backward forms 2 (y - target) / n inside the transposed
+        synthesis' load (no elementwise kernels in between).  target
+        [..., 65536] float32 like the output; returns the 0-dim loss, or
+        (loss, y) with ``return_output`` (y carries no gradient)."""
+        lead = blocks[0].shape[:-2]
+        B = 1
+        for d in lead:
+            B *= d
+        if tuple(target.shape) != (*lead, N):
+            raise ValueError(f"target must be {(*lead, N)}, got {tuple(target.shape)}")
+        ops = self.eng._ops
+        h = None
+        if ops is not None and side is not None:
+            h = ops.last_heap(list(blocks) + list(side))
+        if h is None:
+            h = self.heap_of(blocks, side)
+        t2 = target if target.dim() == 2 else target.reshape(B, N)
+        if ops is not None:
+            loss, y = ops.mse(h, t2)
+        else:
+            loss, y = _SynthesisMSE.apply(h, t2, self.eng)
+        if return_output:
+            return loss, (y if len(lead) == 1 else y.reshape(*lead, N))
+        return loss
 
     # flat-heap entry points (no per-group views), used by the fused sliced path
     def analysis_heap(self, x):

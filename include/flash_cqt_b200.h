@@ -133,6 +133,31 @@ int cqt_adj_synthesis(const cqt_tables* t, const float* gy, float* g_re,
                       float* g_im, int layout, int batch, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* MSE training loss folded into the engines (the optional fused MSE of the
+ * adjoint-synthesis entry point; the reference runs the loss and its
+ * gradient as separate torch operations between its engines, the train step
+ * of bench/profile_step.py and trainable.py:180-191).
+ *
+ * cqt_synthesis_sqerr: y = synthesis(coefficients) exactly as cqt_synthesis,
+ * and *loss (one device float) = loss_scale * sum over all batch * 65536
+ * samples of (y - target)^2, summed in a fixed order (deterministic; the
+ * mean is loss_scale = 1 / (batch * 65536)).  target as y (8-byte aligned).
+ * An empty batch writes 0.
+ *
+ * cqt_adj_synthesis_sqerr: the transpose of the synthesis (as
+ * cqt_adj_synthesis) applied to dL/dy = s * (y - target), formed while the
+ * signal is loaded, with s = scale * (*scale_dev) (scale_dev: an optional
+ * device float such as the loss gradient dL/dloss; NULL means 1).  For the
+ * mean squared error, scale = 2 / (batch * 65536). */
+int cqt_synthesis_sqerr(const cqt_tables* t, const float* c_re, const float* c_im,
+                        int layout, float* y, const float* target, float* loss,
+                        float loss_scale, int batch, void* workspace,
+                        size_t workspace_bytes, void* stream);
+int cqt_adj_synthesis_sqerr(const cqt_tables* t, const float* y, const float* target,
+                            float scale, const float* scale_dev, float* g_re,
+                            float* g_im, int layout, int batch, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Diagnostic: launch one kernel of the pipeline on its own, for per-kernel
  * timing and profiling.  stage: 0 spectrum_fwd (in = signal, out = workspace
  * spectrum), 1 bands_fwd analysis (in = workspace spectrum, out = coefficients
@@ -154,9 +179,12 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in,
  * Scratch comes from a static device array inside this library sized for at
  * most 8 slices (batch > 8 returns CQT_ERR_ARG); every GPU that loads the
  * library holds those 2 MiB until exit.  The first call on a device (that
- * device current) looks the array up with cudaGetSymbolAddress: make it
- * before any stream capture.  All calls share the array: calls that overlap
- * on the GPU race.  Allocates nothing, never synchronises. */
+ * device current) looks the array up with cudaGetSymbolAddress, which may
+ * make the CUDA runtime load this library's device code and so allocate and
+ * synchronise: make one warm-up call per device at start-up, off the
+ * real-time thread and before any stream capture (batch 0 suffices).  After
+ * it, calls allocate nothing and never synchronise.  All calls share the
+ * array: calls that overlap on the GPU race. */
 int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* c_re,
                          float* c_im, int layout, int batch, void* stream);
 

@@ -116,8 +116,8 @@ def test_torch_fast_path_raises_python_errors():
     class Owner:
         pass
 
-    h = mod.Handle(0, 0, 10, 1, 1, 1, 1, 1, _native.fn_address("cqt_last_error"), Owner(),
-                   [2, 2], [3, 2], 1)
+    h = mod.Handle(0, 0, 10, 1, 1, 1, 1, 1, _native.fn_address("cqt_last_error"), 1, 1,
+                   Owner(), [2, 2], [3, 2], 1)
     cases = ((h.analysis, torch.zeros(1, 65536)),
              (h.synthesis, torch.zeros(1, 10, dtype=torch.complex64)),
              (h.adj_analysis, torch.zeros(1, 10, dtype=torch.complex64)),
@@ -125,6 +125,8 @@ def test_torch_fast_path_raises_python_errors():
     for fn, t in cases:
         with pytest.raises(ValueError, match="must be a tensor on cuda:0"):
             fn(t)
+    with pytest.raises(ValueError, match="must be a tensor on cuda:0"):
+        h.mse(torch.zeros(1, 10, dtype=torch.complex64), torch.zeros(1, 65536))
     p = torch.zeros(1, 10)
     with pytest.raises(ValueError, match="must be a tensor on cuda:0"):
         h.analysis_planar(torch.zeros(1, 65536), p, p)

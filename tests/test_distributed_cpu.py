@@ -28,7 +28,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _local_synthesis(so, coef_per_slice, part):
+def _local_synthesis(so, coef_per_slice, part, L=L):
     """the rank's overlap-add over part.synthesis_window() from the oracle's
     per-slice inverses (un-rolled by +-H by slice parity)"""
     lo, hi = part.synthesis_window()
@@ -42,7 +42,7 @@ def _local_synthesis(so, coef_per_slice, part):
     return out
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, L=L):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -61,7 +61,7 @@ def _worker(rank, world, port, q):
         coef = [[c[None] for c in so.cqt.fwd(sl[g][None])] for g in range(S)]
         coef = [[c[0] for c in cs] for cs in coef]
         part = Partition(L, S, rank, world)
-        local = torch.from_numpy(_local_synthesis(so, coef, part))
+        local = torch.from_numpy(_local_synthesis(so, coef, part, L))
         own = exchange_halo(local, part)
         lo, hi = part.owned()
         q.put((rank, lo, hi, own.numpy().copy()))
@@ -69,14 +69,16 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_partitioned_overlap_add_equals_whole_buffer(world):
+# (3, 30000) and (4, 30000): a 2-slice stream on more ranks than slices, so
+# the trailing ranks own nothing and must not be waited for
+@pytest.mark.parametrize("world,L", [(2, L), (3, L), (3, 30000), (4, 30000)])
+def test_partitioned_overlap_add_equals_whole_buffer(world, L):
     from oracle.cqt_oracle import SlicedOracle
     from signals import chirp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, L)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=300) for _ in range(world)]

@@ -34,12 +34,14 @@ def eng():
                               torch.device("cuda:0"))
 
 
-def _noalloc(eng, x, out):
+def _noalloc(eng, x, out, out_im=None, layout=None):
     from flash_cqt_b200 import _native
     L = _native.lib()
+    if layout is None:
+        layout = _native.CQT_LAYOUT_COMPLEX
+    im = ctypes.c_void_p(out_im.data_ptr()) if out_im is not None else None
     rc = L.cqt_analysis_noalloc(eng.tables.handle, ctypes.c_void_p(x.data_ptr()),
-                                ctypes.c_void_p(out.data_ptr()), None,
-                                _native.CQT_LAYOUT_COMPLEX, x.shape[0],
+                                ctypes.c_void_p(out.data_ptr()), im, layout, x.shape[0],
                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     return rc, L.cqt_last_error().decode()
 
@@ -58,6 +60,57 @@ def test_noalloc_matches_workspace_entry_point_twice(eng):
         assert snr_db(w, h) >= COEF_DB
         for b in range(batch):
             assert snr_db(w[b], h[b]) >= COEF_DB, b
+
+
+def test_noalloc_stale_nan_scratch_does_not_leak(eng):
+    """a call on NaN input leaves NaN in every scratch row; the next call, on
+    finite input and fewer slices, must still be finite and exact"""
+    nan_x = torch.full((8, 65536), float("nan"), device=eng.dev)
+    junk = torch.empty(8, eng.ncoef, dtype=torch.complex64, device=eng.dev)
+    rc, msg = _noalloc(eng, nan_x, junk)
+    assert rc == 0, msg
+    g = torch.Generator(device="cpu").manual_seed(7)
+    x = torch.randn(3, 65536, generator=g).to(eng.dev)
+    got = torch.full((3, eng.ncoef), float("nan"), dtype=torch.complex64, device=eng.dev)
+    rc, msg = _noalloc(eng, x, got)
+    assert rc == 0, msg
+    want = eng.analysis(x)
+    torch.cuda.synchronize()
+    h = got.cpu().numpy()
+    assert np.isfinite(h).all()
+    assert snr_db(want.cpu().numpy(), h) >= COEF_DB
+
+
+def test_noalloc_planar_layout(eng):
+    from flash_cqt_b200 import _native
+    g = torch.Generator(device="cpu").manual_seed(11)
+    x = torch.randn(5, 65536, generator=g).to(eng.dev)
+    kr = torch.full((5, eng.ncoef), float("nan"), device=eng.dev)
+    ki = torch.full((5, eng.ncoef), float("nan"), device=eng.dev)
+    rc, msg = _noalloc(eng, x, kr, ki, _native.CQT_LAYOUT_PLANAR)
+    assert rc == 0, msg
+    want = eng.analysis(x)
+    torch.cuda.synchronize()
+    got = torch.complex(kr, ki).cpu().numpy()
+    assert np.isfinite(got).all()
+    assert snr_db(want.cpu().numpy(), got) >= COEF_DB
+
+
+def test_noalloc_allocates_nothing_after_warmup(eng):
+    """after the warm-up call (batch 0: address lookup only), a call leaves
+    the device's free memory unchanged -- nothing is allocated for it"""
+    x = torch.randn(8, 65536, device=eng.dev)
+    out = torch.empty(8, eng.ncoef, dtype=torch.complex64, device=eng.dev)
+    rc, msg = _noalloc(eng, x[:0], out[:0])
+    assert rc == 0, msg
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(eng.dev)
+    for _ in range(3):
+        rc, msg = _noalloc(eng, x, out)
+        assert rc == 0, msg
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(eng.dev)
+    assert free1 == free0, (free0, free1)
 
 
 def test_noalloc_rejects_batches_above_its_scratch(eng):
