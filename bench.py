@@ -43,6 +43,9 @@ def parse():
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the batch sweep, train step, e2e and CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--reference-gpu-only", action="store_true",
+                    help="run only the same-box GPU baseline of the reference's own "
+                         "kernels and print it")
     ap.add_argument("--sliced-only", action="store_true",
                     help="run only the config-5 long-stream measurement and print its "
                          "result (for profiling the sliced kernels)")
@@ -120,22 +123,60 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- reference arm
+REF_ARM_SECONDS = 150.0   # bound on the whole --impl reference run
+
+
+def reference_round_trip():
+    """(round_trip(x), describe) of the reference's own CPU path: the unmodified
+    ``OctCQT.fwd`` -> ``.bwd`` (oct_cqt.py:84-117) imported from the build in
+    oracle/_ref when present, else the torch restatement in oracle/cpu_port.py"""
+    import torch
+    from oracle import ref_loader
+    from oracle.cpu_port import cpu_model
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    if ref_loader.available():
+        fc = ref_loader.package()
+        cqt = fc.OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=N)
+
+        @torch.no_grad()
+        def rt(x):
+            return cqt.bwd(*cqt.fwd(x))
+        return rt, "reference", threads, ("the reference's unmodified OctCQT.fwd -> .bwd "
+                                          "(byte-compiled from its sources, oracle/build_ref.py) "
+                                          f"on {cpu_model()}")
+    from oracle.cpu_port import CPUPort
+    port = CPUPort(threads)
+    return port.round_trip, "port", threads, ("torch CPU float32 restatement of "
+                                              f"OctCQT.fwd/bwd (oracle/cpu_port.py) on {cpu_model()}")
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
-    from oracle.cpu_port import CPUPort, cpu_model
     import torch
-    port = CPUPort()
-    B = 16   # bounded sample of the workload per step
+    rt, kind, cores, what = reference_round_trip()
     g = torch.Generator().manual_seed(4)
+    # per-slice cost from a small warm-up, then the largest per-step batch (up
+    # to the GPU arm's) that keeps the whole run inside REF_ARM_SECONDS
+    probe = torch.randn(16, N, generator=g)
+    rt(probe)
+    t0 = time.perf_counter()
+    rt(probe)
+    per_slice = (time.perf_counter() - t0) / 16
+    B = args.batch
+    budget = REF_ARM_SECONDS / max(1, args.steps + args.warmup)
+    while B > 16 and B * per_slice > budget:
+        B //= 2
     x = torch.randn(B, N, generator=g)
     for _ in range(max(args.warmup, 1)):
-        port.round_trip(x)
+        rt(x)
     ts = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        port.round_trip(x)
+        y = rt(x)
         ts.append(time.perf_counter() - t0)
+    err = float(((y.double() - x.double()) ** 2).sum() / (x.double() ** 2).sum())
     tot = sum(ts)
     value = B * args.steps / tot
     line = {
@@ -143,18 +184,125 @@ def run_reference(args, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "FusedOctCQT round trip, OctCQT([3,4,2],[8,16,32]) "
-                               "65536-sample N(0,1) slices (config 4)",
-                   "global_batch": B, "seq_len": N, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "round_trips/s",
-                         "cores": port.threads, "kind": "port",
-                         "sample": f"{args.steps} round trips of {B} slices on the host "
-                                   f"({cpu_model()}), torch CPU float32 restatement "
-                                   "of OctCQT.fwd/bwd"},
+        "config": {"workload": "FusedOctCQT round trip (analysis + synthesis), "
+                               "OctCQT([3,4,2],[8,16,32]) fs 44100, 65536-sample N(0,1) "
+                               "slices (config 4)",
+                   "global_batch": B, "per_gpu_batch": args.batch if B == args.batch else B,
+                   "seq_len": N, "parallelism": "cpu, rank 0 only",
+                   "same_batch_as_gpu_arm": B == args.batch,
+                   "note": "per-step batch lowered only to keep the run within "
+                           f"{REF_ARM_SECONDS:.0f} s; per-slice CPU throughput is flat "
+                           "above ~64 slices"},
+        "round_trip_snr_db": -10 * math.log10(err),
+        "cpu_baseline": {"value": value, "unit": "round_trips/s", "cores": cores,
+                         "kind": kind,
+                         "sample": f"{args.steps} round trips of {B} slices, {what}"},
         "e2e": {"value": value, "unit": "round_trips/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(seconds):
+    """the reference's CPU path timed on the host for ~`seconds` (bounded
+    sample: 64-slice round trips) -- the cpu_baseline object of the GPU arm"""
+    import torch
+    rt, kind, cores, what = reference_round_trip()
+    B = 64
+    x = torch.randn(B, N, generator=torch.Generator().manual_seed(4))
+    rt(x)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        y = rt(x)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    err = float(((y.double() - x.double()) ** 2).sum() / (x.double() ** 2).sum())
+    return {"value": B * calls / el, "unit": "round_trips/s", "cores": cores, "kind": kind,
+            "sample": "%d calls of a %d-slice round trip (%.0f s), %s, %.1f dB"
+                      % (calls, B, el, what, -10 * math.log10(err))}
+
+
+def reference_gpu(dev, batches=(1, 64, 256, 1024), reps=20):
+    """Same-box GPU baseline of the reference's own CUDA kernels (built from
+    its sources for sm_100a by oracle/build_ref.py): its TrainableCQT factored
+    round trip (fft3 + radix bands, trainable.py:75-109) under CUDA-graph
+    replay, and its factored resident pair (persist2.cu fwd2 + inv2, one
+    cooperative launch per direction, driven as bench/resident2.py does).
+    Reported beside this build's own graphed round trip; never part of the
+    timed product path."""
+    import torch
+    from oracle import ref_loader
+    if not ref_loader.available(cuda=True):
+        return {"unavailable": "reference not built here (python oracle/build_ref.py)"}
+    fc = ref_loader.package(cuda=True)
+    from flash_cqt.trainable import TrainableCQT as RefTrainable
+    import flash_cqt.fused as rfused
+    cqt = fc.OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=N, device=dev)
+    rt_ = RefTrainable(cqt, dev)
+    f, rx = rt_.f, rt_.f.radix
+    p2 = rfused._P2EXT
+    w32r, w32i = rt_.FR[1].contiguous(), rt_.FI[1].contiguous()
+    out = {}
+
+    def graphed(fn):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            res = fn()
+        return g, res
+
+    def timed(run):
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            run()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / reps
+
+    def snr(x, y):
+        return float(10 * torch.log10((x.double() ** 2).sum() / ((y.double() - x.double()) ** 2).sum()))
+
+    for B in batches:
+        x = torch.randn(B, N, device=dev, generator=torch.Generator(device=dev).manual_seed(4))
+        with torch.no_grad():
+            g, y = graphed(lambda: rt_._synthesis(*rt_._analysis(x)))
+            ms_f = timed(g.replay)
+            s_f = snr(x, y)
+            del g
+            w = f._workspace(B)
+            pl = [torch.empty(B, N // 2, device=dev) for _ in range(4)]
+            args = (x, w["KR"], w["KI"], w["FR"], w["FI"], w["XO"], *pl, w32r, w32i,
+                    rt_.WLR, rt_.WLI, rt_.WKR, rt_.WKI, rt_.WNR, rt_.WNI,
+                    rx["desc"], rx["route"], rx["gdv"], rx["pos"], rx["rr"], rx["ri"],
+                    f.ncoef, B)
+
+            def resident():
+                p2.fwd2(*args)
+                p2.inv2(*args)
+            ms_r = timed(resident)
+            s_r = snr(x, w["XO"])
+        out[str(B)] = {"trainable_factored_graphed": {"ms": ms_f, "round_trips_per_s": B / (ms_f / 1e3),
+                                                       "snr_db": s_f},
+                       "resident_pair_persist2": {"ms": ms_r, "round_trips_per_s": B / (ms_r / 1e3),
+                                                  "snr_db": s_r}}
+        del w, pl, args
+        f._ws.clear()
+        rt_.scr.clear()
+        torch.cuda.empty_cache()
+    out["what"] = ("the reference's own kernels (packedfft.cu, radix.cu, persist2.cu) "
+                   "built for sm_100a from its sources, run on this GPU")
+    return out
 
 
 # -------------------------------------------------------------------- b200
@@ -197,6 +345,13 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.reference_gpu_only:
+        if rank == 0:
+            print(json.dumps({"reference_gpu": reference_gpu(dev)}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.sliced_only:
         pk = ROOT / "MEASURED_PEAKS.json"
         hbm = (json.loads(pk.read_text()).get("hbm_gbs") if pk.exists() else None) or 6650.0
@@ -336,14 +491,7 @@ def main():
     if not args.no_extras:
         line.update(extras(args, eng, t, dev, world, rank, barrier, W, K, hbm))
         if world == 1 and rank == 0:
-            from oracle.cpu_port import time_round_trips
-            r = time_round_trips(batch=16, seconds=args.cpu_seconds)
-            line["cpu_baseline"] = {
-                "value": r["round_trips_per_s"], "unit": "round_trips/s",
-                "cores": r["threads"], "kind": "port",
-                "sample": "%d calls of a 16-slice round trip (~%.0f s) on %s, torch CPU "
-                          "float32 restatement of OctCQT.fwd/bwd, %.1f dB"
-                          % (r["calls"], args.cpu_seconds, r["cpu"], r["snr_db"])}
+            line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -512,6 +660,19 @@ def extras(args, eng, t, dev, world, rank, barrier, W, K, hbm=6549.1):
         sweep[str(Bs)] = {"ms": med, "round_trips_per_s": Bs / (med / 1e3)}
         del gg
     out["sweep_per_gpu"] = sweep
+    # same-box GPU baseline: the reference's own factored kernels and its
+    # resident pair, built from its sources (oracle/build_ref.py)
+    if world == 1:
+        try:
+            rg = reference_gpu(dev)
+        except Exception as e:   # a missing build or a failure here must not hide the run
+            rg = {"unavailable": f"{type(e).__name__}: {e}"}
+        for Bs, r in list(rg.items()):
+            if isinstance(r, dict) and Bs in sweep:
+                best = max(v["round_trips_per_s"] for v in r.values())
+                r["this_build_round_trips_per_s"] = sweep[Bs]["round_trips_per_s"]
+                r["this_build_over_best_reference"] = sweep[Bs]["round_trips_per_s"] / best
+        out["reference_gpu"] = rg
     # ---- config 2: one slice of 8 seeded sinusoids (log-uniform 43 Hz - 20 kHz,
     # amplitudes U(0.1, 1), phases U(0, 2 pi)) + N(0, 0.01^2) noise, graphed
     # round trip and its reconstruction SNR

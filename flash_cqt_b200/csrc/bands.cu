@@ -40,7 +40,17 @@ namespace {
 
 constexpr int kP = kBandP;
 constexpr int kSH = kP == 32 ? 5 : 4;                    // shared padding shift
-constexpr int kBandData = padded<kSH>(kBandCap);         // float2 per CTA
+// shared-memory stride of one (band, slice) instance: the padded length
+// rounded up to an even number of float2, so that every instance buffer
+// starts on a 16-byte boundary (TMA bulk copies need it; with kSH = 5 and
+// M = 32 the padded length, 33, is odd)
+constexpr int inst_stride(int M) { return (padded<kSH>(M) + 1) & ~1; }
+constexpr int data_need(int M) { return M > kBandCap ? 0 : (kBandCap / M) * inst_stride(M); }
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+constexpr int kBandData =                                 // float2 per CTA
+    cmax(cmax(cmax(data_need(32), data_need(64)), cmax(data_need(128), data_need(256))),
+         cmax(cmax(data_need(512), data_need(1024)), data_need(2048)));
+static_assert(kBandData >= padded<kSH>(kBandCap), "instance buffers overlap");
 // Build-time tuning switches (defaults are the measured best):
 //   FCQT_TW3_SMEM   stage-3 twiddles as shared rows (1) or from the global
 //                   W_2048 table (0: less shared memory per CTA, faster);
@@ -346,16 +356,18 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     constexpr int IPC = kBandThreads / T;
     const Inst in = locate<M, EXT>(bp, c);
     const int t = in.t;
-    float2* buf = smem + in.il * padded<kSH>(M);
+    float2* buf = smem + in.il * inst_stride(M);
     const float2* Xs = X + (long)in.slice * kPlaneStride;
     const int off = in.d.x;
     constexpr bool side = KIND == kSide;   // every instance of the class is of one kind
     // octave classes whose first-stage inputs r = 6..9 are outside every
     // band's window support (checked at upload) skip them: no gather, no
     // gain, a DFT that knows they are zero
-    constexpr unsigned kZero = KIND == kOctavePruned ? 0x3C0u : 0u;
-    static_assert(KIND != kOctavePruned || (R1 == 16 && kP / R1 == 1),
-                  "pruning assumes one radix-16 butterfly per thread in stage 1");
+    // (taps [6M/16, 10M/16): first-stage inputs 6..9 of a radix-16 butterfly,
+    // 12..19 of a radix-32 one)
+    constexpr unsigned kZero = KIND != kOctavePruned ? 0u : R1 == 16 ? 0x3C0u : 0xFF000u;
+    static_assert(KIND != kOctavePruned || ((R1 == 16 || R1 == 32) && kP / R1 == 1),
+                  "pruning assumes one radix-16 or radix-32 butterfly per thread in stage 1");
 
     // stage the band's contiguous spectrum segment [lo, lo + n), n <= M,
     // into shared memory with one TMA bulk load issued by the instance's
@@ -525,7 +537,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     constexpr int IPC = kBandThreads / T;
     const Inst in = locate<M, EXT>(bp, c);
     const int t = in.t;
-    float2* buf = smem + in.il * padded<kSH>(M);
+    float2* buf = smem + in.il * inst_stride(M);
     const int off = in.d.x;
     const CoefAddr ca = coef_addr<M, SLICED>(bp, in.slice, in.d);
 
@@ -611,8 +623,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     // M = 2048 the radix-8 outputs 3 and 4 -- no gain, no index, no store
     constexpr int RL = TwLayout<M>::R3 > 1 ? TwLayout<M>::R3
                        : TwLayout<M>::R2 > 1 ? TwLayout<M>::R2 : TwLayout<M>::R1;
-    constexpr unsigned kDeadOut = (KIND == kOctavePruned && M == 2048) ? 0x18u : 0u;
-    static_assert(kDeadOut == 0 || RL == 8, "dead outputs assume a radix-8 last stage");
+    constexpr unsigned kDeadOut = (KIND == kOctavePruned && M == 2048 && RL == 8) ? 0x18u : 0u;
 #if FCQT_PREFETCH_GAINS
     // the gains of this thread's final-stage outputs, loaded before the
     // stages so the scatter does not wait on them

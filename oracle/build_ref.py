@@ -11,8 +11,10 @@ product's own built libraries).  No reference source file is copied:
 
 * ``flash_cqt/*.py`` (the pure-torch ``OctCQT`` / ``FusedOctCQT`` /
   ``TrainableCQT`` package, ``oct_cqt.py:18-117``, ``trainable.py:28-191``)
-  is byte-compiled to ``oracle/_ref/flash_cqt/*.pyc``, a sourceless package
-  the interpreter imports as it is;
+  is byte-compiled, and the code objects are marshalled into one bundle,
+  ``oracle/_ref/flash_cqt.bundle`` (a dict module name -> code, what a
+  ``.pyc`` holds after its header; one file because the GPU box snapshot does
+  not carry ``.pyc`` files), which ``oracle/ref_loader.py`` imports unchanged;
 * ``flash_cqt/csrc/{packedfft,radix,persist2}.cu`` (the factored path's CUDA
   extensions, ``fused.py:63-132``) are compiled by
   ``torch.utils.cpp_extension`` for sm_100a into
@@ -25,7 +27,7 @@ used.
 import argparse
 import os
 import pathlib
-import py_compile
+import marshal
 import shutil
 import sys
 
@@ -40,27 +42,36 @@ EXTENSIONS = {"packedfft": "flash_cqt_packedfft", "radix": "flash_cqt_radix",
 ARCH = ["-gencode=arch=compute_100a,code=sm_100a"]
 
 
+BUNDLE = OUT / "flash_cqt.bundle"
+
+
 def build_python(ref):
     src = pathlib.Path(ref) / "flash_cqt"
-    dst = OUT / "flash_cqt"
-    dst.mkdir(parents=True, exist_ok=True)
+    OUT.mkdir(parents=True, exist_ok=True)
+    codes = {}
     for m in PY_MODULES:
-        py_compile.compile(str(src / f"{m}.py"), cfile=str(dst / f"{m}.pyc"),
-                           dfile=f"flash_cqt/{m}.py", doraise=True)
-    return dst
+        text = (src / f"{m}.py").read_text()
+        name = "flash_cqt" if m == "__init__" else f"flash_cqt.{m}"
+        codes[name] = marshal.dumps(compile(text, f"flash_cqt/{m}.py", "exec", dont_inherit=True))
+    BUNDLE.write_bytes(marshal.dumps({"python": sys.version_info[:2], "modules": codes}))
+    return BUNDLE
 
 
-def build_extensions(ref, verbose=False):
+def build_extensions(ref, verbose=False, force=False):
+    """compile the extensions that are missing (all with force); about ten
+    minutes for the three from scratch"""
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
     from torch.utils import cpp_extension as ce
     built = {}
     for stem, name in EXTENSIONS.items():
         bdir = OUT / "ext" / name
-        bdir.mkdir(parents=True, exist_ok=True)
-        src = pathlib.Path(ref) / "flash_cqt" / "csrc" / f"{stem}.cu"
-        ce.load(name=name, sources=[str(src)], build_directory=str(bdir),
-                extra_cuda_cflags=ARCH + ["-O3"], verbose=verbose)
-        built[name] = bdir / f"{name}.so"
+        so = bdir / f"{name}.so"
+        if force or not so.exists():
+            bdir.mkdir(parents=True, exist_ok=True)
+            src = pathlib.Path(ref) / "flash_cqt" / "csrc" / f"{stem}.cu"
+            ce.load(name=name, sources=[str(src)], build_directory=str(bdir),
+                    extra_cuda_cflags=ARCH + ["-O3"], verbose=verbose)
+        built[name] = so
     return built
 
 
@@ -69,6 +80,7 @@ def main(argv=None):
     ap.add_argument("--ref", default=DEFAULT_REF)
     ap.add_argument("--no-cuda", action="store_true", help="byte-compile the package only")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--force", action="store_true", help="rebuild the CUDA extensions")
     a = ap.parse_args(argv)
     ref = pathlib.Path(a.ref)
     if not (ref / "flash_cqt" / "oct_cqt.py").exists():
@@ -76,7 +88,7 @@ def main(argv=None):
         return 0
     print(build_python(ref))
     if not a.no_cuda:
-        for name, so in build_extensions(ref, a.verbose).items():
+        for name, so in build_extensions(ref, a.verbose, a.force).items():
             print(name, so, so.exists())
     return 0
 
