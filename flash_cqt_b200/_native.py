@@ -95,6 +95,10 @@ def lib():
             L.cqt_synthesis_sqerr.restype = ci
             L.cqt_adj_synthesis_sqerr.argtypes = [vp, vp, vp, fl, vp, vp, vp, ci, ci, vp, sz, vp]
             L.cqt_adj_synthesis_sqerr.restype = ci
+            L.cqt_workspace_waits.argtypes = [vp, sz, ctypes.POINTER(ctypes.c_uint), ci]
+            L.cqt_workspace_waits.restype = ci
+            L.cqt_debug_expire_waits.argtypes = [ci]
+            L.cqt_debug_expire_waits.restype = ci
             L.cqt_launch_stage.argtypes = [vp, ci, vp, vp, vp, vp, ci, ci, vp, sz, vp]
             L.cqt_launch_stage.restype = ci
             L.cqt_analysis_noalloc.argtypes = [vp, vp, vp, vp, ci, ci, vp]
@@ -122,8 +126,27 @@ def exported_symbols():
             "cqt_adj_synthesis_sqerr", "cqt_launch_stage",
             "cqt_analysis_noalloc", "cqt_sliced_count", "cqt_sliced_analysis",
             "cqt_sliced_synthesis", "cqt_sliced_adj_analysis",
-            "cqt_sliced_adj_synthesis", "cqt_wait_timeouts", "cqt_last_error",
-            "cqt_version"]
+            "cqt_sliced_adj_synthesis", "cqt_wait_timeouts", "cqt_workspace_waits",
+            "cqt_debug_expire_waits", "cqt_last_error", "cqt_version"]
+
+
+WS_HEADER = 256   # bytes at the front of a workspace: the wait-status word
+
+
+def workspace_waits(ws, clear=True):
+    """expired bounded waits recorded in the workspace tensor `ws` by the calls
+    that used it since its header was last cleared (synchronous)"""
+    n = ctypes.c_uint(0)
+    _check(lib().cqt_workspace_waits(ws.data_ptr(), ws.numel() * ws.element_size(),
+                                     ctypes.byref(n), 1 if clear else 0),
+           "cqt_workspace_waits")
+    return int(n.value)
+
+
+def check_waits_enabled():
+    """FLASH_CQT_B200_CHECK_WAITS=1: every engine call reads its workspace's
+    wait status afterwards (synchronising) and raises if a wait ran out"""
+    return os.environ.get("FLASH_CQT_B200_CHECK_WAITS", "0") not in ("", "0")
 
 
 def wait_timeouts():

@@ -203,6 +203,41 @@ __device__ __forceinline__ void stage_compute_pow(float2 (&v)[P], int t, const T
     });
 }
 
+// stage_compute_pow with the base twiddles W^k, W^2k, W^4k of each butterfly
+// already loaded (wb[b][0..2]), so their loads can be issued early
+template <int M, int T, int R, int NS, int S, int P>
+__device__ __forceinline__ void stage_compute_pow_pre(float2 (&v)[P], const float2 (&wb)[P / R][3]) {
+    static_assert(R == 2 || R == 4 || R == 8, "power twiddles for radix 2, 4, 8");
+    static_for<0, P / R>([&](auto Bb) {
+        constexpr int b = decltype(Bb)::value;
+        float2 w[R];
+        w[1] = wb[b][0];
+        if constexpr (R >= 4) {
+            w[2] = wb[b][1];
+            w[3] = cmul(w[1], w[2]);
+        }
+        if constexpr (R == 8) {
+            w[4] = wb[b][2];
+            w[5] = cmul(w[1], w[4]);
+            w[6] = cmul(w[2], w[4]);
+            w[7] = cmul(w[3], w[4]);
+        }
+#pragma unroll
+        for (int r = 1; r < R; ++r) {
+            float2 x = w[r];
+            if constexpr (S > 0) x.y = -x.y;
+            v[b * R + r] = cmul(v[b * R + r], x);
+        }
+        dft<R, S, b * R, 1>(v);
+    });
+}
+
+// the last stage's twiddle loads are issued before the exchange that
+// precedes it, so the barrier hides their latency (1), or after it (0)
+#ifndef FCQT_TW3_EARLY
+#define FCQT_TW3_EARLY 0
+#endif
+
 // stages 2 and 3 after stage 1's DFT; the last stage's outputs (index
 // n = j + r M / R_last, j = t + T b) go to `emit`
 struct Tw2048 {
@@ -227,6 +262,22 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const fl
         stage_compute_rows<M, T, R2, R1, S>(v, t, tws);
         if constexpr (R3 == 1) {
             emit(v, integral_constant<int, R2>{}, integral_constant<int, R1>{});
+        } else if constexpr (FCQT_TW3_EARLY && FCQT_TW3_POW && !FCQT_TW3_SMEM) {
+            constexpr int NS = R1 * R2, scale = 2048 / (NS * R3);
+            float2 wb[kP / R3][3];
+#pragma unroll
+            for (int b = 0; b < kP / R3; ++b) {
+                const int e = ((t + T * b) % NS) * scale;
+                wb[b][0] = __ldg(bp_tw + (e & 2047));
+                wb[b][1] = R3 >= 4 ? __ldg(bp_tw + ((2 * e) & 2047)) : wb[b][0];
+                wb[b][2] = R3 == 8 ? __ldg(bp_tw + ((4 * e) & 2047)) : wb[b][0];
+            }
+            stage_store<M, T, R2, R1, kSH>(v, buf, t);
+            __syncthreads();
+            stage_load<M, T, R3, kSH>(v, buf, t);
+            __syncthreads();
+            stage_compute_pow_pre<M, T, R3, NS, S>(v, wb);
+            emit(v, integral_constant<int, R3>{}, integral_constant<int, NS>{});
         } else {
             stage_store<M, T, R2, R1, kSH>(v, buf, t);
             __syncthreads();
@@ -275,11 +326,15 @@ __device__ __forceinline__ void bulk_commit_wait_read() {
     asm volatile("cp.async.bulk.commit_group;\ncp.async.bulk.wait_group.read 0;\n" ::: "memory");
 }
 
-// TMA bulk loads completing on an mbarrier.  Every wait is bounded: after
-// kMaxWaitSpins polls (each try_wait also suspends for a while) the wait
-// counts itself in g_wait_timeouts and returns, so a lost completion cannot
-// hang the GPU.
+// TMA bulk loads completing on an mbarrier.  Every wait is bounded in time:
+// a wait whose first poll fails reads the global nanosecond timer and gives
+// up after kWaitLimitNs (a TMA bulk copy normally lands within microseconds),
+// with kMaxWaitSpins polls as a second bound.  A wait that gives up counts
+// itself in g_wait_timeouts (process-wide, cqt_wait_timeouts) and in the
+// call's wait-status word (the workspace header, cqt_workspace_waits) and
+// returns, so a lost completion can neither hang the GPU nor go unnoticed.
 constexpr int kMaxWaitSpins = 1 << 22;
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;   // 1 s
 __device__ unsigned int g_wait_timeouts;
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
@@ -300,18 +355,34 @@ __device__ __forceinline__ void bulk_load(void* sdst, const void* gsrc, unsigned
                  " [%0], [%1], %2, [%3];\n"
                  ::"r"(smem_u32(sdst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
 }
-__device__ __forceinline__ bool mbar_wait(unsigned long long* mbar, unsigned phase) {
-    const unsigned a = smem_u32(mbar);
+__device__ __forceinline__ bool mbar_try(unsigned a, unsigned phase) {
+    unsigned done;
+    asm volatile("{\n.reg .pred p;\n"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 "selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(done) : "r"(a), "r"(phase) : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __noinline__ bool mbar_wait_slow(unsigned a, unsigned phase, unsigned* status) {
+    const unsigned long long t0 = global_ns();
     for (int i = 0; i < kMaxWaitSpins; ++i) {
-        unsigned done;
-        asm volatile("{\n.reg .pred p;\n"
-                     "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-                     "selp.u32 %0, 1, 0, p;\n}\n"
-                     : "=r"(done) : "r"(a), "r"(phase) : "memory");
-        if (done) return true;
+        if (mbar_try(a, phase)) return true;
+        if (global_ns() - t0 > kWaitLimitNs) break;
     }
     atomicAdd(&g_wait_timeouts, 1u);
+    if (status) atomicAdd(status, 1u);
     return false;
+}
+__device__ __forceinline__ bool mbar_wait(unsigned long long* mbar, unsigned phase,
+                                          unsigned* status) {
+    const unsigned a = smem_u32(mbar);
+    if (mbar_try(a, phase)) return true;
+    return mbar_wait_slow(a, phase, status);
 }
 
 // where an instance's M coefficients live: element n at
@@ -391,7 +462,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     pdl_wait();   // the previous kernel of the stream has completed
     if (t == 0) {
         const int a = lo - sh, bytes = n > 0 ? (((lo + n + 1) & ~1) - a) * 8 : 0;
-        mbar_arrive_expect(mbar, (unsigned)bytes);
+        mbar_arrive_expect(mbar, (unsigned)bytes + (bp.expire_waits ? 16u : 0u));
         if (bytes) bulk_load(buf, Xs + a, (unsigned)bytes, mbar);
     }
     fill_twiddles<M>(tws, bp.tw2048);
@@ -425,7 +496,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     // each thread's completed wait makes the bulk-loaded segment visible to
     // it; the twiddle rows filled above are first read in stage 2, behind the
     // stage-1 exchange barrier, so no CTA barrier is needed here
-    mbar_wait(mbar, 0);
+    mbar_wait(mbar, 0, bp.status);
     float2 v[kP];
     const float2* seg = buf + sh;
     if constexpr (!side) {
@@ -556,7 +627,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     __syncthreads();
     pdl_wait();   // the previous kernel of the stream has completed
     if (t == 0) {
-        mbar_arrive_expect(mbar, bulk ? M * 8 : 0);
+        mbar_arrive_expect(mbar, (bulk ? M * 8 : 0) + (bp.expire_waits ? 16u : 0u));
         if (bulk) {
             // smem [0, M - r) <- src [r, M), smem [M - r, M) <- src [0, r)
             const int r = SLICED ? (ca.roll & (M - 1)) : 0;
@@ -588,7 +659,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     }
     fill_twiddles<M>(tws, bp.tw2048);
     cp_async_wait_all();
-    mbar_wait(mbar, 0);
+    mbar_wait(mbar, 0, bp.status);
     __syncthreads();
     float2 v[kP];
     if (interleaved) {

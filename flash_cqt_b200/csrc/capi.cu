@@ -68,18 +68,32 @@ int check_device(const cqt_tables* t) {
     return CQT_OK;
 }
 
-// workspace: the spectrum rows / colour planes, then the per-CTA partial sums
-// of the squared-error entry points (16-byte aligned: the planes are)
+// workspace: a 256-byte header (the wait-status word, cqt_workspace_waits),
+// the spectrum rows / colour planes, then the per-CTA partial sums of the
+// squared-error entry points (16-byte aligned: the planes are)
+constexpr size_t kWsHeader = 256;
 size_t ws_planes(const cqt_tables* t, int batch) {
     return (size_t)batch * (size_t)t->max_planes * kPlaneStride * sizeof(float2);
 }
 size_t ws_need(const cqt_tables* t, int batch) {
     const size_t partials = ((size_t)spectrum_ctas(batch) * sizeof(float) + 15) & ~(size_t)15;
-    return ws_planes(t, batch) + partials;
+    return kWsHeader + ws_planes(t, batch) + partials;
 }
 float* ws_partials(const cqt_tables* t, int batch, void* ws) {
-    return reinterpret_cast<float*>(static_cast<char*>(ws) + ws_planes(t, batch));
+    return reinterpret_cast<float*>(static_cast<char*>(ws) + kWsHeader + ws_planes(t, batch));
 }
+
+// what one call's kernels use: the spectrum rows / planes and the status word
+struct Scratch {
+    float2* rows;
+    unsigned* status;
+};
+Scratch scratch_of(void* ws) {
+    return Scratch{reinterpret_cast<float2*>(static_cast<char*>(ws) + kWsHeader),
+                   static_cast<unsigned*>(ws)};
+}
+
+std::atomic<int> g_expire_waits{0};   // cqt_debug_expire_waits
 
 // the band kernels split an instance index into (band, slice) with a float
 // reciprocal, exact while slices x (bands of one block length) < 2^24
@@ -116,7 +130,7 @@ int coef_ptr(const float* re, const float* im, int layout, CoefPtr* out) {
 }
 
 BandParams band_params(const cqt_tables* t, int batch) {
-    BandParams bp;
+    BandParams bp{};
     bp.sc = make_sched(t->ncls, t->cls_M, t->cls_nb, t->cls_first, t->cls_kind, batch);
     bp.tw2048 = t->tw2048;
     bp.ncoef = t->ncoef;
@@ -125,6 +139,8 @@ BandParams band_params(const cqt_tables* t, int batch) {
     std::memcpy(bp.desc_inline, t->desc_host,
                 sizeof(int4) * (t->nbands < kInlineBands ? t->nbands : kInlineBands));
     bp.sl = SliceLayout{};
+    bp.status = nullptr;
+    bp.expire_waits = g_expire_waits.load(std::memory_order_relaxed);
     return bp;
 }
 
@@ -154,9 +170,10 @@ int check_signal(const float* p, bool input) {
 
 // one analysis-engine pass: real signal -> spectrum -> bands
 int run_fwd(const cqt_tables* t, int which, const SigMap& sig, CoefPtr out,
-            const BandParams& bp, int batch, void* ws, cudaStream_t s) {
+            BandParams bp, int batch, Scratch sc, cudaStream_t s) {
     if (batch == 0) return CQT_OK;
-    float2* X = static_cast<float2*>(ws);
+    float2* X = sc.rows;
+    bp.status = sc.status;
     cudaError_t e = launch_spectrum_fwd(sig, X, t->spec, batch, s);
     if (e != cudaSuccess) return cuda_fail(e, "spectrum_fwd launch");
     e = launch_bands_fwd(X, t->fwd[which], bp, out, s);
@@ -165,15 +182,16 @@ int run_fwd(const cqt_tables* t, int which, const SigMap& sig, CoefPtr out,
 }
 
 int run_fwd_engine(const cqt_tables* t, int which, const float* sig, CoefPtr out,
-                   int batch, void* ws, cudaStream_t s) {
-    return run_fwd(t, which, contiguous_in(sig), out, band_params(t, batch), batch, ws, s);
+                   int batch, Scratch sc, cudaStream_t s) {
+    return run_fwd(t, which, contiguous_in(sig), out, band_params(t, batch), batch, sc, s);
 }
 
 // one synthesis-engine pass: bands -> colour planes -> real signal
 int run_inv(const cqt_tables* t, int which, CoefPtr in, const SigMap& sig,
-            const BandParams& bp, int batch, void* ws, cudaStream_t s) {
+            BandParams bp, int batch, Scratch sc, cudaStream_t s) {
     if (batch == 0) return CQT_OK;
-    float2* E = static_cast<float2*>(ws);
+    float2* E = sc.rows;
+    bp.status = sc.status;
     cudaError_t e = launch_bands_inv(in, t->inv[which], which, bp, E, s);
     if (e != cudaSuccess) return cuda_fail(e, "bands_inv launch");
     e = launch_spectrum_inv(E, t->inv[which], sig, t->spec, batch, s);
@@ -183,7 +201,8 @@ int run_inv(const cqt_tables* t, int which, CoefPtr in, const SigMap& sig,
 
 int run_inv_engine(const cqt_tables* t, int which, CoefPtr in, float* sig, int batch,
                    void* ws, cudaStream_t s) {
-    return run_inv(t, which, in, contiguous_out(sig), band_params(t, batch), batch, ws, s);
+    return run_inv(t, which, in, contiguous_out(sig), band_params(t, batch), batch,
+                   scratch_of(ws), s);
 }
 
 int sliced_count(long long length) {
@@ -234,6 +253,24 @@ int cqt_wait_timeouts(unsigned int* count) {
     *count = 0;
     const cudaError_t e = read_wait_timeouts(count);
     return e == cudaSuccess ? CQT_OK : cuda_fail(e, "reading the wait-timeout counter");
+}
+
+int cqt_workspace_waits(void* workspace, size_t workspace_bytes, unsigned int* expired,
+                        int clear) {
+    if (!workspace || !expired || workspace_bytes < kWsHeader)
+        return fail(CQT_ERR_ARG, "null workspace or count, or workspace without its header");
+    cudaError_t e = cudaMemcpy(expired, workspace, sizeof(unsigned), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the workspace wait status");
+    if (clear) {
+        e = cudaMemset(workspace, 0, sizeof(unsigned));
+        if (e != cudaSuccess) return cuda_fail(e, "clearing the workspace wait status");
+    }
+    return CQT_OK;
+}
+
+int cqt_debug_expire_waits(int on) {
+    g_expire_waits.store(on ? 1 : 0, std::memory_order_relaxed);
+    return CQT_OK;
 }
 
 int32_t cqt_ncoef(const cqt_tables* t) { return t ? t->ncoef : -1; }
@@ -544,7 +581,7 @@ int cqt_analysis(const cqt_tables* t, const float* x, float* c_re, float* c_im, 
     if (batch && (rc = check_signal(x, true))) return rc;
     CoefPtr out;
     if (batch && (rc = coef_ptr(c_re, c_im, layout, &out))) return rc;
-    return run_fwd_engine(t, 0, x, out, batch, ws, static_cast<cudaStream_t>(stream));
+    return run_fwd_engine(t, 0, x, out, batch, scratch_of(ws), static_cast<cudaStream_t>(stream));
 }
 
 int cqt_adj_synthesis(const cqt_tables* t, const float* gy, float* g_re, float* g_im,
@@ -554,7 +591,7 @@ int cqt_adj_synthesis(const cqt_tables* t, const float* gy, float* g_re, float* 
     if (batch && (rc = check_signal(gy, true))) return rc;
     CoefPtr out;
     if (batch && (rc = coef_ptr(g_re, g_im, layout, &out))) return rc;
-    return run_fwd_engine(t, 1, gy, out, batch, ws, static_cast<cudaStream_t>(stream));
+    return run_fwd_engine(t, 1, gy, out, batch, scratch_of(ws), static_cast<cudaStream_t>(stream));
 }
 
 int cqt_synthesis(const cqt_tables* t, const float* c_re, const float* c_im, int layout,
@@ -593,7 +630,8 @@ int cqt_synthesis_sqerr(const cqt_tables* t, const float* c_re, const float* c_i
         SigMap out = contiguous_out(y);
         out.target = target;
         out.partial = ws_partials(t, batch, ws);
-        if ((rc = run_inv(t, 0, in, out, band_params(t, batch), batch, ws, s))) return rc;
+        if ((rc = run_inv(t, 0, in, out, band_params(t, batch), batch, scratch_of(ws), s)))
+            return rc;
     }
     // an empty batch still defines the loss: the sum of nothing
     cudaError_t e = launch_sqerr_finish(batch > 0 ? ws_partials(t, batch, ws) : nullptr,
@@ -616,7 +654,7 @@ int cqt_adj_synthesis_sqerr(const cqt_tables* t, const float* y, const float* ta
     in.target = target;
     in.scale_dev = scale_dev;
     in.scale = scale;
-    return run_fwd(t, 1, in, out, band_params(t, batch), batch, ws,
+    return run_fwd(t, 1, in, out, band_params(t, batch), batch, scratch_of(ws),
                    static_cast<cudaStream_t>(stream));
 }
 
@@ -629,26 +667,25 @@ int cqt_launch_stage(const cqt_tables* t, int stage, const float* sig_in, float*
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
     CoefPtr cp;
+    const Scratch sc = scratch_of(ws);
+    BandParams bp = band_params(t, batch);
+    bp.status = sc.status;
     switch (stage) {
     case 0:
         if ((rc = check_signal(sig_in, true))) return rc;
-        e = launch_spectrum_fwd(contiguous_in(sig_in), static_cast<float2*>(ws), t->spec, batch,
-                                s);
+        e = launch_spectrum_fwd(contiguous_in(sig_in), sc.rows, t->spec, batch, s);
         break;
     case 1:
         if ((rc = coef_ptr(c_re, c_im, layout, &cp))) return rc;
-        e = launch_bands_fwd(static_cast<const float2*>(ws), t->fwd[0], band_params(t, batch),
-                             cp, s);
+        e = launch_bands_fwd(sc.rows, t->fwd[0], bp, cp, s);
         break;
     case 2:
         if ((rc = coef_ptr(c_re, c_im, layout, &cp))) return rc;
-        e = launch_bands_inv(cp, t->inv[0], 0, band_params(t, batch), static_cast<float2*>(ws),
-                             s);
+        e = launch_bands_inv(cp, t->inv[0], 0, bp, sc.rows, s);
         break;
     case 3:
         if ((rc = check_signal(sig_out, false))) return rc;
-        e = launch_spectrum_inv(static_cast<const float2*>(ws), t->inv[0],
-                                contiguous_out(sig_out), t->spec, batch, s);
+        e = launch_spectrum_inv(sc.rows, t->inv[0], contiguous_out(sig_out), t->spec, batch, s);
         break;
     default:
         return fail(CQT_ERR_ARG, "unknown stage");
@@ -723,7 +760,8 @@ extern "C" int cqt_analysis_noalloc(const cqt_tables* t, const float* x, float* 
     if ((rc = check_signal(x, true))) return rc;
     CoefPtr out;
     if ((rc = coef_ptr(c_re, c_im, layout, &out))) return rc;
-    return run_fwd_engine(t, 0, x, out, batch, scratch, static_cast<cudaStream_t>(stream));
+    return run_fwd_engine(t, 0, x, out, batch, Scratch{static_cast<float2*>(scratch), nullptr},
+                          static_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------------------------------
@@ -744,7 +782,7 @@ int cqt_sliced_analysis(const cqt_tables* t, const cqt_signal* x, const cqt_slic
     const CoefPtr out{coef, nullptr, 1};
     return run_fwd(t, 0, sig_map(sl, x, true, sl->window), out,
                    band_params_sliced(t, sl->rows, sl->slice0, sl->slices),
-                   sl->rows * sl->slices, ws, static_cast<cudaStream_t>(stream));
+                   sl->rows * sl->slices, scratch_of(ws), static_cast<cudaStream_t>(stream));
 }
 
 int cqt_sliced_adj_synthesis(const cqt_tables* t, const cqt_signal* gy, const cqt_slices* sl,
@@ -757,7 +795,7 @@ int cqt_sliced_adj_synthesis(const cqt_tables* t, const cqt_signal* gy, const cq
     const CoefPtr out{gcoef, nullptr, 1};
     return run_fwd(t, 1, sig_map(sl, gy, true, nullptr), out,
                    band_params_sliced(t, sl->rows, sl->slice0, sl->slices),
-                   sl->rows * sl->slices, ws, static_cast<cudaStream_t>(stream));
+                   sl->rows * sl->slices, scratch_of(ws), static_cast<cudaStream_t>(stream));
 }
 
 static int sliced_inv(const cqt_tables* t, int which, const float* coef, const cqt_slices* sl,
@@ -778,7 +816,7 @@ static int sliced_inv(const cqt_tables* t, int which, const float* coef, const c
     const CoefPtr in{const_cast<float*>(coef), nullptr, 1};
     return run_inv(t, which, in, sig_map(sl, y, false, window),
                    band_params_sliced(t, sl->rows, sl->slice0, sl->slices),
-                   sl->rows * sl->slices, ws, s);
+                   sl->rows * sl->slices, scratch_of(ws), s);
 }
 
 int cqt_sliced_synthesis(const cqt_tables* t, const float* coef, const cqt_slices* sl,

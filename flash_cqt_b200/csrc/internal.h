@@ -108,6 +108,12 @@ struct BandParams {
     const int4* desc;
     int ext;               // more than kInlineBands bands: read desc
     SliceLayout sl;
+    // wait-status word in the caller's workspace header (null: none); a
+    // bounded wait that gives up adds 1 to it
+    unsigned* status;
+    // test hook (cqt_debug_expire_waits): the staging barrier expects 16
+    // bytes that no copy delivers, so every bounded wait runs out
+    int expire_waits;
 };
 
 struct CoefPtr {           // coefficient heap addressing

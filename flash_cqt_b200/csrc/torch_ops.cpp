@@ -25,6 +25,7 @@ namespace {
 constexpr int64_t kN = 65536;
 constexpr int kLayoutPlanar = 0;    // CQT_LAYOUT_PLANAR
 constexpr int kLayoutComplex = 1;   // CQT_LAYOUT_COMPLEX
+constexpr int64_t kWsHeader = 256;  // workspace header (the wait-status word)
 
 // cqt_analysis / cqt_adj_synthesis: signal first
 using FnSignalFirst = int (*)(const void*, const float*, float*, float*, int, int, void*,
@@ -88,8 +89,9 @@ struct Ops : torch::CustomClassHolder {
         }
         if (!ws.defined() || (size_t)ws.numel() < n) {
             if (ws.defined()) retired.push_back(ws);
-            ws = at::empty({(int64_t)std::max<size_t>(n, 16)},
+            ws = at::empty({(int64_t)std::max<size_t>(n, kWsHeader)},
                            at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device));
+            ws.narrow(0, 0, kWsHeader).zero_();   // the wait-status header
         }
         *bytes = (size_t)ws.numel();
         return ws.data_ptr();

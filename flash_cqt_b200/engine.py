@@ -77,8 +77,22 @@ class Engine:
         if self._ws is None or self._ws.numel() < need:
             if self._ws is not None:
                 self._ws_retired.append(self._ws)
-            self._ws = torch.empty(max(need, 16), dtype=torch.uint8, device=self.dev)
+            self._ws = torch.empty(max(need, _native.WS_HEADER), dtype=torch.uint8,
+                                   device=self.dev)
+            self._ws[:_native.WS_HEADER].zero_()   # the wait-status header
         return self._ws
+
+    def wait_status(self, clear=True):
+        """bounded kernel waits that gave up in the calls on this engine's
+        workspace since the last check (synchronous; 0 when healthy)"""
+        ws = self.workspace(0)
+        return _native.workspace_waits(ws, clear)
+
+    def _check_waits(self, what):
+        n = self.wait_status()
+        if n:
+            raise RuntimeError(f"{what}: {n} bounded wait(s) in the kernels gave up; "
+                               "the results of this call are not trustworthy")
 
     def _stream(self):
         return ctypes_stream(torch.cuda.current_stream(self.dev))
@@ -128,6 +142,8 @@ class Engine:
         ws = self.workspace(batch)
         self.tables.call(name, a, b, c, layout, batch, ws.data_ptr(), ws.numel(),
                          _raw_stream_of(self.dev.index))
+        if _native.check_waits_enabled():
+            self._check_waits(name)
 
     # ----------------------------------------------------------------- complex
     def analysis(self, x, out=None):

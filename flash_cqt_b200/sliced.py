@@ -349,8 +349,8 @@ class SliceStream:
         self.ybuf = z(rows, 2 * hop)
         self.tail = z(rows, hop)
         self.out = z(rows, hop)
-        self.ws = torch.empty(max(se.eng.tables.workspace_bytes(rows), 16), dtype=torch.uint8,
-                              device=dev)
+        self.ws = torch.zeros(max(se.eng.tables.workspace_bytes(rows), 256), dtype=torch.uint8,
+                              device=dev)   # zeroed: the header holds the wait status
         self.kf = self.kb = 0
 
         def fwd_body(s0):

@@ -32,7 +32,9 @@
  *     complex64 [batch][ncoef] array and c_im is ignored (may be NULL).
  *   - workspace: caller-owned device scratch of at least
  *     cqt_workspace_bytes(t, batch) bytes, 16-byte aligned; it may be reused
- *     between calls that are ordered on one stream.
+ *     between calls that are ordered on one stream.  Its first 256 bytes are a
+ *     header holding the wait-status word (cqt_workspace_waits): zero them
+ *     once when the workspace is allocated.
  *   - One call takes fewer than 2^24 / (largest number of bands sharing one
  *     block length) slices (batch, or rows x slices); 349,525 for the default
  *     bank, far more than fit in device memory.  Larger calls return
@@ -246,6 +248,24 @@ int cqt_sliced_adj_synthesis(const cqt_tables* t, const cqt_signal* gy, const cq
  * count means results computed since then are not trustworthy.  Synchronous
  * (reads device memory). */
 int cqt_wait_timeouts(unsigned int* count);
+
+/* Diagnostic (no reference counterpart): the bounded waits that gave up in
+ * the calls that used `workspace` since its header was last cleared -- the
+ * per-workspace, so per-call when checked after each call, form of
+ * cqt_wait_timeouts.  Every band kernel of a call adds its expired waits to
+ * the status word in the workspace header; a nonzero count means those
+ * calls' results are not trustworthy.  Synchronous (reads, and with
+ * clear != 0 zeroes, 4 bytes of device memory on the legacy default
+ * stream). */
+int cqt_workspace_waits(void* workspace, size_t workspace_bytes, unsigned int* expired,
+                        int clear);
+
+/* Test hook for the failure detection above (no reference counterpart):
+ * while on != 0, every launch made by this process arms the band kernels'
+ * staging barriers for 16 bytes more than their copies deliver, so every
+ * bounded wait runs out (after 1 s) and is recorded; results are garbage.
+ * Nothing faults or hangs; the context stays usable. */
+int cqt_debug_expire_waits(int on);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* cqt_last_error(void);

@@ -81,6 +81,7 @@ int main(int argc, char** argv) {
         cudaMalloc((void**)&dc, nc * 8) || cudaMalloc(&ws, wsb))
         return 3;
     cudaMemcpy(dx, x, nx * 4, cudaMemcpyHostToDevice);
+    cudaMemset(ws, 0, 256);   /* the workspace header: the wait-status word */
     if (cqt_analysis(t, dx, dc, NULL, CQT_LAYOUT_COMPLEX, batch, ws, wsb, NULL))
         return fail("cqt_analysis");
     if (cqt_synthesis(t, dc, NULL, CQT_LAYOUT_COMPLEX, dy, batch, ws, wsb, NULL))
@@ -93,6 +94,8 @@ int main(int argc, char** argv) {
     }
     unsigned timeouts = 0;
     if (cqt_wait_timeouts(&timeouts) || timeouts) return fail("bounded waits");
+    if (cqt_workspace_waits(ws, wsb, &timeouts, 1) || timeouts)
+        return fail("bounded waits of the round trip");
     printf("snr_db %.3f\n", 10.0 * log10(num / den));
     cudaFree(dx); cudaFree(dy); cudaFree(dc); cudaFree(ws);
     cqt_tables_free(t);
