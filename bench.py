@@ -43,6 +43,10 @@ def parse():
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the batch sweep, train step, e2e and CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--halo", choices=["auto", "peer", "collective"], default="auto",
+                    help="transport of the config-5 overlap-add halo at N > 1: this build's "
+                         "peer-memory kernels, torch.distributed send / receive, or auto "
+                         "(peer memory under NCCL)")
     ap.add_argument("--reference-gpu-only", action="store_true",
                     help="run only the same-box GPU baseline of the reference's own "
                          "kernels and print it")
@@ -332,6 +336,9 @@ def main():
                                     device_id=torch.device("cuda", local))
         else:
             dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+        if rank == 0:
+            print(f"process group: backend {dist.get_backend()}, "
+                  f"{dist.get_world_size()} ranks", file=sys.stderr, flush=True)
     if args.impl == "reference":
         run_reference(args, rank)
         if world > 1:
@@ -355,7 +362,7 @@ def main():
     if args.sliced_only:
         pk = ROOT / "MEASURED_PEAKS.json"
         hbm = (json.loads(pk.read_text()).get("hbm_gbs") if pk.exists() else None) or 6650.0
-        r = sliced_stream(dev, world, rank, max(args.warmup, 3), args.steps, hbm)
+        r = sliced_stream(dev, world, rank, max(args.warmup, 3), args.steps, hbm, args.halo)
         if rank == 0:
             print(json.dumps({"sliced_stream": r}), flush=True)
         if world > 1:
@@ -481,6 +488,11 @@ def main():
                    "l2": "inputs larger than L2 (x %d MiB, coefficients %d MiB per GPU)"
                          % (B * N * 4 >> 20, B * eng.ncoef * 8 >> 20)},
         "round_trip_snr_db": rt_db,
+        "comm": ({"backend": dist.get_backend(), "nranks": dist.get_world_size(),
+                  "data_path_collectives": 0,
+                  "note": "one NCCL communicator of all ranks; used only for the barrier "
+                          "and the max-over-ranks timing reduction"}
+                 if world > 1 else {"backend": None, "nranks": 1}),
         "gpu_launches": 4 * K,
         "roofline": roofline,
         "pipeline_roofline": pipeline,
@@ -506,7 +518,7 @@ SLICED_LEN = 2646000
 SLICED_BYTES = 10584000 + 82 * 2127872 + 10584000
 
 
-def sliced_stream(dev, world, rank, W, K, hbm):
+def sliced_stream(dev, world, rank, W, K, hbm, halo="auto"):
     """SlicedCQT fwd + bwd (fused kernels) on the config-5 stream; at N > 1
     the slices are range-partitioned and only the overlap-add halo crosses
     NVLink.  Strong scaling: the whole stream is fixed, time is max over ranks."""
@@ -524,7 +536,7 @@ def sliced_stream(dev, world, rank, W, K, hbm):
     x = (torch.sin(phase).float().expand(SLICED_SIGNALS, SLICED_LEN)
          + 0.05 * torch.randn(SLICED_SIGNALS, SLICED_LEN, device=dev, generator=g))
     x = x.reshape(SLICED_SIGNALS, 1, SLICED_LEN).contiguous()
-    pc = PartitionedSlicedCQT(sl, rank, world)
+    pc = PartitionedSlicedCQT(sl, rank, world, halo=halo)
 
     def step():
         if world == 1:
@@ -552,17 +564,21 @@ def sliced_stream(dev, world, rank, W, K, hbm):
     e1.synchronize()
     ms = e0.elapsed_time(e1) / reps
     if world > 1:
+        pc.check_halo()   # raises if a bounded wait on a neighbour gave up
         tt_ = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(tt_, op=dist.ReduceOp.MAX)
         ms = float(tt_.item())
     gbs = SLICED_SIGNALS * SLICED_BYTES / (ms / 1e3) / 1e9
     return {"workload": "SlicedCQT fwd + bwd, 8 x 2,646,000-sample chirp + noise, 82 "
                         "slices per signal, fused sliced kernels, slices range-partitioned "
-                        "over ranks with an NVLink overlap-add halo",
+                        "over ranks with an NVLink overlap-add halo (strong scaling)",
             "ms_per_step": ms, "signals_per_s": SLICED_SIGNALS / (ms / 1e3),
             "slices_per_s": SLICED_SIGNALS * 82 / (ms / 1e3),
             "achieved_gbs": gbs, "frac_of_hbm": gbs / (hbm * world),
-            "snr_db": snr, "scaling": "strong", "n_gpus": world}
+            "snr_db": snr, "scaling": "strong", "n_gpus": world,
+            "halo": ("this build's peer-memory kernels (CUDA IPC, plain NVLink stores, "
+                     "flag + acknowledgement, bounded waits)" if world > 1 and pc._use_peer(y)
+                     else "torch.distributed send / receive" if world > 1 else None)}
 
 
 def extras(args, eng, t, dev, world, rank, barrier, W, K, hbm=6549.1):
@@ -571,7 +587,7 @@ def extras(args, eng, t, dev, world, rank, barrier, W, K, hbm=6549.1):
     import torch
     from flash_cqt_b200 import FusedOctCQT, Graphed, HostPipeline
     out = {}
-    out["sliced_stream"] = sliced_stream(dev, world, rank, W, K, hbm)
+    out["sliced_stream"] = sliced_stream(dev, world, rank, W, K, hbm, args.halo)
     B = args.batch
     # ---- e2e through the public host API: pinned host x -> HostPipeline
     # (H2D, graphed FusedOctCQT fwd -> bwd, D2H, overlapped chunk by chunk)

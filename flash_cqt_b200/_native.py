@@ -95,6 +95,16 @@ def lib():
             L.cqt_synthesis_sqerr.restype = ci
             L.cqt_adj_synthesis_sqerr.argtypes = [vp, vp, vp, fl, vp, vp, vp, ci, ci, vp, sz, vp]
             L.cqt_adj_synthesis_sqerr.restype = ci
+            i64_ = ctypes.c_int64
+            L.cqt_halo_create.argtypes = [ci, ci, i64_, ci, ctypes.POINTER(vp), vp]
+            L.cqt_halo_connect.argtypes = [vp, vp, vp]
+            L.cqt_halo_send.argtypes = [vp, vp, i64_, i64_, vp]
+            L.cqt_halo_recv_add.argtypes = [vp, vp, i64_, i64_, vp]
+            L.cqt_halo_waits.argtypes = [vp, ctypes.POINTER(ctypes.c_uint), ci]
+            L.cqt_halo_free.argtypes = [vp]
+            for nm in ("cqt_halo_create", "cqt_halo_connect", "cqt_halo_send",
+                       "cqt_halo_recv_add", "cqt_halo_waits", "cqt_halo_free"):
+                getattr(L, nm).restype = ci
             L.cqt_workspace_waits.argtypes = [vp, sz, ctypes.POINTER(ctypes.c_uint), ci]
             L.cqt_workspace_waits.restype = ci
             L.cqt_debug_expire_waits.argtypes = [ci]
@@ -126,7 +136,9 @@ def exported_symbols():
             "cqt_adj_synthesis_sqerr", "cqt_launch_stage",
             "cqt_analysis_noalloc", "cqt_sliced_count", "cqt_sliced_analysis",
             "cqt_sliced_synthesis", "cqt_sliced_adj_analysis",
-            "cqt_sliced_adj_synthesis", "cqt_wait_timeouts", "cqt_workspace_waits",
+            "cqt_sliced_adj_synthesis", "cqt_halo_create", "cqt_halo_connect",
+            "cqt_halo_send", "cqt_halo_recv_add", "cqt_halo_waits", "cqt_halo_free",
+            "cqt_wait_timeouts", "cqt_workspace_waits",
             "cqt_debug_expire_waits", "cqt_last_error", "cqt_version"]
 
 

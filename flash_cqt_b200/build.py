@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "_lib" / "libflashcqt_b200.so"
 INCLUDE = PKG.parent / "include"
-SOURCES = ["spectrum.cu", "bands.cu", "capi.cu"]
+SOURCES = ["spectrum.cu", "bands.cu", "halo.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-O3", "-I", str(INCLUDE)]

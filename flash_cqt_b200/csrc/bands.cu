@@ -203,41 +203,6 @@ __device__ __forceinline__ void stage_compute_pow(float2 (&v)[P], int t, const T
     });
 }
 
-// stage_compute_pow with the base twiddles W^k, W^2k, W^4k of each butterfly
-// already loaded (wb[b][0..2]), so their loads can be issued early
-template <int M, int T, int R, int NS, int S, int P>
-__device__ __forceinline__ void stage_compute_pow_pre(float2 (&v)[P], const float2 (&wb)[P / R][3]) {
-    static_assert(R == 2 || R == 4 || R == 8, "power twiddles for radix 2, 4, 8");
-    static_for<0, P / R>([&](auto Bb) {
-        constexpr int b = decltype(Bb)::value;
-        float2 w[R];
-        w[1] = wb[b][0];
-        if constexpr (R >= 4) {
-            w[2] = wb[b][1];
-            w[3] = cmul(w[1], w[2]);
-        }
-        if constexpr (R == 8) {
-            w[4] = wb[b][2];
-            w[5] = cmul(w[1], w[4]);
-            w[6] = cmul(w[2], w[4]);
-            w[7] = cmul(w[3], w[4]);
-        }
-#pragma unroll
-        for (int r = 1; r < R; ++r) {
-            float2 x = w[r];
-            if constexpr (S > 0) x.y = -x.y;
-            v[b * R + r] = cmul(v[b * R + r], x);
-        }
-        dft<R, S, b * R, 1>(v);
-    });
-}
-
-// the last stage's twiddle loads are issued before the exchange that
-// precedes it, so the barrier hides their latency (1), or after it (0)
-#ifndef FCQT_TW3_EARLY
-#define FCQT_TW3_EARLY 0
-#endif
-
 // stages 2 and 3 after stage 1's DFT; the last stage's outputs (index
 // n = j + r M / R_last, j = t + T b) go to `emit`
 struct Tw2048 {
@@ -262,22 +227,6 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const fl
         stage_compute_rows<M, T, R2, R1, S>(v, t, tws);
         if constexpr (R3 == 1) {
             emit(v, integral_constant<int, R2>{}, integral_constant<int, R1>{});
-        } else if constexpr (FCQT_TW3_EARLY && FCQT_TW3_POW && !FCQT_TW3_SMEM) {
-            constexpr int NS = R1 * R2, scale = 2048 / (NS * R3);
-            float2 wb[kP / R3][3];
-#pragma unroll
-            for (int b = 0; b < kP / R3; ++b) {
-                const int e = ((t + T * b) % NS) * scale;
-                wb[b][0] = __ldg(bp_tw + (e & 2047));
-                wb[b][1] = R3 >= 4 ? __ldg(bp_tw + ((2 * e) & 2047)) : wb[b][0];
-                wb[b][2] = R3 == 8 ? __ldg(bp_tw + ((4 * e) & 2047)) : wb[b][0];
-            }
-            stage_store<M, T, R2, R1, kSH>(v, buf, t);
-            __syncthreads();
-            stage_load<M, T, R3, kSH>(v, buf, t);
-            __syncthreads();
-            stage_compute_pow_pre<M, T, R3, NS, S>(v, wb);
-            emit(v, integral_constant<int, R3>{}, integral_constant<int, NS>{});
         } else {
             stage_store<M, T, R2, R1, kSH>(v, buf, t);
             __syncthreads();

@@ -76,7 +76,7 @@ size_t ws_planes(const cqt_tables* t, int batch) {
     return (size_t)batch * (size_t)t->max_planes * kPlaneStride * sizeof(float2);
 }
 size_t ws_need(const cqt_tables* t, int batch) {
-    const size_t partials = ((size_t)spectrum_ctas(batch) * sizeof(float) + 15) & ~(size_t)15;
+    const size_t partials = ((size_t)spectrum_inv_ctas(batch) * sizeof(float) + 15) & ~(size_t)15;
     return kWsHeader + ws_planes(t, batch) + partials;
 }
 float* ws_partials(const cqt_tables* t, int batch, void* ws) {
@@ -274,6 +274,89 @@ int cqt_debug_expire_waits(int on) {
 }
 
 int32_t cqt_ncoef(const cqt_tables* t) { return t ? t->ncoef : -1; }
+
+// ---- overlap-add halo over peer memory (halo.cu)
+struct cqt_halo {
+    HaloState st;
+};
+
+int cqt_halo_create(int device, int rows, int64_t hop, int wait_ms, cqt_halo** out,
+                    void* handle) {
+    if (!out || !handle || rows < 1 || hop < 1 || wait_ms < 0)
+        return fail(CQT_ERR_ARG, "bad halo arguments (rows, hop >= 1, wait_ms >= 0, out, handle)");
+    *out = nullptr;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    cqt_halo* h = new cqt_halo{};
+    h->st.device = device;
+    h->st.rows = rows;
+    h->st.hop = hop;
+    h->st.wait_ns = (unsigned long long)(wait_ms > 0 ? wait_ms : 10000) * 1000000ull;
+    e = halo_create(&h->st, handle);
+    if (prev >= 0) cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        halo_destroy(&h->st);
+        delete h;
+        return cuda_fail(e, "halo buffer (cudaMalloc / cudaIpcGetMemHandle)");
+    }
+    *out = h;
+    return CQT_OK;
+}
+
+int cqt_halo_connect(cqt_halo* h, const void* left_handle, const void* right_handle) {
+    if (!h) return fail(CQT_ERR_ARG, "null halo");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(h->st.device);
+    if (e == cudaSuccess && left_handle && !h->st.left) e = halo_open(left_handle, &h->st.left);
+    if (e == cudaSuccess && right_handle && !h->st.right)
+        e = halo_open(right_handle, &h->st.right);
+    if (prev >= 0) cudaSetDevice(prev);
+    return e == cudaSuccess ? CQT_OK : cuda_fail(e, "cudaIpcOpenMemHandle(neighbour halo)");
+}
+
+int cqt_halo_send(cqt_halo* h, const float* src, int64_t ld, int64_t epoch, void* stream) {
+    if (!h || !h->st.left || !src || ld < h->st.hop || epoch < 1)
+        return fail(CQT_ERR_ARG, "halo send: not connected to a left neighbour, or bad args");
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != h->st.device) return fail(CQT_ERR_DEVICE, "halo send: wrong current device");
+    const cudaError_t e = halo_send(&h->st, src, ld, epoch, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? CQT_OK : cuda_fail(e, "halo send launch");
+}
+
+int cqt_halo_recv_add(cqt_halo* h, float* dst, int64_t ld, int64_t epoch, void* stream) {
+    if (!h || !h->st.right || !dst || ld < h->st.hop || epoch < 1)
+        return fail(CQT_ERR_ARG, "halo receive: not connected to a right neighbour, or bad args");
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != h->st.device) return fail(CQT_ERR_DEVICE, "halo receive: wrong current device");
+    const cudaError_t e = halo_recv_add(&h->st, dst, ld, epoch, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? CQT_OK : cuda_fail(e, "halo receive launch");
+}
+
+int cqt_halo_waits(cqt_halo* h, unsigned int* expired, int clear) {
+    if (!h || !expired) return fail(CQT_ERR_ARG, "null halo or count");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->st.device);
+    const cudaError_t e = halo_status(&h->st, expired, clear);
+    if (prev >= 0) cudaSetDevice(prev);
+    return e == cudaSuccess ? CQT_OK : cuda_fail(e, "reading the halo wait status");
+}
+
+int cqt_halo_free(cqt_halo* h) {
+    if (!h) return CQT_OK;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->st.device);
+    halo_destroy(&h->st);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete h;
+    return CQT_OK;
+}
 
 size_t cqt_workspace_bytes(const cqt_tables* t, int batch) {
     if (!t || batch < 0) return 0;
@@ -489,6 +572,21 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
         qm_aa[n] = b;
     }
     size_t i_qsy = add(qm_sy.data(), qm_sy.size() * 2), i_qaa = add(qm_aa.data(), qm_aa.size() * 2);
+    // octet masks of the four-CTA inverse spectrum engine
+    constexpr int kO = kQuarter / 2;   // 8192
+    std::vector<uint32_t> om_sy(kO / 2 + 1), om_aa(kO / 2 + 1);
+    for (int n = 0; n <= kO / 2; ++n) {
+        const int bins[8] = {n, kO - n, kO + n, 2 * kO - n, 2 * kO + n, 3 * kO - n, 3 * kO + n,
+                             4 * kO - n};
+        uint32_t a = 0, b = 0;
+        for (int k = 0; k < 8; ++k) {
+            a |= (uint32_t)(h->sy_mask[bins[k]] & 15) << (4 * k);
+            b |= (uint32_t)(h->aa_mask[bins[k]] & 15) << (4 * k);
+        }
+        om_sy[n] = a;
+        om_aa[n] = b;
+    }
+    size_t i_osy = add(om_sy.data(), om_sy.size() * 4), i_oaa = add(om_aa.data(), om_aa.size() * 4);
     // band descriptors in class order (see BandParams)
     std::vector<int4> desc(h->nbands);
     for (int i = 0; i < h->nbands; ++i) {
@@ -542,10 +640,10 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     t->fwd[1] = FwdTab{(const int*)P(i_ass), (const float*)P(i_asg), (const int2*)P(i_assg)};
     t->inv[0] = InvTab{(const int*)P(i_syd), (const float*)P(i_syr), (const float*)P(i_syi),
                        (const unsigned char*)P(i_sym), (const unsigned short*)P(i_qsy),
-                       h->sy_nplanes};
+                       (const unsigned*)P(i_osy), h->sy_nplanes};
     t->inv[1] = InvTab{(const int*)P(i_aad), (const float*)P(i_aar), (const float*)P(i_aai),
                        (const unsigned char*)P(i_aam), (const unsigned short*)P(i_qaa),
-                       h->aa_nplanes};
+                       (const unsigned*)P(i_oaa), h->aa_nplanes};
     t->tw2048 = (const float2*)P(i_tw);
     t->ngroups = h->ngroups;
     for (int g = 0; g < h->ngroups; ++g) {
@@ -635,7 +733,7 @@ int cqt_synthesis_sqerr(const cqt_tables* t, const float* c_re, const float* c_i
     }
     // an empty batch still defines the loss: the sum of nothing
     cudaError_t e = launch_sqerr_finish(batch > 0 ? ws_partials(t, batch, ws) : nullptr,
-                                        spectrum_ctas(batch), loss_scale, loss, s);
+                                        spectrum_inv_ctas(batch), loss_scale, loss, s);
     return e == cudaSuccess ? CQT_OK : cuda_fail(e, "squared-error sum launch");
 }
 

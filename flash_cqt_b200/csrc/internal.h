@@ -20,6 +20,10 @@ struct InvTab {            // synthesis-engine tap table (one per use)
     // per quad n in [0, Q/2]: the masks of bins n, L - n, Q + n, Q - n in
     // bits 0-3, 4-7, 8-11, 12-15 (derived from `mask` at upload)
     const unsigned short* qmask;
+    // per octet n in [0, Q/2] (Q = L/2): the masks of bins n, Q/2 - n,
+    // Q/2 + n, Q - n, Q + n, 3Q/2 - n, 3Q/2 + n, L - n in bits 4i..4i+3
+    // (derived from `mask` at upload; the four-CTA inverse spectrum engine)
+    const unsigned* omask;
     int nplanes;
 };
 
@@ -195,10 +199,37 @@ cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap
 // CTAs of one spectrum launch over `batch` slices (partial sums of the
 // squared-error mode: one per CTA)
 inline int spectrum_ctas(int batch) { return 2 * batch; }
+// the inverse spectrum engine: two CTAs per slice, or four (one cluster of
+// four 8192-point CTAs, two CTAs per SM) with FCQT_SPEC_INV4
+#ifndef FCQT_SPEC_INV4
+#define FCQT_SPEC_INV4 0
+#endif
+inline int spectrum_inv_ctas(int batch) { return (FCQT_SPEC_INV4 ? 4 : 2) * batch; }
 // loss = scale * sum of the n partials, in a fixed order (one CTA)
 cudaError_t launch_sqerr_finish(const float* partial, int n, float scale, float* loss,
                                 cudaStream_t s);
 cudaError_t read_wait_timeouts(unsigned* count);   // expired bounded waits (device)
+
+// overlap-add halo over peer memory (halo.cu)
+struct HaloDev;
+struct HaloState {
+    int device;
+    int rows;
+    long long hop;
+    char* own;          // own exchange buffer (cudaMalloc, IPC-exported)
+    char* left;         // left neighbour's buffer (IPC-mapped) or null
+    char* right;        // right neighbour's buffer (IPC-mapped) or null
+    HaloDev* dv;        // status word, CTA counters, failed epochs (own memory)
+    unsigned long long wait_ns;   // bound of every wait on a neighbour
+};
+cudaError_t halo_create(HaloState* h, void* handle_out);
+cudaError_t halo_open(const void* handle, char** out);
+cudaError_t halo_send(HaloState* h, const float* src, long long ld, long long epoch,
+                      cudaStream_t s);
+cudaError_t halo_recv_add(HaloState* h, float* dst, long long ld, long long epoch,
+                          cudaStream_t s);
+cudaError_t halo_status(HaloState* h, unsigned* expired, int clear);
+void halo_destroy(HaloState* h);
 cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParams& bp,
                              CoefPtr out, cudaStream_t s);
 cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const BandParams& bp,

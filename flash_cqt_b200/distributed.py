@@ -92,6 +92,76 @@ def exchange_halo(local, part, group=None):
     return local[:, start:start + (hi - lo)]
 
 
+class PeerHalo:
+    """The overlap-add halo over peer memory (``cqt_halo_*``): this build's own
+    kernels store rank r's first hop straight into rank r - 1's receive buffer
+    over NVLink (plain peer stores, CUDA IPC mapping, no multicast) and raise
+    a flag; rank r - 1 waits (bounded, 10 s), adds it into its last owned hop
+    and acknowledges.  Stream-ordered, no host synchronisation; an expired
+    wait is counted on the device and raised by ``check`` (or by the next
+    ``exchange`` once the count has reached the host)."""
+
+    HANDLE = 64
+
+    def __init__(self, rows, hop, device, rank, world, has_left, has_right, group=None,
+                 wait_ms=10000):
+        import ctypes
+        from . import _native
+        self._n = _native
+        self._c = ctypes
+        L = _native.lib()
+        self.rows, self.hop, self.device = rows, hop, device
+        self.h = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * self.HANDLE)()
+        _native._check(L.cqt_halo_create(device.index, rows, hop, int(wait_ms),
+                                         ctypes.byref(self.h), handle), "cqt_halo_create")
+        mine = bytes(handle)
+        handles = [None] * world
+        dist.all_gather_object(handles, mine, group=group)
+        left = handles[rank - 1] if has_left else None
+        right = handles[rank + 1] if has_right else None
+        buf = lambda b: (ctypes.c_ubyte * self.HANDLE).from_buffer_copy(b) if b else None
+        _native._check(L.cqt_halo_connect(self.h, buf(left), buf(right)), "cqt_halo_connect")
+        self.epoch = 0
+        self._pending = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    def exchange(self, local, send, recv):
+        """local [rows, window] float32 on the device: send local[:, :hop]
+        to the left neighbour and/or add the right neighbour's hop into
+        local[:, -hop:] (the calls every rank makes in the same order)"""
+        from .engine import _raw_stream_of
+        L = self._n.lib()
+        self.epoch += 1
+        stream = _raw_stream_of(self.device.index)
+        if local.stride(-1) != 1:
+            raise ValueError("the overlap-add window must have unit sample stride")
+        ld = local.stride(0)
+        if send:
+            self._n._check(L.cqt_halo_send(self.h, local.data_ptr(), ld, self.epoch, stream),
+                           "cqt_halo_send")
+        if recv:
+            dst = local[:, local.shape[1] - self.hop:]
+            self._n._check(L.cqt_halo_recv_add(self.h, dst.data_ptr(), ld, self.epoch, stream),
+                           "cqt_halo_recv_add")
+
+    def check(self):
+        """synchronous: raise if any wait of this exchange gave up"""
+        n = self._c.c_uint(0)
+        self._n._check(self._n.lib().cqt_halo_waits(self.h, self._c.byref(n), 1),
+                       "cqt_halo_waits")
+        if n.value:
+            raise RuntimeError(f"overlap-add halo: {n.value} bounded wait(s) on a neighbour "
+                               "gave up (a rank stopped or fell too far behind)")
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h is not None and h.value and self._n._lib is not None:
+            try:
+                self._n.lib().cqt_halo_free(h)
+            except Exception:
+                pass
+
+
 class PartitionedSlicedCQT:
     """A SlicedCQT whose slices are spread over the ranks of a process group.
 
@@ -100,9 +170,16 @@ class PartitionedSlicedCQT:
         y_owned = part.bwd(blocks, side, length)           # owned samples only
     """
 
-    def __init__(self, sliced, rank, world, group=None):
+    def __init__(self, sliced, rank, world, group=None, halo="auto", halo_wait_ms=10000):
+        """halo: "peer" (this build's peer-memory kernels), "collective"
+        (torch.distributed send / receive), or "auto" -- peer memory for CUDA
+        tensors under an NCCL group, the collective otherwise; halo_wait_ms
+        bounds every peer-memory wait on a neighbour"""
         self.sl = sliced
         self.rank, self.world, self.group = rank, world, group
+        self.halo = halo
+        self.halo_wait_ms = halo_wait_ms
+        self._peer = {}
 
     def partition(self, length):
         return Partition(length, self.sl._num_slices(length), self.rank, self.world,
@@ -137,5 +214,34 @@ class PartitionedSlicedCQT:
             buf = self.sl._fused_buffer(se, blocks, side, B * C, p.nslices)
             local = se.synthesis(buf, B * C, p.nslices, length, slice0=p.s0, sample0=lo,
                                  count=hi - lo)
-        own = exchange_halo(local, p, self.group)
+        if self._use_peer(local):
+            self._peer_halo(B * C, p, local.device).exchange(
+                local, send=p.rank > 0 and p.nslices > 0, recv=p.right_nslices > 0)
+            lo_, hi_ = p.owned()
+            start = lo_ - p.synthesis_window()[0]
+            own = local[:, start:start + (hi_ - lo_)]
+        else:
+            own = exchange_halo(local, p, self.group)
         return own.reshape(B, C, -1)
+
+    def _use_peer(self, t):
+        if self.halo == "collective" or self.world == 1:
+            return False
+        if self.halo == "peer":
+            return True
+        return t.is_cuda and dist.get_backend(self.group) == "nccl"
+
+    def _peer_halo(self, rows, p, device):
+        """one exchange per (rows, left, right) shape; created collectively on
+        first use (every rank takes the same bwd calls in the same order)"""
+        key = (rows, p.rank > 0 and p.nslices > 0, p.right_nslices > 0)
+        if key not in self._peer:
+            self._peer[key] = PeerHalo(rows, p.hop, device, p.rank, p.world,
+                                       has_left=key[1], has_right=key[2], group=self.group,
+                                       wait_ms=self.halo_wait_ms)
+        return self._peer[key]
+
+    def check_halo(self):
+        """synchronous: raise if a peer-memory halo wait gave up"""
+        for h in self._peer.values():
+            h.check()

@@ -249,6 +249,31 @@ int cqt_sliced_adj_synthesis(const cqt_tables* t, const cqt_signal* gy, const cq
  * (reads device memory). */
 int cqt_wait_timeouts(unsigned int* count);
 
+/* ---- Overlap-add halo over peer memory (no reference counterpart: the
+ * reference is single-GPU) -----------------------------------------------
+ * A long stream's slices range-partitioned over ranks (one process per GPU)
+ * overlap-add locally; rank r > 0 sends the first hop of its output window
+ * (rows x hop floats) to rank r - 1, which adds it into its last owned hop.
+ * Each rank creates one exchange (a receive buffer exported by CUDA IPC,
+ * handle of CQT_HALO_HANDLE_BYTES), learns its neighbours' handles by any
+ * host means (e.g. an all-gather), and connects.  Calls are stream-ordered
+ * and take an epoch, 1, 2, ... per exchange: send stores the hop into the
+ * left neighbour's buffer with plain peer stores once that neighbour has
+ * consumed epoch - 1, then raises its flag; recv_add waits for its own flag
+ * to reach the epoch, adds, and acknowledges.  Every wait is bounded (10 s
+ * by default) and a wait that gives up is counted in cqt_halo_waits (the data movement is
+ * skipped); nothing hangs.  No multicast or switch reduction is used. */
+#define CQT_HALO_HANDLE_BYTES 64
+typedef struct cqt_halo cqt_halo;
+/* wait_ms: the bound of every wait on a neighbour (0: 10 s) */
+int cqt_halo_create(int device, int rows, int64_t hop, int wait_ms, cqt_halo** out,
+                    void* handle);
+int cqt_halo_connect(cqt_halo* h, const void* left_handle, const void* right_handle);
+int cqt_halo_send(cqt_halo* h, const float* src, int64_t ld, int64_t epoch, void* stream);
+int cqt_halo_recv_add(cqt_halo* h, float* dst, int64_t ld, int64_t epoch, void* stream);
+int cqt_halo_waits(cqt_halo* h, unsigned int* expired, int clear);
+int cqt_halo_free(cqt_halo* h);
+
 /* Diagnostic (no reference counterpart): the bounded waits that gave up in
  * the calls that used `workspace` since its header was last cleared -- the
  * per-workspace, so per-call when checked after each call, form of

@@ -1,9 +1,12 @@
 """The slice-range partitioned sliced transform on the GPU.
 
 Ranks are emulated in one process on one GPU (the halo added by hand) and, when
-two GPUs are present, run as two NCCL processes.  Both must reproduce the
-whole-stream SlicedCQT bit for bit: every slice is computed by the same
-kernel arithmetic, and every output sample is the same two-term sum.
+two to four GPUs are present, run as NCCL processes with either halo transport
+(this build's peer-memory kernels, or torch.distributed send / receive), over
+several consecutive calls.  All must reproduce the whole-stream SlicedCQT bit
+for bit: every slice is computed by the same kernel arithmetic, and every
+output sample is the same two-term sum.  A send dropped on the host must make
+the neighbour's bounded wait give up and be reported.
 """
 import os
 import socket
@@ -72,7 +75,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, q):
+def _nccl_worker(rank, world, port, q, halo="auto", steps=3, drop=False):
+    """one rank of the partitioned stream under NCCL: `steps` fwd + bwd
+    calls (the peer-memory halo's flags and acknowledgements advance one
+    epoch per call); with `drop`, a last exchange in which rank 1 does not
+    send, so rank 0's bounded wait must run out and be reported"""
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -87,38 +94,76 @@ def _nccl_worker(rank, world, port, q):
         dev = torch.device("cuda", rank)
         x = _signal(dev)
         sl = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
-        pc = PartitionedSlicedCQT(sl, rank, world)
-        blocks, side = pc.fwd(x, L)
-        own = pc.bwd(blocks, side, L)
+        pc = PartitionedSlicedCQT(sl, rank, world, halo=halo, halo_wait_ms=1500)
+        outs = []
+        for _ in range(steps):
+            blocks, side = pc.fwd(x, L)
+            outs.append(pc.bwd(blocks, side, L).cpu().numpy())
         torch.cuda.synchronize()
+        pc.check_halo()
+        dropped = None
+        if drop:
+            h = next(iter(pc._peer.values()))
+            p = pc.partition(L)
+            lo, hi = p.synthesis_window()
+            local = torch.zeros(2, hi - lo, device=dev)
+            h.exchange(local, send=False, recv=rank == 0)   # rank 1 drops its hop
+            torch.cuda.synchronize()
+            try:
+                pc.check_halo()
+                dropped = "no error"
+            except RuntimeError as e:
+                dropped = "raised" if "gave up" in str(e) else repr(e)
+            # the context is still usable after the expired wait
+            xs = x[..., :70000].contiguous()
+            assert torch.isfinite(sl.bwd(*sl.fwd(xs), length=70000)).all()
         lo, hi = pc.partition(L).owned()
-        q.put((rank, lo, hi, own.cpu().numpy()))
+        q.put((rank, lo, hi, outs, dropped))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_nccl_ranks_match_whole_stream(dev):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _run_ranks(world, **kw):
     import torch.multiprocessing as mp
-    from flash_cqt_b200 import SlicedCQT
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q), kwargs=kw)
+             for r in range(world)]
     for p in procs:
         p.start()
-    got = sorted(q.get(timeout=300) for _ in range(world))
+    got = sorted((q.get(timeout=300) for _ in range(world)), key=lambda g: g[0])
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    y = np.concatenate([g[3] for g in got], axis=-1)
+    return got
+
+
+@pytest.mark.parametrize("halo", ["peer", "collective"])
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_nccl_ranks_match_whole_stream(dev, halo, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from flash_cqt_b200 import SlicedCQT
+    got = _run_ranks(world, halo=halo, steps=3)
     sl = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=65536, device=dev)
     x = _signal(dev)
     want = sl.bwd(*sl.fwd(x), length=L).cpu().numpy()
-    np.testing.assert_array_equal(y, want)
+    for step in range(3):
+        y = np.concatenate([g[3][step] for g in got], axis=-1)
+        np.testing.assert_array_equal(y, want)
+
+
+def test_peer_halo_dropped_send_is_reported(dev):
+    """rank 1 skips one send (a failure made on the host, between steps):
+    rank 0's bounded wait gives up after 1.5 s, check_halo raises, and the
+    context stays usable; nothing faults or hangs"""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    got = _run_ranks(2, halo="peer", steps=1, drop=True)
+    assert got[0][4] == "raised", got[0][4]
+    assert got[1][4] == "no error"
 
 
 def test_unaligned_rows_and_offsets_agree_bitwise(dev):
