@@ -76,7 +76,7 @@ size_t ws_planes(const cqt_tables* t, int batch) {
     return (size_t)batch * (size_t)t->max_planes * kPlaneStride * sizeof(float2);
 }
 size_t ws_need(const cqt_tables* t, int batch) {
-    const size_t partials = ((size_t)spectrum_inv_ctas(batch) * sizeof(float) + 15) & ~(size_t)15;
+    const size_t partials = ((size_t)spectrum_ctas(batch) * sizeof(float) + 15) & ~(size_t)15;
     return kWsHeader + ws_planes(t, batch) + partials;
 }
 float* ws_partials(const cqt_tables* t, int batch, void* ws) {
@@ -572,21 +572,6 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
         qm_aa[n] = b;
     }
     size_t i_qsy = add(qm_sy.data(), qm_sy.size() * 2), i_qaa = add(qm_aa.data(), qm_aa.size() * 2);
-    // octet masks of the four-CTA inverse spectrum engine
-    constexpr int kO = kQuarter / 2;   // 8192
-    std::vector<uint32_t> om_sy(kO / 2 + 1), om_aa(kO / 2 + 1);
-    for (int n = 0; n <= kO / 2; ++n) {
-        const int bins[8] = {n, kO - n, kO + n, 2 * kO - n, 2 * kO + n, 3 * kO - n, 3 * kO + n,
-                             4 * kO - n};
-        uint32_t a = 0, b = 0;
-        for (int k = 0; k < 8; ++k) {
-            a |= (uint32_t)(h->sy_mask[bins[k]] & 15) << (4 * k);
-            b |= (uint32_t)(h->aa_mask[bins[k]] & 15) << (4 * k);
-        }
-        om_sy[n] = a;
-        om_aa[n] = b;
-    }
-    size_t i_osy = add(om_sy.data(), om_sy.size() * 4), i_oaa = add(om_aa.data(), om_aa.size() * 4);
     // band descriptors in class order (see BandParams)
     std::vector<int4> desc(h->nbands);
     for (int i = 0; i < h->nbands; ++i) {
@@ -640,10 +625,10 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     t->fwd[1] = FwdTab{(const int*)P(i_ass), (const float*)P(i_asg), (const int2*)P(i_assg)};
     t->inv[0] = InvTab{(const int*)P(i_syd), (const float*)P(i_syr), (const float*)P(i_syi),
                        (const unsigned char*)P(i_sym), (const unsigned short*)P(i_qsy),
-                       (const unsigned*)P(i_osy), h->sy_nplanes};
+                       h->sy_nplanes};
     t->inv[1] = InvTab{(const int*)P(i_aad), (const float*)P(i_aar), (const float*)P(i_aai),
                        (const unsigned char*)P(i_aam), (const unsigned short*)P(i_qaa),
-                       (const unsigned*)P(i_oaa), h->aa_nplanes};
+                       h->aa_nplanes};
     t->tw2048 = (const float2*)P(i_tw);
     t->ngroups = h->ngroups;
     for (int g = 0; g < h->ngroups; ++g) {
@@ -733,7 +718,7 @@ int cqt_synthesis_sqerr(const cqt_tables* t, const float* c_re, const float* c_i
     }
     // an empty batch still defines the loss: the sum of nothing
     cudaError_t e = launch_sqerr_finish(batch > 0 ? ws_partials(t, batch, ws) : nullptr,
-                                        spectrum_inv_ctas(batch), loss_scale, loss, s);
+                                        spectrum_ctas(batch), loss_scale, loss, s);
     return e == cudaSuccess ? CQT_OK : cuda_fail(e, "squared-error sum launch");
 }
 

@@ -20,10 +20,6 @@ struct InvTab {            // synthesis-engine tap table (one per use)
     // per quad n in [0, Q/2]: the masks of bins n, L - n, Q + n, Q - n in
     // bits 0-3, 4-7, 8-11, 12-15 (derived from `mask` at upload)
     const unsigned short* qmask;
-    // per octet n in [0, Q/2] (Q = L/2): the masks of bins n, Q/2 - n,
-    // Q/2 + n, Q - n, Q + n, 3Q/2 - n, 3Q/2 + n, L - n in bits 4i..4i+3
-    // (derived from `mask` at upload; the four-CTA inverse spectrum engine)
-    const unsigned* omask;
     int nplanes;
 };
 
@@ -199,12 +195,6 @@ cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap
 // CTAs of one spectrum launch over `batch` slices (partial sums of the
 // squared-error mode: one per CTA)
 inline int spectrum_ctas(int batch) { return 2 * batch; }
-// the inverse spectrum engine: two CTAs per slice, or four (one cluster of
-// four 8192-point CTAs, two CTAs per SM) with FCQT_SPEC_INV4
-#ifndef FCQT_SPEC_INV4
-#define FCQT_SPEC_INV4 0
-#endif
-inline int spectrum_inv_ctas(int batch) { return (FCQT_SPEC_INV4 ? 4 : 2) * batch; }
 // loss = scale * sum of the n partials, in a fixed order (one CTA)
 cudaError_t launch_sqerr_finish(const float* partial, int n, float scale, float* loss,
                                 cudaStream_t s);

@@ -43,12 +43,6 @@ namespace fcqt {
 
 // points per thread of the forward and inverse kernels (16 -> 1024 threads,
 // stages 16 x 16 x 16 x 4; 32 -> 512 threads, stages 32 x 32 x 16)
-// the forward reads each sample once and pushes half of the DIF outputs
-// into the partner CTA (1) or reads each sample in both CTAs (0)
-#ifndef FCQT_SPEC_FWD_PUSH
-#define FCQT_SPEC_FWD_PUSH 0
-#endif
-
 #ifndef FCQT_SPEC_P_FWD
 #define FCQT_SPEC_P_FWD 32
 #endif
@@ -68,9 +62,6 @@ struct SpecSched {
 // 16384 points per CTA (two CTAs per slice, one CTA per SM)
 using S16k32 = SpecSched<16384, 32, 3, 32, 32, 16, 1>;
 using S16k16 = SpecSched<16384, 16, 4, 16, 16, 16, 4>;
-// 8192 points per CTA (four CTAs per slice, two CTAs per SM): the inverse of
-// the four-CTA engine
-using S8k16 = SpecSched<8192, 16, 4, 16, 16, 16, 2>;
 
 template <class C>
 constexpr int sR(int s) { return s == 1 ? C::R1 : s == 2 ? C::R2 : s == 3 ? C::R3 : C::R4; }
@@ -95,17 +86,13 @@ constexpr int smemOf() { return (padded<shiftOf<C>()>(C::N) + 512 + twTotal<C>()
 
 template <class C>
 constexpr bool sched_ok() { return sNS<C>(C::NST) * sR<C>(C::NST) == C::N; }
-static_assert(sched_ok<S16k32>() && sched_ok<S16k16>() && sched_ok<S8k16>(),
+static_assert(sched_ok<S16k32>() && sched_ok<S16k16>(),
               "stage radices must multiply to the length");
 
 // the twiddle-row blob holds the rows of every schedule, in this order
 template <class C>
-constexpr int rowsOff() {
-    return std::is_same<C, S16k32>::value   ? 0
-           : std::is_same<C, S16k16>::value ? twTotal<S16k32>()
-                                            : twTotal<S16k32>() + twTotal<S16k16>();
-}
-constexpr int kSpecRowsTotal = twTotal<S16k32>() + twTotal<S16k16>() + twTotal<S8k16>();
+constexpr int rowsOff() { return std::is_same<C, S16k32>::value ? 0 : twTotal<S16k32>(); }
+constexpr int kSpecRowsTotal = twTotal<S16k32>() + twTotal<S16k16>();
 
 using CF = std::conditional<FCQT_SPEC_P_FWD == 32, S16k32, S16k16>::type;
 using CI = std::conditional<FCQT_SPEC_P_INV == 32, S16k32, S16k16>::type;
@@ -303,17 +290,11 @@ __device__ __forceinline__ void prefetch_signal_part(const SigMap& m, long g, in
     }
 }
 
-// The forward body.  PUSH = false: every CTA reads both halves z[n], z[n + Q]
-// of its slice and keeps its own DIF branch (each sample is read by both
-// CTAs, the second time from L2).  PUSH = true (the two CTAs form a cluster):
-// CTA h reads the pairs n in [h Q/2, (h + 1) Q/2) only, forms both branches,
-// keeps its own in shared memory and pushes the partner's into the partner's
-// shared memory while its loads are in flight -- every sample is read once.
-template <int MODE, bool PUSH>
-__device__ __forceinline__ void spectrum_fwd_body(const SigMap& in, float2* __restrict__ X,
-                                                  const float2* __restrict__ ghi,
-                                                  const float2* __restrict__ glo,
-                                                  const float2* __restrict__ gtw, int ahead) {
+template <int MODE>
+__global__ void __launch_bounds__(CF::T, 1)
+spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
+                    const float2* __restrict__ ghi, const float2* __restrict__ glo,
+                    const float2* __restrict__ gtw, int ahead) {
     using C = CF;
     constexpr bool SLICED = MODE == kSigSliced;
     constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
@@ -326,45 +307,23 @@ __device__ __forceinline__ void spectrum_fwd_body(const SigMap& in, float2* __re
     const int t = threadIdx.x;
     pdl_launch_dependents();
     load_tables<C>(hl, tws, ghi, glo, gtw);
-    if constexpr (PUSH)
-        cooperative_groups::this_cluster().sync();   // tables staged, the partner is running
-    else
-        __syncthreads();
+    __syncthreads();
     pdl_wait();   // the previous kernel of the stream has completed
     const Tw64k tw{hl, hl + 256};
 
-    // stage 1 inputs: the radix-2 DIF split of z
+    // stage 1 inputs straight from global: the radix-2 DIF split of z
     const SliceReader z = make_reader<SLICED>(in, slice);
     float2 v[P];
     auto load = [&](auto&& zf) {
-        if constexpr (PUSH) {
-            namespace cg = cooperative_groups;
-            cg::cluster_group cl = cg::this_cluster();
-            float2* peer = cl.map_shared_rank(buf, h ^ 1);
-            float2* u0 = h ? peer : buf;
-            float2* u1 = h ? buf : peer;
 #pragma unroll
-            for (int i = 0; i < (kQuarter / 2) / T; ++i) {
-                const int n = h * (kQuarter / 2) + t + T * i;
+        for (int b = 0; b < P / C::R1; ++b)
+#pragma unroll
+            for (int r = 0; r < C::R1; ++r) {
+                const int n = t + T * b + r * (kQuarter / C::R1);
                 const float2 a = zf(n);
                 const float2 c = zf(n + kQuarter);
-                u0[PADI<SH>(n)] = cadd(a, c);
-                u1[PADI<SH>(n)] = cmul(csub(a, c), tw(2 * n));
+                v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
             }
-            cl.sync();   // both halves of u_h are in place
-            stage_load<kQuarter, T, C::R1, SH>(v, buf, t);
-            __syncthreads();   // stage 1 reads done before stage 2's stores
-        } else {
-#pragma unroll
-            for (int b = 0; b < P / C::R1; ++b)
-#pragma unroll
-                for (int r = 0; r < C::R1; ++r) {
-                    const int n = t + T * b + r * (kQuarter / C::R1);
-                    const float2 a = zf(n);
-                    const float2 c = zf(n + kQuarter);
-                    v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
-                }
-        }
     };
     if constexpr (MODE == kSigSqErr) {
         // the MSE gradient s (y - target) formed on load (s = 2 dL/dloss / n)
@@ -422,22 +381,6 @@ __device__ __forceinline__ void spectrum_fwd_body(const SigMap& in, float2* __re
             Xs[kHalf - q] = make_float2(0.5f * (sb.x - wdb.y), 0.5f * (sb.y + wdb.x));
         }
     }
-}
-
-template <int MODE>
-__global__ void __launch_bounds__(CF::T, 1)
-spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
-                    const float2* __restrict__ ghi, const float2* __restrict__ glo,
-                    const float2* __restrict__ gtw, int ahead) {
-    spectrum_fwd_body<MODE, false>(in, X, ghi, glo, gtw, ahead);
-}
-
-template <int MODE>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CF::T, 1)
-spectrum_fwd_push_kernel(const SigMap in, float2* __restrict__ X,
-                         const float2* __restrict__ ghi, const float2* __restrict__ glo,
-                         const float2* __restrict__ gtw, int ahead) {
-    spectrum_fwd_body<MODE, true>(in, X, ghi, glo, gtw, ahead);
 }
 
 // F[q] from the colour planes flagged in the 4-bit mask mk, fixed plane order.
@@ -658,201 +601,6 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     }
 }
 
-// ---------------------------------------------------------------------------
-// Four-CTA inverse engine.  The 32768-point inverse FFT of a slice splits by
-// output residue mod 4 (radix-4 decimation in frequency): CTA h of the
-// slice's cluster computes z[4m + h] as the 8192-point inverse FFT of
-//   u_h[k] = conj(W_32768^{k h}) sum_j Zs[k + 8192 j] i^{j h},   k < 8192.
-// Octets of half-spectrum bins {n, O - n, O + n, 2O - n, 2O + n, 3O - n,
-// 3O + n, 4O - n} (O = 8192, n <= O/2) close under the retangle pairing
-// (q, L - q) and give Zs at k = n and k = O - n for all four j: so each CTA
-// reads the colour planes of a quarter of the octets, forms their eight Zs
-// values, runs the two radix-4 butterflies and writes u_h[n], u_h[O - n] into
-// CTA h's shared memory (six of the eight into peers).  Two such CTAs share an
-// SM (8192 points, 512 threads of 64 registers), so one can compute while the
-// other waits on memory or a barrier.
-template <int MODE>
-__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(S8k16::T, 2)
-spectrum_inv4_kernel(const float2* __restrict__ E, const unsigned* __restrict__ omask,
-                     const SigMap out, const float2* __restrict__ ghi,
-                     const float2* __restrict__ glo, const float2* __restrict__ gtw,
-                     int nplanes, int ahead) {
-    using C = S8k16;
-    constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
-    constexpr int O = kQuarter / 2;   // 8192
-    constexpr bool SLICED = MODE == kSigSliced;
-    namespace cg = cooperative_groups;
-    extern __shared__ float4 smem_raw[];
-    float2* buf = reinterpret_cast<float2*>(smem_raw);
-    float2* hl = buf + padded<SH>(O);
-    float2* tws = hl + 512;
-    cg::cluster_group cl = cg::this_cluster();
-    const int h = (int)cl.block_rank();
-    float2* dst[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) dst[k] = cl.map_shared_rank(buf, k);
-    const long slice = blockIdx.x >> 2;
-    const int t = threadIdx.x;
-    pdl_launch_dependents();
-    load_tables<C>(hl, tws, ghi, glo, gtw);
-    cl.sync();   // tables staged, and every CTA of the cluster is running
-    pdl_wait();  // the previous kernel of the stream has completed
-    const Tw64k tw{hl, hl + 256};
-    const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
-    const bool two = nplanes > 1;
-
-    // octets [h O/8, (h + 1) O/8), the last CTA also the middle octet O/2
-    const int nlo = h * (O / 8);
-    const int nhi = h == 3 ? O / 2 + 1 : (h + 1) * (O / 8);
-    for (int n = nlo + t; n < nhi; n += T) {
-        const unsigned om = __ldg(omask + n);
-        const int bin[8] = {n, O - n, O + n, 2 * O - n, 2 * O + n, 3 * O - n, 3 * O + n,
-                            4 * O - n};
-        float2 f[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float2 e0 = Es[bin[k]];
-            const float2 e1 = two ? Es[kPlaneStride + bin[k]] : make_float2(0.f, 0.f);
-            f[k] = plane_pick(Es, (om >> (4 * k)) & 15u, bin[k], e0, e1);
-        }
-        if (n == 0) {   // irfft ignores the imaginary parts of DC and Nyquist
-            f[0].y = 0.f;
-            f[7].y = 0.f;
-        }
-        // W^q (W = W_65536) of the eight Zs positions from three lookups and
-        // exact symmetries: W^{2O} = -i, W^{4O} = -1
-        const float2 wa = tw(n), wb = tw(O + n), wc = tw(O - n);
-        const float2 mi_wa = make_float2(wa.y, -wa.x);     // -i W^n      = W^{2O + n}
-        const float2 mi_wb = make_float2(wb.y, -wb.x);     // -i W^{O+n}  = W^{3O + n}
-        const float2 mi_wc = make_float2(wc.y, -wc.x);     // -i W^{O-n}  = W^{3O - n}
-        const float2 mi_cwa = make_float2(-wa.y, -wa.x);   // -i conj W^n = W^{2O - n}
-        const float2 m_cwa = make_float2(-wa.x, wa.y);     // -conj W^n   = W^{4O - n}
-        float2 x[4], xm[4];
-        x[0] = retangle(f[0], f[7], wa);       // Zs[n]
-        x[1] = retangle(f[2], f[5], wb);       // Zs[O + n]
-        x[2] = retangle(f[4], f[3], mi_wa);    // Zs[2O + n]
-        x[3] = retangle(f[6], f[1], mi_wb);    // Zs[3O + n]
-        xm[0] = retangle(f[1], f[6], wc);      // Zs[O - n]
-        xm[1] = retangle(f[3], f[4], mi_cwa);  // Zs[2O - n]
-        xm[2] = retangle(f[5], f[2], mi_wc);   // Zs[3O - n]
-        xm[3] = retangle(f[7], f[0], m_cwa);   // Zs[4O - n]
-        dft<4, +1>(x);    // sum_j x_j i^{j h}, h = 0..3
-        dft<4, +1>(xm);
-        // u_h[n] = conj(W_32768^{n h}) x_h; u_h[O - n] = conj(W_32768^{(O - n) h}) xm_h
-        // with W_32768^{O h} = (-i)^h, so conj(W_32768^{(O-n)h}) = i^h W_32768^{n h}
-        const float2 t1 = tw(2 * n), t2 = tw(4 * n), t3 = tw(6 * n);
-        const int pn = PADI<SH>(n);
-        dst[0][pn] = x[0];
-        dst[1][pn] = cmulc(x[1], t1);
-        dst[2][pn] = cmulc(x[2], t2);
-        dst[3][pn] = cmulc(x[3], t3);
-        const int m = O - n;
-        if (m != n && m < O) {
-            const int pm = PADI<SH>(m);
-            dst[0][pm] = xm[0];
-            dst[1][pm] = mul_si<+1>(cmul(xm[1], t1));                      // i W^{n}
-            dst[2][pm] = make_float2(-cmul(xm[2], t2).x, -cmul(xm[2], t2).y);  // -W^{2n}
-            dst[3][pm] = mul_si<-1>(cmul(xm[3], t3));                      // -i W^{3n}
-        }
-    }
-    if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
-        // planes 0 and 1 of the slice `ahead / 4` slices ahead: CTA h of that
-        // cluster prefetches half h & 1 of plane h >> 1 (rows 16-byte aligned)
-        const long nb = blockIdx.x + (long)ahead;
-        const int pl = (int)((nb & 3) >> 1), half = (int)(nb & 1);
-        if (pl < nplanes)
-            prefetch_l2_bulk(E + (nb >> 2) * (long)(nplanes * kPlaneStride) +
-                                 (long)pl * kPlaneStride + half * (kPlaneStride / 2),
-                             (long long)(kPlaneStride / 2) * 8, t);
-    }
-    cl.sync();   // every u_h is in place
-
-    float2 v[P];
-    stage_load<O, T, C::R1, SH>(v, buf, t);
-    __syncthreads();
-    spec_compute<C, 1, +1>(v, t, tws);
-    const float inv = 1.0f / (float)kHalf;
-    if constexpr (MODE == kSigPlain) {
-        // z[4m + h] -> samples 8m + 2h, 8m + 2h + 1
-        float2* ys = reinterpret_cast<float2*>(out.y + slice * kSlice);
-        spec_stages<C, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-            constexpr int R = sR<C>(C::NST), NS = sNS<C>(C::NST);
-#pragma unroll
-            for (int b = 0; b < P / R; ++b)
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int nn = t + T * b + NS * r;
-                    ys[4 * nn + h] = cscale(w[b * R + r], inv);
-                }
-        });
-    } else if constexpr (MODE == kSigSqErr) {
-        float2* ys = reinterpret_cast<float2*>(out.y + slice * kSlice);
-        const float2* ts = reinterpret_cast<const float2*>(out.target + slice * kSlice);
-        float acc = 0.f;
-        spec_stages<C, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-            constexpr int R = sR<C>(C::NST), NS = sNS<C>(C::NST);
-#pragma unroll
-            for (int b = 0; b < P / R; ++b)
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int nn = t + T * b + NS * r;
-                    const float2 val = cscale(w[b * R + r], inv);
-                    ys[4 * nn + h] = val;
-                    const float2 tv = __ldg(ts + 4 * nn + h);
-                    const float dx = val.x - tv.x, dy = val.y - tv.y;
-                    acc = fmaf(dx, dx, acc);
-                    acc = fmaf(dy, dy, acc);
-                }
-        });
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-        __shared__ float warp_sum[T / 32];
-        if ((t & 31) == 0) warp_sum[t >> 5] = acc;
-        __syncthreads();
-        if (t == 0) {
-            float sum = 0.f;
-            for (int w = 0; w < T / 32; ++w) sum += warp_sum[w];
-            out.partial[blockIdx.x] = sum;
-        }
-    } else {
-        // un-roll by +-H and overlap-add into the zeroed output (two terms per
-        // sample: order-independent)
-        const long long row = slice / out.S;
-        const int sg = out.slice0 + (int)(slice % out.S);
-        float* yr = out.y + row * out.ld - out.sample0;
-        const long long p0 = 2LL * kQuarter * (sg - 1);
-        const int shift = (sg & 1) ? -kQuarter : kQuarter;
-        const float* wnd = out.window;
-        long long lo, hi;
-        sample_range(out, lo, hi);
-        const bool vec = pairs_aligned(out.y + row * out.ld, out.sample0, wnd);
-        spec_stages<C, 2, +1>(v, buf, tws, t, [&](float2 (&w)[P]) {
-            constexpr int R = sR<C>(C::NST), NS = sNS<C>(C::NST);
-#pragma unroll
-            for (int b = 0; b < P / R; ++b)
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int nn = t + T * b + NS * r;
-                    float2 val = cscale(w[b * R + r], inv);
-                    const int j = (2 * (4 * nn + h) + shift) & (kSlice - 1);
-                    if (wnd) {
-                        const float2 wj = vec ? __ldg(reinterpret_cast<const float2*>(wnd + j))
-                                              : make_float2(__ldg(wnd + j), __ldg(wnd + j + 1));
-                        val.x *= wj.x;
-                        val.y *= wj.y;
-                    }
-                    const long long p = p0 + j;
-                    if (vec && p >= lo && p + 1 < hi) {
-                        atomicAdd(reinterpret_cast<float2*>(yr + p), val);
-                    } else {
-                        if (p >= lo && p < hi) atomicAdd(yr + p, val.x);
-                        if (p + 1 >= lo && p + 1 < hi) atomicAdd(yr + p + 1, val.y);
-                    }
-                }
-        });
-    }
-}
-
 }  // namespace
 
 int spectrum_twiddle_count() { return kSpecRowsTotal; }
@@ -887,7 +635,6 @@ void rows_for(float2* out) {
 void spectrum_twiddle_rows(float2* out) {
     rows_for<S16k32>(out + rowsOff<S16k32>());
     rows_for<S16k16>(out + rowsOff<S16k16>());
-    rows_for<S8k16>(out + rowsOff<S8k16>());
 }
 
 #ifndef FCQT_SPEC_PREFETCH
@@ -947,11 +694,6 @@ cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& s
         return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_ctas(batch)), dim3(CF::T),
                           smemOf<CF>(), s, in, X, st.hi, st.lo, st.rows, ahead);
     };
-    if (FCQT_SPEC_FWD_PUSH) {
-        if (in.S > 0) return go(spectrum_fwd_push_kernel<kSigSliced>);
-        if (in.target) return go(spectrum_fwd_push_kernel<kSigSqErr>);
-        return go(spectrum_fwd_push_kernel<kSigPlain>);
-    }
     if (in.S > 0) return go(spectrum_fwd_kernel<kSigSliced>);
     if (in.target) return go(spectrum_fwd_kernel<kSigSqErr>);
     return go(spectrum_fwd_kernel<kSigPlain>);
@@ -960,17 +702,6 @@ cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& s
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
                                 const SpecTables& st, int batch, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    if (FCQT_SPEC_INV4) {   // four 8192-point CTAs per slice, two per SM
-        const int ahead = 2 * wave_ctas();
-        auto go4 = [&](auto kern) {
-            return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_inv_ctas(batch)),
-                              dim3(S8k16::T), smemOf<S8k16>(), s, E, tab.omask, out, st.hi,
-                              st.lo, st.rows, tab.nplanes, ahead);
-        };
-        if (out.S > 0) return go4(spectrum_inv4_kernel<kSigSliced>);
-        if (out.partial) return go4(spectrum_inv4_kernel<kSigSqErr>);
-        return go4(spectrum_inv4_kernel<kSigPlain>);
-    }
     const int ahead = wave_ctas();
     auto go = [&](auto kern) {
         return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_ctas(batch)), dim3(CI::T),
@@ -985,21 +716,10 @@ cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap
 cudaError_t init_spectrum_attributes() {
     const void* fwd[] = {(const void*)spectrum_fwd_kernel<kSigPlain>,
                          (const void*)spectrum_fwd_kernel<kSigSliced>,
-                         (const void*)spectrum_fwd_kernel<kSigSqErr>,
-                         (const void*)spectrum_fwd_push_kernel<kSigPlain>,
-                         (const void*)spectrum_fwd_push_kernel<kSigSliced>,
-                         (const void*)spectrum_fwd_push_kernel<kSigSqErr>};
+                         (const void*)spectrum_fwd_kernel<kSigSqErr>};
     const void* inv[] = {(const void*)spectrum_inv_kernel<kSigPlain>,
                          (const void*)spectrum_inv_kernel<kSigSliced>,
                          (const void*)spectrum_inv_kernel<kSigSqErr>};
-    const void* inv4[] = {(const void*)spectrum_inv4_kernel<kSigPlain>,
-                          (const void*)spectrum_inv4_kernel<kSigSliced>,
-                          (const void*)spectrum_inv4_kernel<kSigSqErr>};
-    for (const void* f : inv4) {
-        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             smemOf<S8k16>());
-        if (e != cudaSuccess) return e;
-    }
     for (const void* f : fwd) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              smemOf<CF>());

@@ -13,7 +13,11 @@ samples [2H s0, 2H s1):
   q + 1, so the only hop a rank cannot finish alone is its last one, which
   also gets the first-half contribution of the next rank's first slice.  Each
   rank r > 0 therefore sends one hop (2H samples per row) to rank r - 1, which
-  adds it in (``exchange_halo``); nothing else crosses NVLink.
+  adds it in; nothing else crosses NVLink.  On GPUs under NCCL the hop moves
+  through this build's peer-memory kernels (``PeerHalo``: plain NVLink stores
+  into the neighbour's IPC-mapped buffer, a flag, an acknowledgement, bounded
+  waits); otherwise -- and on CPU ranks -- through torch.distributed send /
+  receive (``exchange_halo``).
 
 The partition is pure bookkeeping on slice indices; the transform itself is
 the fused sliced kernels (``SlicedEngine``) on each rank's device.
@@ -214,9 +218,9 @@ class PartitionedSlicedCQT:
             buf = self.sl._fused_buffer(se, blocks, side, B * C, p.nslices)
             local = se.synthesis(buf, B * C, p.nslices, length, slice0=p.s0, sample0=lo,
                                  count=hi - lo)
-        if self._use_peer(local):
-            self._peer_halo(B * C, p, local.device).exchange(
-                local, send=p.rank > 0 and p.nslices > 0, recv=p.right_nslices > 0)
+        halo = self._peer_halo(B * C, p, local.device) if self._use_peer(local) else None
+        if halo is not None:
+            halo.exchange(local, send=p.rank > 0 and p.nslices > 0, recv=p.right_nslices > 0)
             lo_, hi_ = p.owned()
             start = lo_ - p.synthesis_window()[0]
             own = local[:, start:start + (hi_ - lo_)]
@@ -236,9 +240,22 @@ class PartitionedSlicedCQT:
         first use (every rank takes the same bwd calls in the same order)"""
         key = (rows, p.rank > 0 and p.nslices > 0, p.right_nslices > 0)
         if key not in self._peer:
-            self._peer[key] = PeerHalo(rows, p.hop, device, p.rank, p.world,
-                                       has_left=key[1], has_right=key[2], group=self.group,
-                                       wait_ms=self.halo_wait_ms)
+            err = None
+            try:
+                h = PeerHalo(rows, p.hop, device, p.rank, p.world, has_left=key[1],
+                             has_right=key[2], group=self.group, wait_ms=self.halo_wait_ms)
+            except RuntimeError as e:   # e.g. no peer access between these devices
+                h, err = None, str(e)
+            # every rank must take the same transport: agree before first use
+            errs = [None] * p.world
+            dist.all_gather_object(errs, err, group=self.group)
+            bad = [e for e in errs if e]
+            if bad:
+                if self.halo == "peer":
+                    raise RuntimeError(f"peer-memory halo unavailable: {bad[0]}")
+                self.halo = "collective"   # auto: torch.distributed on every rank
+                return None
+            self._peer[key] = h
         return self._peer[key]
 
     def check_halo(self):
