@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--reference-gpu-only", action="store_true",
                     help="run only the same-box GPU baseline of the reference's own "
                          "kernels and print it")
+    ap.add_argument("--train-only", action="store_true",
+                    help="run only the B = 16 train step measurements and print them "
+                         "(for profiling its launches)")
     ap.add_argument("--sliced-only", action="store_true",
                     help="run only the config-5 long-stream measurement and print its "
                          "result (for profiling the sliced kernels)")
@@ -355,6 +358,17 @@ def main():
     if args.reference_gpu_only:
         if rank == 0:
             print(json.dumps({"reference_gpu": reference_gpu(dev)}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    if args.train_only:
+        pk = ROOT / "MEASURED_PEAKS.json"
+        hbm = (json.loads(pk.read_text()).get("hbm_gbs") if pk.exists() else None) or 6650.0
+        cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=N, device=dev)
+        r = train_step(TrainableCQT(cqt, dev), dev, max(args.warmup, 3), args.steps, hbm)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -732,7 +746,16 @@ def extras(args, eng, t, dev, world, rank, barrier, W, K, hbm=6549.1):
         "snr_db": float(10 * torch.log10((xd ** 2).sum() / ((yd - xd) ** 2).sum())),
         "input": "8 seeded sinusoids + N(0, 0.01^2), seed 1, graph replay"}
     del g2
-    # ---- train step, batch 16: analysis -> synthesis -> MSE -> backward
+    out.update(train_step(t, dev, W, K, hbm))
+    return out
+
+
+def train_step(t, dev, W, K, hbm):
+    """config 3: B = 16 train step (analysis -> synthesis -> MSE vs a seeded
+    target -> backward), eager as the reference writes it, with the loss
+    folded into the engines, and the latter's device time under graph replay"""
+    import torch
+    out = {}
     Bt = 16
     gx = torch.Generator(device=dev).manual_seed(2)
     xt = torch.randn(Bt, N, device=dev, generator=gx)

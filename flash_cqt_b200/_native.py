@@ -39,6 +39,7 @@ class HostTables(ctypes.Structure):
         ("aa_dest", _i32p), ("aa_gre", _f32p), ("aa_gim", _f32p),
         ("aa_mask", _u8p), ("aa_nplanes", ctypes.c_int32),
         ("tw2048", _f32p), ("tw_hi", _f32p), ("tw_lo", _f32p),
+        ("slice_len", ctypes.c_int32),
     ]
 
 
@@ -80,6 +81,8 @@ def lib():
             L.cqt_tables_free.restype = ci
             L.cqt_ncoef.argtypes = [vp]
             L.cqt_ncoef.restype = ctypes.c_int32
+            L.cqt_slice_len.argtypes = [vp]
+            L.cqt_slice_len.restype = ctypes.c_int32
             L.cqt_workspace_bytes.argtypes = [vp, ci]
             L.cqt_workspace_bytes.restype = sz
             for name in ("cqt_analysis", "cqt_synthesis", "cqt_adj_analysis",
@@ -130,7 +133,7 @@ def lib():
 
 def exported_symbols():
     """Names the C header declares (checked by the CPU tests)."""
-    return ["cqt_tables_upload", "cqt_tables_free", "cqt_ncoef",
+    return ["cqt_tables_upload", "cqt_tables_free", "cqt_ncoef", "cqt_slice_len",
             "cqt_workspace_bytes", "cqt_analysis", "cqt_synthesis",
             "cqt_adj_analysis", "cqt_adj_synthesis", "cqt_synthesis_sqerr",
             "cqt_adj_synthesis_sqerr", "cqt_launch_stage",
@@ -263,12 +266,14 @@ class DeviceTables:
         h.tw2048 = arr(tabs["tw2048"], np.float32, ctypes.c_float)
         h.tw_hi = arr(tabs["tw_hi"], np.float32, ctypes.c_float)
         h.tw_lo = arr(tabs["tw_lo"], np.float32, ctypes.c_float)
+        h.slice_len = int(tabs.get("slice_len", 65536))
         handle = ctypes.c_void_p()
         _check(L.cqt_tables_upload(ctypes.byref(h), int(device_index),
                                    ctypes.byref(handle)), "cqt_tables_upload")
         self.handle = handle
         self.device_index = int(device_index)
         self.ncoef = int(L.cqt_ncoef(handle))
+        self.slice_len = int(L.cqt_slice_len(handle))
 
     def workspace_bytes(self, batch):
         return int(lib().cqt_workspace_bytes(self.handle, int(batch)))

@@ -48,7 +48,8 @@ constexpr int inst_stride(int M) { return (padded<kSH>(M) + 1) & ~1; }
 constexpr int data_need(int M) { return M > kBandCap ? 0 : (kBandCap / M) * inst_stride(M); }
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 constexpr int kBandData =                                 // float2 per CTA
-    cmax(cmax(cmax(data_need(32), data_need(64)), cmax(data_need(128), data_need(256))),
+    cmax(cmax(cmax(cmax(data_need(16), data_need(32)), data_need(64)),
+              cmax(data_need(128), data_need(256))),
          cmax(cmax(data_need(512), data_need(1024)), data_need(2048)));
 static_assert(kBandData >= padded<kSH>(kBandCap), "instance buffers overlap");
 // Build-time tuning switches (defaults are the measured best):
@@ -72,6 +73,7 @@ template <> struct Sched<256, 32>  { static constexpr int R1 = 32, R2 = 8,  R3 =
 template <> struct Sched<512, 32>  { static constexpr int R1 = 32, R2 = 16, R3 = 1; };
 template <> struct Sched<1024, 32> { static constexpr int R1 = 32, R2 = 32, R3 = 1; };
 template <> struct Sched<2048, 32> { static constexpr int R1 = 32, R2 = 32, R3 = 2; };
+template <> struct Sched<16, 16>   { static constexpr int R1 = 16, R2 = 1,  R3 = 1; };
 template <> struct Sched<32, 16>   { static constexpr int R1 = 16, R2 = 2,  R3 = 1; };
 template <> struct Sched<64, 16>   { static constexpr int R1 = 16, R2 = 4,  R3 = 1; };
 template <> struct Sched<128, 16>  { static constexpr int R1 = 16, R2 = 8,  R3 = 1; };
@@ -377,7 +379,7 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     const Inst in = locate<M, EXT>(bp, c);
     const int t = in.t;
     float2* buf = smem + in.il * inst_stride(M);
-    const float2* Xs = X + (long)in.slice * kPlaneStride;
+    const float2* Xs = X + (long)in.slice * bp.stride;
     const int off = in.d.x;
     constexpr bool side = KIND == kSide;   // every instance of the class is of one kind
     // octave classes whose first-stage inputs r = 6..9 are outside every
@@ -634,10 +636,10 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     });
     __syncthreads();   // stage 1 reads done; the exchange reuses the buffer
 
-    float2* Es = E + (long)in.slice * tab.nplanes * kPlaneStride;
+    float2* Es = E + (long)in.slice * tab.nplanes * bp.stride;
     constexpr bool side = KIND == kSide;   // every instance of the class is of one kind
     const int lo = in.d.y, l = d_l(in.d), lg = d_lg(in.d);
-    const int pbase = d_plane(in.d, which) * kPlaneStride + lo;
+    const int pbase = d_plane(in.d, which) * bp.stride + lo;
     // last-stage outputs r of a pruned octave class that lie outside every
     // band's window support (taps [6M/16, 10M/16), checked at upload): for
     // M = 2048 the radix-8 outputs 3 and 4 -- no gain, no index, no store
@@ -731,6 +733,7 @@ bands_fwd_kernel(const float2* __restrict__ X, FwdTab tab, const __grid_constant
     case 128:  run(std::integral_constant<int, 128>{}); break;
     case 64:   run(std::integral_constant<int, 64>{}); break;
     case 32:   run(std::integral_constant<int, 32>{}); break;
+    case 16:   if constexpr (kP <= 16) run(std::integral_constant<int, 16>{}); break;
     default: break;
     }
 }
@@ -764,6 +767,7 @@ bands_inv_kernel(CoefPtr in, InvTab tab, int which, const __grid_constant__ Band
     case 128:  run(std::integral_constant<int, 128>{}); break;
     case 64:   run(std::integral_constant<int, 64>{}); break;
     case 32:   run(std::integral_constant<int, 32>{}); break;
+    case 16:   if constexpr (kP <= 16) run(std::integral_constant<int, 16>{}); break;
     default: break;
     }
 }

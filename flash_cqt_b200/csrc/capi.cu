@@ -35,6 +35,7 @@ struct cqt_tables {
     int group_count[kMaxGroups], group_len[kMaxGroups], group_roll[kMaxGroups];
     SpecTables spec;
     int max_planes;
+    int nslice, half, quarter, stride;   // slice geometry (65536 or 32768 samples)
     void* blob;
 };
 
@@ -73,7 +74,7 @@ int check_device(const cqt_tables* t) {
 // squared-error entry points (16-byte aligned: the planes are)
 constexpr size_t kWsHeader = 256;
 size_t ws_planes(const cqt_tables* t, int batch) {
-    return (size_t)batch * (size_t)t->max_planes * kPlaneStride * sizeof(float2);
+    return (size_t)batch * (size_t)t->max_planes * (size_t)t->stride * sizeof(float2);
 }
 size_t ws_need(const cqt_tables* t, int batch) {
     const size_t partials = ((size_t)spectrum_ctas(batch) * sizeof(float) + 15) & ~(size_t)15;
@@ -141,6 +142,7 @@ BandParams band_params(const cqt_tables* t, int batch) {
     bp.sl = SliceLayout{};
     bp.status = nullptr;
     bp.expire_waits = g_expire_waits.load(std::memory_order_relaxed);
+    bp.stride = t->stride;
     return bp;
 }
 
@@ -244,7 +246,7 @@ SigMap sig_map(const cqt_slices* sl, const cqt_signal* sig, bool input, const fl
 
 extern "C" {
 
-int cqt_version(void) { return 100; }
+int cqt_version(void) { return 101; }
 
 const char* cqt_last_error(void) { return g_err.c_str(); }
 
@@ -274,6 +276,8 @@ int cqt_debug_expire_waits(int on) {
 }
 
 int32_t cqt_ncoef(const cqt_tables* t) { return t ? t->ncoef : -1; }
+
+int32_t cqt_slice_len(const cqt_tables* t) { return t ? t->nslice : -1; }
 
 // ---- overlap-add halo over peer memory (halo.cu)
 struct cqt_halo {
@@ -366,6 +370,11 @@ size_t cqt_workspace_bytes(const cqt_tables* t, int batch) {
 int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     if (!h || !out) return fail(CQT_ERR_ARG, "null argument");
     *out = nullptr;
+    // slice geometry (0: the 65536 of the first version of this structure)
+    const int nslice = h->slice_len ? h->slice_len : kSlice;
+    if (nslice != 65536 && nslice != 32768)
+        return fail(CQT_ERR_ARG, "slice length must be 65536 or 32768 samples");
+    const int kHalf = nslice / 2, kQuarter = nslice / 4, kPlaneStride = kHalf + 8;
     if (h->nclasses < 1 || h->nclasses > kMaxHostClasses)
         return fail(CQT_ERR_ARG, "class count out of range");
     if (h->sy_nplanes < 1 || h->sy_nplanes > kMaxPlanes || h->aa_nplanes < 1 ||
@@ -374,8 +383,8 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     if (h->ncoef <= 0 || h->nbands <= 0) return fail(CQT_ERR_ARG, "empty tables");
     for (int c = 0; c < h->nclasses; ++c) {
         const int M = h->class_len[c];
-        if (M < 32 || M > 2048 || (M & (M - 1)))
-            return fail(CQT_ERR_ARG, "block length must be a power of two in 32..2048");
+        if (M < 16 || M > 2048 || (M & (M - 1)))
+            return fail(CQT_ERR_ARG, "block length must be a power of two in 16..2048");
     }
     // host-side bounds check of every table index, so no kernel can read or
     // write outside its buffers whatever tables it is handed
@@ -638,8 +647,14 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     }
     t->desc = (const int4*)P(i_desc);
     for (int i = 0; i < h->nbands && i < kInlineBands; ++i) t->desc_host[i] = desc[i];
-    t->spec = SpecTables{(const float2*)P(i_hi), (const float2*)P(i_lo), (const float2*)P(i_rows)};
+    t->spec = SpecTables{(const float2*)P(i_hi), (const float2*)P(i_lo), (const float2*)P(i_rows),
+                         nslice};
     t->max_planes = h->sy_nplanes > h->aa_nplanes ? h->sy_nplanes : h->aa_nplanes;
+    t->nslice = nslice;
+    t->half = kHalf;
+    t->quarter = kQuarter;
+    t->stride = kPlaneStride;
+    t->spec.nslice = nslice;
     t->blob = blob;
     *out = t;
     if (prev >= 0) cudaSetDevice(prev);

@@ -114,6 +114,7 @@ struct BandParams {
     // test hook (cqt_debug_expire_waits): the staging barrier expects 16
     // bytes that no copy delivers, so every bounded wait runs out
     int expire_waits;
+    int stride;            // complex values per spectrum row / colour plane
 };
 
 struct CoefPtr {           // coefficient heap addressing
@@ -144,6 +145,7 @@ struct SpecTables {        // packed-spectrum engine twiddles (device)
     const float2* hi;      // W_65536^(256 e), e < 256
     const float2* lo;      // W_65536^e, e < 256
     const float2* rows;    // per-stage twiddle rows (spectrum_twiddle_rows)
+    int nslice;            // samples per slice: 65536 or 32768
 };
 
 // ---------------------------------------------------------------------------

@@ -62,6 +62,9 @@ struct SpecSched {
 // 16384 points per CTA (two CTAs per slice, one CTA per SM)
 using S16k32 = SpecSched<16384, 32, 3, 32, 32, 16, 1>;
 using S16k16 = SpecSched<16384, 16, 4, 16, 16, 16, 4>;
+// 8192 points per CTA: 32768-sample slices
+using S8k32 = SpecSched<8192, 32, 3, 32, 16, 16, 1>;
+using S8k16 = SpecSched<8192, 16, 4, 16, 16, 16, 2>;
 
 template <class C>
 constexpr int sR(int s) { return s == 1 ? C::R1 : s == 2 ? C::R2 : s == 3 ? C::R3 : C::R4; }
@@ -86,16 +89,39 @@ constexpr int smemOf() { return (padded<shiftOf<C>()>(C::N) + 512 + twTotal<C>()
 
 template <class C>
 constexpr bool sched_ok() { return sNS<C>(C::NST) * sR<C>(C::NST) == C::N; }
-static_assert(sched_ok<S16k32>() && sched_ok<S16k16>(),
+static_assert(sched_ok<S16k32>() && sched_ok<S16k16>() && sched_ok<S8k32>() && sched_ok<S8k16>(),
               "stage radices must multiply to the length");
 
 // the twiddle-row blob holds the rows of every schedule, in this order
 template <class C>
-constexpr int rowsOff() { return std::is_same<C, S16k32>::value ? 0 : twTotal<S16k32>(); }
-constexpr int kSpecRowsTotal = twTotal<S16k32>() + twTotal<S16k16>();
+constexpr int rowsOff() {
+    return std::is_same<C, S16k32>::value   ? 0
+           : std::is_same<C, S16k16>::value ? twTotal<S16k32>()
+           : std::is_same<C, S8k32>::value  ? twTotal<S16k32>() + twTotal<S16k16>()
+                                            : twTotal<S16k32>() + twTotal<S16k16>() +
+                                                  twTotal<S8k32>();
+}
+constexpr int kSpecRowsTotal =
+    twTotal<S16k32>() + twTotal<S16k16>() + twTotal<S8k32>() + twTotal<S8k16>();
 
-using CF = std::conditional<FCQT_SPEC_P_FWD == 32, S16k32, S16k16>::type;
-using CI = std::conditional<FCQT_SPEC_P_INV == 32, S16k32, S16k16>::type;
+// the slice geometry: N samples, L = N/2 packed complex points, Q = N/4 per
+// CTA, spectrum rows / colour planes of STRIDE complex values, and W_N^e =
+// W_65536^(e TWM) from the shared two-level W_65536 table
+template <int NS>
+struct Geo {
+    static constexpr int N = NS, L = NS / 2, Q = NS / 4, STRIDE = NS / 2 + 8,
+                         TWM = 65536 / NS;
+    static_assert(NS == 65536 || NS == 32768, "slices of 65536 or 32768 samples");
+};
+// forward / inverse schedule of each geometry
+template <class G>
+using CFg = typename std::conditional<
+    G::N == 65536, std::conditional<FCQT_SPEC_P_FWD == 32, S16k32, S16k16>::type,
+    std::conditional<FCQT_SPEC_P_FWD == 32, S8k32, S8k16>::type>::type;
+template <class G>
+using CIg = typename std::conditional<
+    G::N == 65536, std::conditional<FCQT_SPEC_P_INV == 32, S16k32, S16k16>::type,
+    std::conditional<FCQT_SPEC_P_INV == 32, S8k32, S8k16>::type>::type;
 
 struct Tw64k {
     const float2* hi;
@@ -164,13 +190,14 @@ struct SliceReader {
                            // outside the row; only [jl, jh) is read); else the slice
     int jl, jh;            // readable slice positions [jl, jh) (sliced)
     int shift;             // +-H
+    int nmask;             // slice samples - 1
     const float* window;
     bool sliced;
     bool whole;            // sliced, every position readable, row and window
                            // 8-byte aligned at even positions: float2 loads
     __device__ __forceinline__ float2 operator()(int n) const {
         if (!sliced) return __ldg(reinterpret_cast<const float2*>(at) + n);
-        const int j = (2 * n + shift) & (kSlice - 1);
+        const int j = (2 * n + shift) & nmask;
         float2 v;
         v.x = (j >= jl && j < jh) ? __ldg(at + j) : 0.f;
         v.y = (j + 1 >= jl && j + 1 < jh) ? __ldg(at + j + 1) : 0.f;
@@ -182,7 +209,7 @@ struct SliceReader {
     }
     // the same value when `whole` holds
     __device__ __forceinline__ float2 pair(int n) const {
-        const int j = (2 * n + shift) & (kSlice - 1);
+        const int j = (2 * n + shift) & nmask;
         float2 v = __ldg(reinterpret_cast<const float2*>(at + j));
         if (window) {
             const float2 w = __ldg(reinterpret_cast<const float2*>(window + j));
@@ -207,32 +234,34 @@ __device__ __forceinline__ void sample_range(const SigMap& m, long long& lo, lon
     hi = m.sample0 + m.count < m.length ? m.sample0 + m.count : m.length;
 }
 
+template <class G>
 __device__ __forceinline__ int clamp_slice(long long v) {
-    return v < 0 ? 0 : (v > kSlice ? kSlice : (int)v);
+    return v < 0 ? 0 : (v > G::N ? G::N : (int)v);
 }
 
-template <bool SLICED>
+template <bool SLICED, class G>
 __device__ __forceinline__ SliceReader make_reader(const SigMap& m, long long g) {
     SliceReader r;
     r.sliced = SLICED;
     r.window = m.window;
     r.whole = false;
+    r.nmask = G::N - 1;
     if constexpr (!SLICED) {
-        r.at = m.x + g * kSlice;
+        r.at = m.x + g * G::N;
         r.jl = r.jh = 0;
         r.shift = 0;
     } else {
         const long long row = g / m.S;
         const int sg = m.slice0 + (int)(g % m.S);
         const float* rp = m.x + row * m.ld;
-        const long long p0 = 2LL * kQuarter * (sg - 1);   // global sample of position 0
+        const long long p0 = 2LL * G::Q * (sg - 1);   // global sample of position 0
         long long lo, hi;
         sample_range(m, lo, hi);
-        r.jl = clamp_slice(lo - p0);
-        r.jh = clamp_slice(hi - p0);
+        r.jl = clamp_slice<G>(lo - p0);
+        r.jh = clamp_slice<G>(hi - p0);
         r.at = rp + (p0 - m.sample0);
-        r.shift = (sg & 1) ? -kQuarter : kQuarter;
-        r.whole = r.jl == 0 && r.jh == kSlice && pairs_aligned(rp, m.sample0, r.window);
+        r.shift = (sg & 1) ? -G::Q : G::Q;
+        r.whole = r.jl == 0 && r.jh == G::N && pairs_aligned(rp, m.sample0, r.window);
     }
     return r;
 }
@@ -259,12 +288,12 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, long long bytes,
 // ahead (`ahead` = the number of resident CTAs), overlapping that HBM traffic
 // with its compute; the next wave then loads at L2 speed.  Only addresses
 // inside the readable ranges are touched.
-template <bool SLICED, int T>
+template <bool SLICED, int T, class G>
 __device__ __forceinline__ void prefetch_signal_part(const SigMap& m, long g, int part, int parts,
                                                      int t) {
-    const int len = kSlice / parts;
+    const int len = G::N / parts;
     if constexpr (!SLICED) {
-        const float* base = m.x + g * kSlice + part * len;
+        const float* base = m.x + g * G::N + part * len;
         if ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
             prefetch_l2_bulk(base, (long long)len * 4, t);
         } else {   // 8-byte aligned signal: per-line prefetches
@@ -276,7 +305,7 @@ __device__ __forceinline__ void prefetch_signal_part(const SigMap& m, long g, in
         long long lo, hi;
         lo = m.sample0 > 0 ? m.sample0 : 0;
         hi = m.sample0 + m.count < m.length ? m.sample0 + m.count : m.length;
-        long long a = 2LL * kQuarter * (sg - 1) + (long long)part * len;
+        long long a = 2LL * G::Q * (sg - 1) + (long long)part * len;
         long long b = a + len;
         a = a > lo ? a : lo;
         b = b < hi ? b : hi;
@@ -290,12 +319,13 @@ __device__ __forceinline__ void prefetch_signal_part(const SigMap& m, long g, in
     }
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(CF::T, 1)
+template <int MODE, class G>
+__global__ void __launch_bounds__(CFg<G>::T, 1)
 spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                     const float2* __restrict__ ghi, const float2* __restrict__ glo,
                     const float2* __restrict__ gtw, int ahead) {
-    using C = CF;
+    using C = CFg<G>;
+    constexpr int kSlice = G::N, kHalf = G::L, kQuarter = G::Q, kPlaneStride = G::STRIDE;
     constexpr bool SLICED = MODE == kSigSliced;
     constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
     extern __shared__ float4 smem_raw[];
@@ -312,7 +342,7 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     const Tw64k tw{hl, hl + 256};
 
     // stage 1 inputs straight from global: the radix-2 DIF split of z
-    const SliceReader z = make_reader<SLICED>(in, slice);
+    const SliceReader z = make_reader<SLICED, G>(in, slice);
     float2 v[P];
     auto load = [&](auto&& zf) {
 #pragma unroll
@@ -322,7 +352,7 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                 const int n = t + T * b + r * (kQuarter / C::R1);
                 const float2 a = zf(n);
                 const float2 c = zf(n + kQuarter);
-                v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n));
+                v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n * G::TWM));
             }
     };
     if constexpr (MODE == kSigSqErr) {
@@ -342,11 +372,11 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     spec_compute<C, 1, -1>(v, t, tws);   // consumes the loads
     if (ahead > 0 && blockIdx.x + ahead < gridDim.x) {
         const long nb = blockIdx.x + (long)ahead;
-        prefetch_signal_part<SLICED, T>(in, nb >> 1, (int)(nb & 1), 2, t);
+        prefetch_signal_part<SLICED, T, G>(in, nb >> 1, (int)(nb & 1), 2, t);
         if constexpr (MODE == kSigSqErr) {
             SigMap tm = in;
             tm.x = in.target;
-            prefetch_signal_part<false, T>(tm, nb >> 1, (int)(nb & 1), 2, t);
+            prefetch_signal_part<false, T, G>(tm, nb >> 1, (int)(nb & 1), 2, t);
         }
     }
     spec_stages<C, 2, -1>(v, buf, tws, t, [&](float2 (&w)[P]) {
@@ -367,7 +397,7 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
         const float2 zq = buf[PADI<SH>(kp)];
         const float2 zb = buf[PADI<SH>(kq)];
         const int q = 2 * kp + h;
-        const float2 w = tw(q);
+        const float2 w = tw(q * G::TWM);
         const float2 sq = cadd(zq, cconj(zb));
         const float2 dq = csub(zq, cconj(zb));
         const float2 wd = cmul(w, dq);
@@ -386,13 +416,14 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
 // F[q] from the colour planes flagged in the 4-bit mask mk, fixed plane order.
 // Planes 0 and 1 cover almost every bin, so they are loaded unconditionally
 // (e0, e1, in parallel with the mask) and selected; planes 2 and 3 are rare.
+template <int STRIDE>
 __device__ __forceinline__ float2 plane_pick(const float2* __restrict__ Es, unsigned mk, int q,
                                              float2 e0, float2 e1) {
     float2 acc = make_float2(0.f, 0.f);
     if (mk & 1u) acc = cadd(acc, e0);
     if (mk & 2u) acc = cadd(acc, e1);
-    if (mk & 4u) acc = cadd(acc, Es[2 * kPlaneStride + q]);
-    if (mk & 8u) acc = cadd(acc, Es[3 * kPlaneStride + q]);
+    if (mk & 4u) acc = cadd(acc, Es[2 * STRIDE + q]);
+    if (mk & 8u) acc = cadd(acc, Es[3 * STRIDE + q]);
     return acc;
 }
 
@@ -410,13 +441,14 @@ __device__ __forceinline__ float2 retangle(float2 a, float2 b, float2 wq) {
 // shared memory, so every plane value is loaded once.  After that exchange
 // the CTAs work alone: CTA h stores z[2m + h] into y (swapping halves through
 // distributed shared memory for whole-sector stores measured slower).
-template <int MODE>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CI::T, 1)
+template <int MODE, class G>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CIg<G>::T, 1)
 spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restrict__ qmask,
                     const SigMap out, const float2* __restrict__ ghi,
                     const float2* __restrict__ glo, const float2* __restrict__ gtw,
                     int nplanes, int ahead) {
-    using C = CI;
+    using C = CIg<G>;
+    constexpr int kSlice = G::N, kHalf = G::L, kQuarter = G::Q, kPlaneStride = G::STRIDE;
     constexpr bool SLICED = MODE == kSigSliced;
     constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
     namespace cg = cooperative_groups;
@@ -471,10 +503,10 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
         if (n + T < nhi) nxt = load_quad(n + T);
         const int bA = n, bB = kHalf - n, bC = kQuarter + n, bD = kQuarter - n;
         const unsigned qm = cur.qm;
-        float2 fA = plane_pick(Es, qm & 15u, bA, cur.a0, cur.a1);
-        float2 fB = plane_pick(Es, (qm >> 4) & 15u, bB, cur.b0, cur.b1);
-        const float2 fC = plane_pick(Es, (qm >> 8) & 15u, bC, cur.c0, cur.c1);
-        const float2 fD = plane_pick(Es, qm >> 12, bD, cur.d0, cur.d1);
+        float2 fA = plane_pick<kPlaneStride>(Es, qm & 15u, bA, cur.a0, cur.a1);
+        float2 fB = plane_pick<kPlaneStride>(Es, (qm >> 4) & 15u, bB, cur.b0, cur.b1);
+        const float2 fC = plane_pick<kPlaneStride>(Es, (qm >> 8) & 15u, bC, cur.c0, cur.c1);
+        const float2 fD = plane_pick<kPlaneStride>(Es, qm >> 12, bD, cur.d0, cur.d1);
         if (n == 0) {  // irfft ignores the imaginary parts of DC and Nyquist
             fA.y = 0.f;
             fB.y = 0.f;
@@ -482,8 +514,8 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
         // every twiddle of the quad follows from W^n and W^2n exactly
         // (W = W_65536, W^Q = -i): W^{Q+n} = -i W^n, W^{Q-n} = -i conj(W^n),
         // W^{2Q-n} = -conj(W^n), W^{2Q-2n} = -conj(W^2n)
-        const float2 wn = tw(n);
-        const float2 w2n = tw(2 * n);
+        const float2 wn = tw(n * G::TWM);
+        const float2 w2n = tw(2 * n * G::TWM);
         const float2 z0 = retangle(fA, fB, wn);
         const float2 z1 = retangle(fC, fD, make_float2(wn.y, -wn.x));
         u0[PADI<SH>(n)] = cadd(z0, z1);
@@ -635,6 +667,8 @@ void rows_for(float2* out) {
 void spectrum_twiddle_rows(float2* out) {
     rows_for<S16k32>(out + rowsOff<S16k32>());
     rows_for<S16k16>(out + rowsOff<S16k16>());
+    rows_for<S8k32>(out + rowsOff<S8k32>());
+    rows_for<S8k16>(out + rowsOff<S8k16>());
 }
 
 #ifndef FCQT_SPEC_PREFETCH
@@ -686,51 +720,75 @@ cudaError_t launch_sqerr_finish(const float* partial, int n, float scale, float*
                       partial, n, scale, loss);
 }
 
+namespace {
+template <class G>
+cudaError_t spectrum_fwd_geo(const SigMap& in, float2* X, const SpecTables& st, int batch,
+                             cudaStream_t s) {
+    using C = CFg<G>;
+    const int ahead = wave_ctas();
+    auto go = [&](auto kern) {
+        return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_ctas(batch)), dim3(C::T),
+                          smemOf<C>(), s, in, X, st.hi, st.lo, st.rows, ahead);
+    };
+    if (in.S > 0) return go(spectrum_fwd_kernel<kSigSliced, G>);
+    if (in.target) return go(spectrum_fwd_kernel<kSigSqErr, G>);
+    return go(spectrum_fwd_kernel<kSigPlain, G>);
+}
+
+template <class G>
+cudaError_t spectrum_inv_geo(const float2* E, const InvTab& tab, const SigMap& out,
+                             const SpecTables& st, int batch, cudaStream_t s) {
+    using C = CIg<G>;
+    const int ahead = wave_ctas();
+    auto go = [&](auto kern) {
+        return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_ctas(batch)), dim3(C::T),
+                          smemOf<C>(), s, E, tab.qmask, out, st.hi, st.lo, st.rows,
+                          tab.nplanes, ahead);
+    };
+    if (out.S > 0) return go(spectrum_inv_kernel<kSigSliced, G>);
+    if (out.partial) return go(spectrum_inv_kernel<kSigSqErr, G>);
+    return go(spectrum_inv_kernel<kSigPlain, G>);
+}
+
+template <class G>
+cudaError_t spectrum_attributes_geo() {
+    const void* fwd[] = {(const void*)spectrum_fwd_kernel<kSigPlain, G>,
+                         (const void*)spectrum_fwd_kernel<kSigSliced, G>,
+                         (const void*)spectrum_fwd_kernel<kSigSqErr, G>};
+    const void* inv[] = {(const void*)spectrum_inv_kernel<kSigPlain, G>,
+                         (const void*)spectrum_inv_kernel<kSigSliced, G>,
+                         (const void*)spectrum_inv_kernel<kSigSqErr, G>};
+    for (const void* f : fwd) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smemOf<CFg<G>>());
+        if (e != cudaSuccess) return e;
+    }
+    for (const void* f : inv) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smemOf<CIg<G>>());
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+}  // namespace
+
 cudaError_t launch_spectrum_fwd(const SigMap& in, float2* X, const SpecTables& st, int batch,
                                 cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    const int ahead = wave_ctas();
-    auto go = [&](auto kern) {
-        return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_ctas(batch)), dim3(CF::T),
-                          smemOf<CF>(), s, in, X, st.hi, st.lo, st.rows, ahead);
-    };
-    if (in.S > 0) return go(spectrum_fwd_kernel<kSigSliced>);
-    if (in.target) return go(spectrum_fwd_kernel<kSigSqErr>);
-    return go(spectrum_fwd_kernel<kSigPlain>);
+    return st.nslice == 32768 ? spectrum_fwd_geo<Geo<32768>>(in, X, st, batch, s)
+                              : spectrum_fwd_geo<Geo<65536>>(in, X, st, batch, s);
 }
 
 cudaError_t launch_spectrum_inv(const float2* E, const InvTab& tab, const SigMap& out,
                                 const SpecTables& st, int batch, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
-    const int ahead = wave_ctas();
-    auto go = [&](auto kern) {
-        return launch_pdl(batch <= kPdlMaxBatch, kern, dim3(spectrum_ctas(batch)), dim3(CI::T),
-                          smemOf<CI>(), s, E, tab.qmask, out, st.hi, st.lo, st.rows,
-                          tab.nplanes, ahead);
-    };
-    if (out.S > 0) return go(spectrum_inv_kernel<kSigSliced>);
-    if (out.partial) return go(spectrum_inv_kernel<kSigSqErr>);
-    return go(spectrum_inv_kernel<kSigPlain>);
+    return st.nslice == 32768 ? spectrum_inv_geo<Geo<32768>>(E, tab, out, st, batch, s)
+                              : spectrum_inv_geo<Geo<65536>>(E, tab, out, st, batch, s);
 }
 
 cudaError_t init_spectrum_attributes() {
-    const void* fwd[] = {(const void*)spectrum_fwd_kernel<kSigPlain>,
-                         (const void*)spectrum_fwd_kernel<kSigSliced>,
-                         (const void*)spectrum_fwd_kernel<kSigSqErr>};
-    const void* inv[] = {(const void*)spectrum_inv_kernel<kSigPlain>,
-                         (const void*)spectrum_inv_kernel<kSigSliced>,
-                         (const void*)spectrum_inv_kernel<kSigSqErr>};
-    for (const void* f : fwd) {
-        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             smemOf<CF>());
-        if (e != cudaSuccess) return e;
-    }
-    for (const void* f : inv) {
-        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             smemOf<CI>());
-        if (e != cudaSuccess) return e;
-    }
-    return cudaSuccess;
+    cudaError_t e = spectrum_attributes_geo<Geo<65536>>();
+    return e == cudaSuccess ? spectrum_attributes_geo<Geo<32768>>() : e;
 }
 
 }  // namespace fcqt

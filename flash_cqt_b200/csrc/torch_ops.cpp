@@ -22,7 +22,7 @@
 
 namespace {
 
-constexpr int64_t kN = 65536;
+constexpr int64_t kDefaultN = 65536;
 constexpr int kLayoutPlanar = 0;    // CQT_LAYOUT_PLANAR
 constexpr int kLayoutComplex = 1;   // CQT_LAYOUT_COMPLEX
 constexpr int64_t kWsHeader = 256;  // workspace header (the wait-status word)
@@ -48,6 +48,7 @@ struct Ops : torch::CustomClassHolder {
     const void* tables = nullptr;
     c10::DeviceIndex device = 0;
     int64_t ncoef = 0;
+    int64_t kN = kDefaultN;   // samples per slice (65536 or 32768)
     FnSignalFirst an = nullptr, adj_syn = nullptr;
     FnCoefFirst syn = nullptr, adj_an = nullptr;
     FnWorkspace ws_bytes = nullptr;
@@ -368,6 +369,11 @@ struct Handle {
         return ops->ws;
     }
 
+    void set_slice_len(int64_t n) {
+        TORCH_CHECK_VALUE(n == 65536 || n == 32768, "slice length must be 65536 or 32768");
+        ops->kN = n;
+    }
+
     at::Tensor analysis(const at::Tensor& x) { return ops->analysis(x); }
     void analysis_planar(const at::Tensor& x, const at::Tensor& kr, const at::Tensor& ki) {
         ops->analysis_planar(x, kr, ki);
@@ -391,13 +397,13 @@ struct Handle {
     // TrainableCQT.fwd: x [..., 65536] -> (blocks [..., b, M], side [..., 1, M])
     pybind11::tuple fwd(const at::Tensor& x) {
         Ops& o = *ops;
-        TORCH_CHECK(x.dim() >= 1 && x.size(-1) == kN, "x must be [..., ", kN, "]");
+        TORCH_CHECK(x.dim() >= 1 && x.size(-1) == ops->kN, "x must be [..., ", ops->kN, "]");
         std::vector<int64_t> lead(x.sizes().begin(), x.sizes().end() - 1);
         int64_t B = 1;   // explicit: reshape cannot infer -1 for an empty batch
         for (int64_t d : lead) B *= d;
         // a [B, 65536] input goes in as it is: a no-op reshape would still
         // add a view node to the autograd graph
-        at::Tensor h = AnalysisFn::apply(x.dim() == 2 ? x : x.reshape({B, kN}), ops);
+        at::Tensor h = AnalysisFn::apply(x.dim() == 2 ? x : x.reshape({B, ops->kN}), ops);
         std::vector<at::Tensor> parts = h.split_with_sizes(o.sizes, 1);
         pybind11::list blocks, side;
         o.last_v.clear();
@@ -430,6 +436,27 @@ struct Handle {
         if (!hp) return pybind11::none();
         return pybind11::cast(at::Tensor(std::move(hp)));
     }
+
+    // TrainableCQT.mse_loss in one call when (blocks, side) are the untouched
+    // views of the last fwd: the target [lead..., 65536] is checked and
+    // flattened here; (loss, y [lead..., 65536]) or None (the caller takes the
+    // general path)
+    pybind11::object mse_views(const std::vector<at::Tensor>& all, const at::Tensor& target) {
+        pybind11::object h = last_heap(all);
+        if (h.is_none()) return pybind11::none();
+        at::Tensor heap = h.cast<at::Tensor>();
+        const int64_t B = heap.size(0);
+        std::vector<int64_t> lead(all[0].sizes().begin(), all[0].sizes().end() - 2);
+        std::vector<int64_t> want(lead);
+        want.push_back(ops->kN);
+        TORCH_CHECK_VALUE(target.defined() && target.sizes().vec() == want, "target must be ",
+                          c10::IntArrayRef(want), ", got ",
+                          target.defined() ? target.sizes() : c10::IntArrayRef());
+        torch::autograd::variable_list r =
+            SynthesisMSEFn::apply(heap, target.dim() == 2 ? target : target.reshape({B, ops->kN}), ops);
+        at::Tensor y = lead.size() == 1 ? r[1] : r[1].reshape(want);
+        return pybind11::make_tuple(r[0], y);
+    }
 };
 
 }  // namespace
@@ -441,6 +468,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                             uintptr_t, uintptr_t, uintptr_t, uintptr_t, pybind11::object,
                             std::vector<int64_t>, std::vector<int64_t>, int64_t>())
         .def("workspace", &Handle::workspace)
+        .def("set_slice_len", &Handle::set_slice_len)
         .def("analysis", &Handle::analysis)
         .def("analysis_planar", &Handle::analysis_planar)
         .def("synthesis_planar", &Handle::synthesis_planar)
@@ -450,6 +478,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("analysis_heap", &Handle::analysis_heap)
         .def("synthesis_heap", &Handle::synthesis_heap)
         .def("mse", &Handle::mse)
+        .def("mse_views", &Handle::mse_views)
         .def("fwd", &Handle::fwd)
         .def("last_heap", &Handle::last_heap);
 }

@@ -38,6 +38,7 @@ class Engine:
         self.dev = _cuda_device(device)
         self.heap = heap
         self.ncoef = heap.ncoef
+        self.N = heap.bank.nn   # samples per slice (65536 or 32768)
         self.host_tables = build_tables(heap)
         self.tables = _native.DeviceTables(self.host_tables, self.dev.index)
         assert self.tables.ncoef == self.ncoef
@@ -58,6 +59,7 @@ class Engine:
                     "cqt_synthesis_sqerr", "cqt_adj_synthesis_sqerr")],
                 self.tables, [b for b, _, _ in heap.gspec], [M for _, M, _ in heap.gspec],
                 ngo)
+            self._ops.set_slice_len(self.N)
 
     @classmethod
     def from_params(cls, num_octs, bins_per_oct, fs, audio_len, device=None):
@@ -102,8 +104,8 @@ class Engine:
             raise ValueError(f"{name} must be a tensor on {self.dev}")
         if t.dtype != torch.float32:
             raise TypeError(f"{name} must be float32, got {t.dtype}")
-        if t.dim() != 2 or t.shape[-1] != N:
-            raise ValueError(f"{name} must be [B, {N}], got {tuple(t.shape)}")
+        if t.dim() != 2 or t.shape[-1] != self.N:
+            raise ValueError(f"{name} must be [B, {self.N}], got {tuple(t.shape)}")
         t = t.contiguous()
         # the engines move signals as float2 / float4 vectors
         return t if t.data_ptr() % 16 == 0 else t.clone()
@@ -166,8 +168,8 @@ class Engine:
         c = self._coef(c, "coefficients")
         B = c.shape[0]
         if out is None:
-            out = torch.empty(B, N, dtype=torch.float32, device=self.dev)
-        self._out(out, (B, N), torch.float32, "out")
+            out = torch.empty(B, self.N, dtype=torch.float32, device=self.dev)
+        self._out(out, (B, self.N), torch.float32, "out")
         self._run("cqt_synthesis", c.data_ptr(), None, out.data_ptr(),
                   _native.CQT_LAYOUT_COMPLEX, B)
         return out
@@ -179,8 +181,8 @@ class Engine:
         g = self._coef(g, "coefficient gradient")
         B = g.shape[0]
         if out is None:
-            out = torch.empty(B, N, dtype=torch.float32, device=self.dev)
-        self._out(out, (B, N), torch.float32, "out")
+            out = torch.empty(B, self.N, dtype=torch.float32, device=self.dev)
+        self._out(out, (B, self.N), torch.float32, "out")
         self._run("cqt_adj_analysis", g.data_ptr(), None, out.data_ptr(),
                   _native.CQT_LAYOUT_COMPLEX, B)
         return out
@@ -207,11 +209,11 @@ class Engine:
         B = c.shape[0]
         target = self._signal(target, "target")
         if target.shape[0] != B:
-            raise ValueError(f"target must be [{B}, {N}], got {tuple(target.shape)}")
-        y = torch.empty(B, N, dtype=torch.float32, device=self.dev)
+            raise ValueError(f"target must be [{B}, {self.N}], got {tuple(target.shape)}")
+        y = torch.empty(B, self.N, dtype=torch.float32, device=self.dev)
         loss = torch.empty((), dtype=torch.float32, device=self.dev)
         self._run_sqerr(c.data_ptr(), y.data_ptr(), target.data_ptr(), loss.data_ptr(),
-                        1.0 / (B * N) if B else 0.0, B)
+                        1.0 / (B * self.N) if B else 0.0, B)
         return loss, y, target
 
     def adj_synthesis_sqerr(self, y, target, scale, g):
@@ -260,7 +262,7 @@ class Engine:
             self._ops.synthesis_planar(kr, ki, y)
             return y
         kr, ki = self._planes(kr, ki)
-        self._out(y, (kr.shape[0], N), torch.float32, "y")
+        self._out(y, (kr.shape[0], self.N), torch.float32, "y")
         self._run("cqt_synthesis", kr.data_ptr(), ki.data_ptr(), y.data_ptr(),
                   _native.CQT_LAYOUT_PLANAR, kr.shape[0])
         return y
@@ -294,14 +296,18 @@ class SlicedEngine:
     def __init__(self, eng, window):
         from . import _native
         self.eng = eng
-        self.N = _native
-        if window.numel() != N:
-            raise ValueError("the slice window must have 65536 samples")
+        self._nat = _native
+        if window.numel() != eng.N:
+            raise ValueError(f"the slice window must have {eng.N} samples")
         self.window = window.to(device=eng.dev, dtype=torch.float32).contiguous()
         self.gspec = eng.heap.gspec
 
     def count(self, length):
-        return int(self.N.lib().cqt_sliced_count(int(length)))
+        """slices of a stream of `length` samples (sliced.py:102-104)"""
+        if length <= 0:
+            return 1
+        H = self.eng.N // 4
+        return (-(-int(length) // H) + 1) // 2 + 1
 
     def coef_numel(self, rows, S):
         return rows * S * self.eng.ncoef
@@ -332,10 +338,10 @@ class SlicedEngine:
         self.eng.tables.sliced(name, *args)
 
     def _slices(self, rows, slice0, S, window):
-        return self.N.CqtSlices(rows, slice0, S, window.data_ptr() if window is not None else None)
+        return self._nat.CqtSlices(rows, slice0, S, window.data_ptr() if window is not None else None)
 
     def _signal(self, t, sample0, length):
-        return self.N.CqtSignal(t.data_ptr(), t.stride(0), int(sample0), t.shape[1],
+        return self._nat.CqtSignal(t.data_ptr(), t.stride(0), int(sample0), t.shape[1],
                                 int(length))
 
     def analysis(self, x, S=None, out=None, adjoint_of_synthesis=False, slice0=0,

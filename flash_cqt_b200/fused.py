@@ -19,10 +19,11 @@ HALF = N // 2
 
 
 class FusedOctCQT:
-    """kernel tables and launchers for one OctCQT at audio_len 65536"""
+    """kernel tables and launchers for one OctCQT at audio_len 65536 (or 32768)"""
 
     def __init__(self, cqt, device=None):
-        assert cqt.nn == N, "fused path is built for sl_len 65536"
+        from .tables import SLICE_LENS
+        assert cqt.nn in SLICE_LENS, f"fused path is built for sl_len in {SLICE_LENS}"
         dev = torch.device(device) if device is not None else cqt.device
         self.cqt = cqt
         self.eng = _engine_for(cqt, dev)
@@ -48,7 +49,7 @@ class FusedOctCQT:
     def _workspace(self, B):
         if B not in self._ws:
             z = lambda *s: torch.zeros(*s, dtype=torch.float32, device=self.dev)
-            self._ws[B] = dict(KR=z(B, self.ncoef), KI=z(B, self.ncoef), XO=z(B, N))
+            self._ws[B] = dict(KR=z(B, self.ncoef), KI=z(B, self.ncoef), XO=z(B, self.eng.N))
         return self._ws[B]
 
     def _check_prec(self):

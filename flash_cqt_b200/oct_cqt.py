@@ -1,4 +1,4 @@
-"""``OctCQT``: the invertible oct-mode CQT of one 65536-sample slice.
+"""``OctCQT``: the invertible oct-mode CQT of one 65536- or 32768-sample slice.
 
 Drop-in for ``flash_cqt/oct_cqt.py:18-117``: same constructor, same
 attributes (``bank``, ``nn``, ``oct_bins``, ``size_per_oct``, ``frqs_hz``,
@@ -6,12 +6,11 @@ attributes (``bank``, ``nn``, ``oct_bins``, ``size_per_oct``, ``frqs_hz``,
 but ``fwd`` / ``bwd`` run on the B200 engines (differentiable through the
 transposed engines), not as eager torch ops.  The layout attributes are built
 on the host and live on ``device`` as in the reference; the transform itself
-needs a CUDA device and a 65536-sample slice and raises otherwise (there is no
-CPU path).
+needs a CUDA device and a 65536- or 32768-sample slice and raises otherwise
+(there is no CPU path).
 """
 import torch
 
-from .engine import N
 from .layout import Filterbank, HeapLayout
 
 
@@ -45,9 +44,10 @@ class OctCQT:
 
     def _trainable(self, device):
         from .trainable import TrainableCQT
-        if self.nn != N:
+        from .tables import SLICE_LENS
+        if self.nn not in SLICE_LENS:
             raise NotImplementedError(
-                f"the B200 engines are specialised to {N}-sample slices "
+                f"the B200 engines are built for slices of {SLICE_LENS} samples "
                 f"(this bank has audio_len {self.nn})")
         if self._t is None or self._t.dev != device:
             self._t = TrainableCQT(self, device)

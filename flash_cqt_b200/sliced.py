@@ -110,7 +110,8 @@ class SlicedCQT:
 
     # the fused kernels serve the default engine on a CUDA device
     def _fused(self, device):
-        if self.cqt is not self._fused_cqt or self.sl_len != 65536 or device.type != "cuda":
+        if (self.cqt is not self._fused_cqt or self.sl_len not in (65536, 32768)
+                or device.type != "cuda"):
             return None
         if self._se is None or self._se.eng.dev != device:
             eng = self.cqt._trainable(device).eng

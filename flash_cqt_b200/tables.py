@@ -30,12 +30,19 @@ import math
 import numpy as np
 
 N_SLICE = 65536
+SLICE_LENS = (65536, 32768)   # slice lengths the CUDA engines are built for
 HALF = N_SLICE // 2
 PLANE_STRIDE = HALF + 8   # complex elements per colour plane (64-B multiple)
 MAX_PLANES = 4
+
+
+def plane_stride(n):
+    """complex elements per spectrum row / colour plane for n-sample slices
+    (n / 2 + 8: every row a 64-byte multiple)"""
+    return n // 2 + 8
 FWD_SETS = ("analysis", "adj_synth")
 INV_SETS = ("synth", "adj_an")
-BAND_ORDER = (2048, 1024, 512, 256, 128, 64, 32)   # scheduling classes
+BAND_ORDER = (2048, 1024, 512, 256, 128, 64, 32, 16)   # scheduling classes
 
 
 def _assign_planes(runs, nbins):
@@ -62,10 +69,11 @@ def build_tables(heap):
     """All host tables for one HeapLayout (numpy, float32 / int32)."""
     bank = heap.bank
     N = bank.nn
-    if N != N_SLICE:
-        raise ValueError("the CUDA engines are built for 65536-sample slices, "
-                         "got %d" % N)
+    if N not in SLICE_LENS:
+        raise ValueError("the CUDA engines are built for 65536- and 32768-sample "
+                         "slices, got %d" % N)
     half = N // 2
+    stride = plane_stride(N)
     nc = heap.ncoef
     groups = heap.groups + heap.side_groups
     src_an = np.full(nc, -1, np.int32)
@@ -136,8 +144,8 @@ def build_tables(heap):
             [dest_bins[s][rn] for rn in rr], half + 1)
         dest = np.full(nc, -1, np.int64)
         for rn, p in zip(rr, plane):
-            dest[rn] = p * PLANE_STRIDE + dest_bins[s][rn]
-        maskp = np.zeros(PLANE_STRIDE, np.uint8)
+            dest[rn] = p * stride + dest_bins[s][rn]
+        maskp = np.zeros(stride, np.uint8)
         maskp[:half + 1] = mask
         t["inv"][s] = (dest.astype(np.int32), gre[s].astype(np.float32),
                        gim[s].astype(np.float32), maskp, nplanes)
@@ -156,7 +164,7 @@ def build_tables(heap):
             continue
         rg = bank.ranges[i + 1]                 # octave bands are windows 1..nb
         lg = rg.size
-        g = _octave_geometry(t, o, M, int(rg[0]), lg // 2, lg)
+        g = _octave_geometry(t, o, M, int(rg[0]), lg // 2, lg, stride)
         geom[i] = g if g is not None else (0, 0, 0, 1)
     t["band_geom"] = geom
     # coefficient groups in heap order (octave groups roll in the sliced
@@ -186,10 +194,11 @@ def build_tables(heap):
     e = np.arange(256)
     t["tw_hi"] = _cplx32(np.exp(-2j * math.pi * (256 * e) / 65536))
     t["tw_lo"] = _cplx32(np.exp(-2j * math.pi * e / 65536))
+    t["slice_len"] = N
     return t
 
 
-def _octave_geometry(t, o, M, lo, l, lg):
+def _octave_geometry(t, o, M, lo, l, lg, stride=PLANE_STRIDE):
     """(lo, l, Lg, flags) when tap m of the band at heap offset o maps to bin
     lo + ((m + l) mod M) inside the window support (live iff that index is
     below Lg) in every gather and scatter table, with one colour plane per
@@ -209,8 +218,8 @@ def _octave_geometry(t, o, M, lo, l, lg):
         writes = live & (gr != 0)
         if ((dest >= 0) != writes).any() or (gi[writes] != gr[writes]).any():
             return None
-        planes = np.unique(dest[writes] // PLANE_STRIDE)
-        if planes.size != 1 or (dest[writes] % PLANE_STRIDE != bins[writes]).any():
+        planes = np.unique(dest[writes] // stride)
+        if planes.size != 1 or (dest[writes] % stride != bins[writes]).any():
             return None
         flags |= int(planes[0]) << (4 + 4 * w)
     return (lo, l, lg, flags)

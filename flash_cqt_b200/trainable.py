@@ -91,9 +91,12 @@ class TrainableCQT:
     """
 
     def __init__(self, cqt, device="cuda"):
-        if cqt.nn != N:
-            raise ValueError(f"the CUDA engines are built for {N}-sample slices")
+        from .tables import SLICE_LENS
+        if cqt.nn not in SLICE_LENS:
+            raise ValueError(f"the CUDA engines are built for slices of {SLICE_LENS} samples, "
+                             f"got {cqt.nn}")
         self.cqt = cqt
+        self.N = cqt.nn
         self.eng = _engine_for(cqt, device)
         self.dev = self.eng.dev
         self.gspec = cqt.heap.gspec
@@ -119,7 +122,7 @@ class TrainableCQT:
         B = 1
         for d in lead:   # explicit: reshape cannot infer -1 for an empty batch
             B *= d
-        h = _Analysis.apply(x.reshape(B, N).contiguous(), self.eng)
+        h = _Analysis.apply(x.reshape(B, self.N).contiguous(), self.eng)
         return self.split(h, lead)
 
     def heap_of(self, blocks, side=None):
@@ -162,9 +165,9 @@ class TrainableCQT:
                 h = self.heap_of(blocks, side)
             y = ops.synthesis_heap(h)
             # a one-dimensional lead is the heap's batch already: no view node
-            return y if len(lead) == 1 else y.reshape(*lead, N)
+            return y if len(lead) == 1 else y.reshape(*lead, self.N)
         h = self.heap_of(blocks, side)
-        return _Synthesis.apply(h, self.eng).reshape(*lead, N)
+        return _Synthesis.apply(h, self.eng).reshape(*lead, self.N)
 
     def mse_loss(self, blocks, side, target, return_output=False):
         """``((self.bwd(blocks, side) - target) ** 2).mean()`` -- the loss of the
@@ -174,25 +177,31 @@ class TrainableCQT:
         synthesis' load (no elementwise kernels in between).  target
         [..., 65536] float32 like the output; returns the 0-dim loss, or
         (loss, y) with ``return_output`` (y carries no gradient)."""
+        ops = self.eng._ops
+        if ops is not None and side is not None:
+            # the views of the last fwd: one call into C++ (ValueError on a bad target)
+            r = ops.mse_views(blocks + side if type(blocks) is list and type(side) is list
+                              else list(blocks) + list(side), target)
+            if r is not None:
+                return r if return_output else r[0]
         lead = blocks[0].shape[:-2]
         B = 1
         for d in lead:
             B *= d
-        if tuple(target.shape) != (*lead, N):
-            raise ValueError(f"target must be {(*lead, N)}, got {tuple(target.shape)}")
-        ops = self.eng._ops
+        if tuple(target.shape) != (*lead, self.N):
+            raise ValueError(f"target must be {(*lead, self.N)}, got {tuple(target.shape)}")
         h = None
         if ops is not None and side is not None:
             h = ops.last_heap(list(blocks) + list(side))
         if h is None:
             h = self.heap_of(blocks, side)
-        t2 = target if target.dim() == 2 else target.reshape(B, N)
+        t2 = target if target.dim() == 2 else target.reshape(B, self.N)
         if ops is not None:
             loss, y = ops.mse(h, t2)
         else:
             loss, y = _SynthesisMSE.apply(h, t2, self.eng)
         if return_output:
-            return loss, (y if len(lead) == 1 else y.reshape(*lead, N))
+            return loss, (y if len(lead) == 1 else y.reshape(*lead, self.N))
         return loss
 
     # flat-heap entry points (no per-group views), used by the fused sliced path

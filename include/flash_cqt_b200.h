@@ -23,8 +23,9 @@
  *   - Every pointer except the host tables of cqt_tables_upload is a device
  *     pointer on the device the tables were uploaded to; that device must be
  *     current when an entry point is called.
- *   - x, y, gx, gy: float32 [batch][65536], 8-byte aligned (CQT_ERR_ARG
- *     otherwise; rows at 16-byte alignment take the vector store path).
+ *   - x, y, gx, gy: float32 [batch][slice_len] (65536, or 32768 for tables
+ *     built for 32768-sample slices), 8-byte aligned (CQT_ERR_ARG otherwise;
+ *     rows at 16-byte alignment take the vector store path).
  *   - coefficients: the heap of one slice is ncoef complex values (octave
  *     groups lowest first, then the DC and the Nyquist side block, each group
  *     [bins][M] row-major).  layout CQT_LAYOUT_PLANAR: c_re and c_im are two
@@ -63,7 +64,7 @@ extern "C" {
 #define CQT_LAYOUT_PLANAR 0
 #define CQT_LAYOUT_COMPLEX 1
 
-#define CQT_SLICE 65536
+#define CQT_SLICE 65536   /* default slice length; 32768 is the other one built */
 
 /* Host-side tables, built once per filterbank (the Python side builds them in
  * float64 and rounds once).  Per-tap arrays have ncoef entries in heap order. */
@@ -103,6 +104,10 @@ typedef struct cqt_host_tables {
     const float* tw2048;        /* [2048][2] W_2048^e */
     const float* tw_hi;         /* [256][2]  W_65536^(256 e) */
     const float* tw_lo;         /* [256][2]  W_65536^e */
+    /* samples per slice: 65536 or 32768 (0 means 65536).  The bins of the
+     * per-tap tables run to slice_len / 2, and plane slots and masks use the
+     * stride slice_len / 2 + 8 (32776 or 16392). */
+    int32_t slice_len;
 } cqt_host_tables;
 
 typedef struct cqt_tables cqt_tables; /* device-resident tables (opaque) */
@@ -111,6 +116,7 @@ typedef struct cqt_tables cqt_tables; /* device-resident tables (opaque) */
 int cqt_tables_upload(const cqt_host_tables* host, int device, cqt_tables** out);
 int cqt_tables_free(cqt_tables* t);
 int32_t cqt_ncoef(const cqt_tables* t);
+int32_t cqt_slice_len(const cqt_tables* t);   /* 65536 or 32768 */
 
 /* Scratch bytes needed by any entry point at this batch size. */
 size_t cqt_workspace_bytes(const cqt_tables* t, int batch);
@@ -226,6 +232,9 @@ typedef struct cqt_slices {
                                 and its transpose only */
 } cqt_slices;
 
+/* slices of a stream of `length` samples at 65536-sample slices; for
+ * 32768-sample slices the same formula with a hop of 16384:
+ * (ceil(length / (slice_len / 4)) + 1) / 2 + 1 */
 int cqt_sliced_count(int64_t length);
 int cqt_sliced_analysis(const cqt_tables* t, const cqt_signal* x, const cqt_slices* sl,
                         float* coef, void* workspace, size_t workspace_bytes, void* stream);

@@ -59,3 +59,34 @@ def gc_seed(ncoef):
 
 def gy_seed():
     return normal(12, (2, N))
+
+
+# 32768-sample slices of the default bank, as in tests/golden/make_golden.py --short
+GOLDEN_32K = pathlib.Path(__file__).resolve().parent / "golden" / "reference_fixtures_32k.npz"
+N_SHORT = 32768
+STRIDE_SHORT = 29
+
+
+@functools.lru_cache(maxsize=1)
+def ref_short():
+    with np.load(GOLDEN_32K) as f:
+        return {k: f[k] for k in f.files}
+
+
+@functools.lru_cache(maxsize=1)
+def oracle_short():
+    from oracle.cqt_oracle import OctCQTOracle
+    return OctCQTOracle((3, 4, 2), (8, 16, 32), 44100, N_SHORT)
+
+
+def x_short():
+    return normal(31, (2, N_SHORT))
+
+
+def gc_short(ncoef):
+    g = normal(32, (2, 2, ncoef))
+    return (g[0] + 1j * g[1]).astype(np.complex64)
+
+
+def gy_short():
+    return normal(33, (2, N_SHORT))

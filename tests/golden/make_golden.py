@@ -4,6 +4,7 @@ Run once, in a container where the reference checkout is mounted read-only::
 
     python tests/golden/make_golden.py /path/to/Flash-CQT          # default bank
     python tests/golden/make_golden.py /path/to/Flash-CQT --alt    # other banks
+    python tests/golden/make_golden.py /path/to/Flash-CQT --short  # 32768-sample slices
 
 It imports the reference package (``flash_cqt``) and runs its own public API
 (``OctCQT.fwd/bwd``, torch autograd through them, ``SlicedCQT.fwd/bwd``) on
@@ -183,10 +184,73 @@ def main_alt(ref_root):
     np.savez_compressed(HERE / "reference_fixtures_alt.npz", **out)
 
 
+# 32768-sample slices of the default bank (band lengths 16..1024)
+N_SHORT = 32768
+STRIDE_SHORT = 29
+
+
+def main_short(ref_root):
+    """reference_fixtures_32k.npz: the default bank at audio_len / sl_len
+    32768 -- layout checksums, strided coefficients and round trip of two
+    N(0,1) slices, the gradients of both transforms through torch autograd,
+    and the sliced transform of a short chirp"""
+    sys.path.insert(0, str(ref_root))
+    import torch
+    from flash_cqt import OctCQT, SlicedCQT
+
+    torch.set_num_threads(8)
+    N = N_SHORT
+    cqt = OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=N)
+    groups = list(cqt.groups) + list(cqt.side_groups)
+    out = {}
+    lay = []
+    for idx, gv, pos, gdv, conj in groups:
+        b, M = idx.shape
+        w = torch.arange(1, b * M + 1, dtype=torch.int64)
+        lay.append([b, M, int(idx.reshape(-1).sum()), int((idx.reshape(-1) * w).sum()),
+                    int(pos.reshape(-1).sum()), int(conj.sum()), int((gv != 0).sum())])
+    out["layout"] = np.array(lay, dtype=np.int64)
+    x = normal(31, (2, N))
+    xt = torch.from_numpy(x)
+    blocks, side = cqt.fwd(xt)
+    h = torch.cat([c.reshape(2, -1) for c in list(blocks) + list(side)], -1)
+    y = cqt.bwd(blocks, side)
+    out["coef_s"] = h.reshape(-1)[::STRIDE_SHORT].numpy()
+    out["y_s"] = y.reshape(-1)[::STRIDE_SHORT].numpy()
+    gcr = normal(32, (2, 2, h.shape[1]))
+    gc = (gcr[0] + 1j * gcr[1]).astype(np.complex64)
+    xg = xt.clone().requires_grad_(True)
+    bl, sd = cqt.fwd(xg)
+    hh = torch.cat([c.reshape(2, -1) for c in list(bl) + list(sd)], -1)
+    (torch.view_as_real(hh) * torch.view_as_real(torch.from_numpy(gc))).sum().backward()
+    out["gx_an_s"] = xg.grad.reshape(-1)[::STRIDE_SHORT].numpy()
+    gy = normal(33, (2, N))
+    leaves = [c.detach().clone().requires_grad_(True) for c in list(blocks) + list(side)]
+    ng = len(cqt.groups)
+    (cqt.bwd(leaves[:ng], leaves[ng:]) * torch.from_numpy(gy)).sum().backward()
+    gk = torch.cat([lv.grad.reshape(2, -1) for lv in leaves], -1)
+    out["gk_syn_s"] = gk.reshape(-1)[::STRIDE_SHORT].numpy()
+    sl = SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=N)
+    L = 100000
+    xc = chirp(35, L)[None, None]
+    sb, sside = sl.fwd(torch.from_numpy(xc))
+    sy = sl.bwd(sb, sside, length=L)
+    out["sliced_S"] = int(sl._num_slices(L))
+    out["sliced_blocks_s"] = np.concatenate([c.reshape(-1)[::STRIDE_SLICED].numpy()
+                                             for c in sb])
+    out["sliced_y_s"] = sy.reshape(-1)[::STRIDE_SLICED].numpy()
+    np.savez_compressed(HERE / "reference_fixtures_32k.npz", **out)
+    print("bands", sum(g[0].shape[0] for g in groups), "ncoef", h.shape[1],
+          "sliced S", out["sliced_S"])
+
+
 if __name__ == "__main__":
-    if len(sys.argv) not in (2, 3) or (len(sys.argv) == 3 and sys.argv[2] != "--alt"):
-        raise SystemExit("usage: make_golden.py <reference checkout> [--alt]")
-    if len(sys.argv) == 3:
+    if len(sys.argv) not in (2, 3) or (len(sys.argv) == 3
+                                       and sys.argv[2] not in ("--alt", "--short")):
+        raise SystemExit("usage: make_golden.py <reference checkout> [--alt | --short]")
+    if len(sys.argv) == 3 and sys.argv[2] == "--alt":
         main_alt(pathlib.Path(sys.argv[1]))
+    elif len(sys.argv) == 3:
+        main_short(pathlib.Path(sys.argv[1]))
     else:
         main(pathlib.Path(sys.argv[1]))

@@ -29,7 +29,7 @@ def test_library_exports_header_symbols():
     for n in names:
         assert hasattr(L, n), n
     assert set(names) == set(_native.exported_symbols())
-    assert L.cqt_version() == 100
+    assert L.cqt_version() == 101
 
 
 def test_bad_arguments_rejected_without_gpu():

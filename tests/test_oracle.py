@@ -124,3 +124,38 @@ def test_other_filterbanks_match_reference(i):
     assert snr_db(r[f"alt{i}_coef_s"], h.reshape(-1)[::STRIDE_ALT]) >= 120
     y = o.bwd(o.fwd(x))
     assert snr_db(r[f"alt{i}_y_s"], y.reshape(-1)[::STRIDE_ALT]) >= 125
+
+
+def test_oracle_pinned_at_32768_sample_slices():
+    """the oracle at audio_len / sl_len 32768 against the reference's own
+    outputs (tests/golden/make_golden.py --short): layout exact, coefficients,
+    round trip, both gradients and the sliced transform"""
+    from fixtures import (N_SHORT, STRIDE_SHORT, gc_short, gy_short, oracle_short,
+                          ref_short, x_short, STRIDE_SLICED, chirp)
+    from oracle.cqt_oracle import SlicedOracle
+    o, r = oracle_short(), ref_short()
+    lay = []
+    for idx, gv, pos, gdv, conj in o.all_groups:
+        b, M = idx.shape
+        w = np.arange(1, b * M + 1, dtype=np.int64)
+        lay.append([b, M, int(idx.reshape(-1).sum()), int((idx.reshape(-1) * w).sum()),
+                    int(pos.reshape(-1).sum()), int(conj.sum()), int((gv != 0).sum())])
+    np.testing.assert_array_equal(np.array(lay, dtype=np.int64), r["layout"])
+    x = x_short().astype(np.float64)
+    h = o.heap(o.fwd(x))
+    assert snr_db(r["coef_s"], h.reshape(-1)[::STRIDE_SHORT]) >= 120
+    y = o.bwd(o.fwd(x))
+    assert snr_db(r["y_s"], y.reshape(-1)[::STRIDE_SHORT]) >= 125
+    gx = o.adj_fwd(o.unheap(gc_short(o.ncoef).astype(np.complex128)))
+    assert snr_db(r["gx_an_s"], gx.reshape(-1)[::STRIDE_SHORT]) >= 120
+    gk = o.heap(o.adj_bwd(gy_short().astype(np.float64)))
+    assert snr_db(r["gk_syn_s"], gk.reshape(-1)[::STRIDE_SHORT]) >= 120
+    so = SlicedOracle(sl_len=N_SHORT)
+    L = 100000
+    xc = chirp(35, L)[None].astype(np.float64)
+    assert so.num_slices(L) == int(r["sliced_S"])
+    bl, sd = so.fwd(xc)
+    bs = np.concatenate([c.reshape(-1)[::STRIDE_SLICED] for c in bl])
+    assert snr_db(r["sliced_blocks_s"], bs) >= 120
+    ys = so.bwd(bl, sd, length=L)
+    assert snr_db(r["sliced_y_s"], ys.reshape(-1)[::STRIDE_SLICED]) >= 125
