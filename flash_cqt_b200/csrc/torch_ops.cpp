@@ -310,6 +310,7 @@ struct SynthesisMSEFn : public torch::autograd::Function<SynthesisMSEFn> {
         ctx->saved_data["y"] = r[1];
         ctx->saved_data["t"] = r[2];
         ctx->mark_non_differentiable({r[1]});
+        ctx->set_materialize_grads(false);   // no zero gradient is built for y
         return {r[0], r[1]};
     }
     static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,

@@ -58,10 +58,13 @@ class _SynthesisMSE(torch.autograd.Function):
         loss, y, t = eng.synthesis_sqerr(c, target)
         ctx.y, ctx.t = y, t
         ctx.mark_non_differentiable(y)
+        ctx.set_materialize_grads(False)   # no zero gradient is built for y
         return loss, y
 
     @staticmethod
     def backward(ctx, gl, _gy):
+        if gl is None:
+            return None, None, None
         y, t = ctx.y, ctx.t
         scale = 2.0 / y.numel() if y.numel() else 0.0
         gl = gl.to(device=y.device, dtype=torch.float32).contiguous()
