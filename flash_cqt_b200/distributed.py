@@ -102,32 +102,36 @@ class PeerHalo:
     over NVLink (plain peer stores, CUDA IPC mapping, no multicast) and raise
     a flag; rank r - 1 waits (bounded, 10 s), adds it into its last owned hop
     and acknowledges.  Stream-ordered, no host synchronisation; an expired
-    wait is counted on the device and raised by ``check`` (or by the next
-    ``exchange`` once the count has reached the host)."""
+    wait is counted on the device and raised by ``check``.
+
+    Set up in two local steps -- ``PeerHalo(...)`` allocates and exports the
+    receive buffer (``handle``), ``connect`` maps the neighbours' buffers --
+    so that the ranks can exchange handles and agree on success between
+    them (``PartitionedSlicedCQT`` does)."""
 
     HANDLE = 64
 
-    def __init__(self, rows, hop, device, rank, world, has_left, has_right, group=None,
-                 wait_ms=10000):
+    def __init__(self, rows, hop, device, wait_ms=10000):
         import ctypes
         from . import _native
         self._n = _native
         self._c = ctypes
-        L = _native.lib()
         self.rows, self.hop, self.device = rows, hop, device
         self.h = ctypes.c_void_p()
         handle = (ctypes.c_ubyte * self.HANDLE)()
-        _native._check(L.cqt_halo_create(device.index, rows, hop, int(wait_ms),
-                                         ctypes.byref(self.h), handle), "cqt_halo_create")
-        mine = bytes(handle)
-        handles = [None] * world
-        dist.all_gather_object(handles, mine, group=group)
-        left = handles[rank - 1] if has_left else None
-        right = handles[rank + 1] if has_right else None
-        buf = lambda b: (ctypes.c_ubyte * self.HANDLE).from_buffer_copy(b) if b else None
-        _native._check(L.cqt_halo_connect(self.h, buf(left), buf(right)), "cqt_halo_connect")
+        _native._check(_native.lib().cqt_halo_create(device.index, rows, hop, int(wait_ms),
+                                                     ctypes.byref(self.h), handle),
+                       "cqt_halo_create")
+        self.handle = bytes(handle)
         self.epoch = 0
-        self._pending = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    def connect(self, left=None, right=None):
+        """map the receive buffers of the left / right neighbour (their
+        ``handle`` bytes, None for no neighbour on that side)"""
+        buf = lambda b: ((self._c.c_ubyte * self.HANDLE).from_buffer_copy(b)
+                         if b is not None else None)
+        self._n._check(self._n.lib().cqt_halo_connect(self.h, buf(left), buf(right)),
+                       "cqt_halo_connect")
 
     def exchange(self, local, send, recv):
         """local [rows, window] float32 on the device: send local[:, :hop]
@@ -237,20 +241,31 @@ class PartitionedSlicedCQT:
 
     def _peer_halo(self, rows, p, device):
         """one exchange per (rows, left, right) shape; created collectively on
-        first use (every rank takes the same bwd calls in the same order)"""
+        first use (every rank takes the same bwd calls in the same order, and
+        every rank makes the same collectives here whatever fails locally)"""
         key = (rows, p.rank > 0 and p.nslices > 0, p.right_nslices > 0)
         if key not in self._peer:
-            err = None
+            h, err = None, None
             try:
-                h = PeerHalo(rows, p.hop, device, p.rank, p.world, has_left=key[1],
-                             has_right=key[2], group=self.group, wait_ms=self.halo_wait_ms)
-            except RuntimeError as e:   # e.g. no peer access between these devices
-                h, err = None, str(e)
-            # every rank must take the same transport: agree before first use
-            errs = [None] * p.world
-            dist.all_gather_object(errs, err, group=self.group)
-            bad = [e for e in errs if e]
+                h = PeerHalo(rows, p.hop, device, wait_ms=self.halo_wait_ms)
+            except RuntimeError as e:   # e.g. no memory for the receive buffer
+                err = str(e)
+            got = [None] * p.world
+            dist.all_gather_object(got, (h.handle if h is not None else None, err),
+                                   group=self.group)
+            bad = [e for _, e in got if e]
+            if not bad:
+                try:
+                    h.connect(left=got[p.rank - 1][0] if key[1] else None,
+                              right=got[p.rank + 1][0] if key[2] else None)
+                except RuntimeError as e:   # e.g. no peer access between these devices
+                    err = str(e)
+                errs = [None] * p.world
+                dist.all_gather_object(errs, err, group=self.group)
+                bad = [e for e in errs if e]
+            # every rank takes the same transport
             if bad:
+                del h
                 if self.halo == "peer":
                     raise RuntimeError(f"peer-memory halo unavailable: {bad[0]}")
                 self.halo = "collective"   # auto: torch.distributed on every rank

@@ -11,8 +11,6 @@ from . import _native
 from .layout import Filterbank, HeapLayout
 from .tables import build_tables
 
-N = 65536
-
 
 def _cuda_device(device):
     dev = torch.device(device) if device is not None else torch.device("cuda")
@@ -149,7 +147,7 @@ class Engine:
 
     # ----------------------------------------------------------------- complex
     def analysis(self, x, out=None):
-        """x [B, 65536] float32 -> coefficient heap complex64 [B, ncoef]."""
+        """x [B, N] float32 (N samples per slice) -> coefficient heap complex64 [B, ncoef]."""
         if out is None and self._ops is not None:
             return self._ops.analysis(x)
         x = self._signal(x, "x")
@@ -162,7 +160,7 @@ class Engine:
         return out
 
     def synthesis(self, c, out=None):
-        """coefficient heap complex64 [B, ncoef] -> y [B, 65536] float32."""
+        """coefficient heap complex64 [B, ncoef] -> y [B, N] float32."""
         if out is None and self._ops is not None:
             return self._ops.synthesis(c)
         c = self._coef(c, "coefficients")
@@ -175,7 +173,7 @@ class Engine:
         return out
 
     def adj_analysis(self, g, out=None):
-        """transpose of analysis: complex64 grads [B, ncoef] -> [B, 65536]."""
+        """transpose of analysis: complex64 grads [B, ncoef] -> [B, N]."""
         if out is None and self._ops is not None:
             return self._ops.adj_analysis(g)
         g = self._coef(g, "coefficient gradient")
@@ -188,7 +186,7 @@ class Engine:
         return out
 
     def adj_synthesis(self, gy, out=None):
-        """transpose of synthesis: [B, 65536] -> complex64 grads [B, ncoef]."""
+        """transpose of synthesis: [B, N] -> complex64 grads [B, ncoef]."""
         if out is None and self._ops is not None:
             return self._ops.adj_synthesis(gy)
         gy = self._signal(gy, "signal gradient")
@@ -202,7 +200,7 @@ class Engine:
 
     # -------------------------------------------------------- squared error
     def synthesis_sqerr(self, c, target):
-        """coefficient heap [B, ncoef] and target [B, 65536] -> (loss, y):
+        """coefficient heap [B, ncoef] and target [B, N] -> (loss, y):
         y = synthesis(c), loss = mean((y - target)^2) as a 0-dim float32
         tensor, summed in a fixed order inside the engines."""
         c = self._coef(c, "coefficients")
@@ -217,19 +215,29 @@ class Engine:
         return loss, y, target
 
     def adj_synthesis_sqerr(self, y, target, scale, g):
-        """transpose of the synthesis applied to scale * g * (y - target), g a
-        device float32 scalar tensor (e.g. dL/dloss)"""
+        """transpose of the synthesis applied to scale * g * (y - target), y and
+        target [B, N] float32, g a device float32 scalar tensor (e.g. dL/dloss)"""
+        y = self._signal(y, "y")
+        target = self._signal(target, "target")
         B = y.shape[0]
-        out = torch.empty(B, self.ncoef, dtype=torch.complex64, device=self.dev)
+        if target.shape[0] != B:
+            raise ValueError(f"target must be [{B}, {self.N}], got {tuple(target.shape)}")
+        if (not torch.is_tensor(g) or g.device != self.dev or g.dtype != torch.float32
+                or g.numel() != 1):
+            raise ValueError(f"g must be a float32 scalar tensor on {self.dev}")
+        g = g.contiguous()
         if torch.cuda.current_device() != self.dev.index:
             with torch.cuda.device(self.dev):
                 return self.adj_synthesis_sqerr(y, target, scale, g)
+        out = torch.empty(B, self.ncoef, dtype=torch.complex64, device=self.dev)
         ws = self.workspace(B)
         rc = _native.lib().cqt_adj_synthesis_sqerr(
             self.tables.handle, y.data_ptr(), target.data_ptr(), float(scale), g.data_ptr(),
             out.data_ptr(), None, _native.CQT_LAYOUT_COMPLEX, B, ws.data_ptr(), ws.numel(),
             _raw_stream_of(self.dev.index))
         _native._check(rc, "cqt_adj_synthesis_sqerr")
+        if _native.check_waits_enabled():
+            self._check_waits("cqt_adj_synthesis_sqerr")
         return out
 
     def _run_sqerr(self, c, y, target, loss, scale, B):
@@ -241,10 +249,12 @@ class Engine:
             self.tables.handle, c, None, _native.CQT_LAYOUT_COMPLEX, y, target, loss,
             float(scale), B, ws.data_ptr(), ws.numel(), _raw_stream_of(self.dev.index))
         _native._check(rc, "cqt_synthesis_sqerr")
+        if _native.check_waits_enabled():
+            self._check_waits("cqt_synthesis_sqerr")
 
     # ------------------------------------------------------------------ planar
     def analysis_planar(self, x, kr, ki):
-        """x [B, 65536] -> the planes kr, ki [B, ncoef] (written in place)"""
+        """x [B, N] -> the planes kr, ki [B, ncoef] (written in place)"""
         if self._ops is not None:
             self._ops.analysis_planar(x, kr, ki)
             return kr, ki
@@ -257,7 +267,7 @@ class Engine:
         return kr, ki
 
     def synthesis_planar(self, kr, ki, y):
-        """planes kr, ki [B, ncoef] -> y [B, 65536] (written in place)"""
+        """planes kr, ki [B, ncoef] -> y [B, N] (written in place)"""
         if self._ops is not None:
             self._ops.synthesis_planar(kr, ki, y)
             return y

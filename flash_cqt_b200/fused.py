@@ -12,10 +12,7 @@ as an attribute for compatibility and only "ieee" (fp32) exists.
 """
 import torch
 
-from .engine import N
 from .trainable import _engine_for
-
-HALF = N // 2
 
 
 class FusedOctCQT:
@@ -57,7 +54,7 @@ class FusedOctCQT:
             raise NotImplementedError("only fp32 ('ieee') kernels exist in this build")
 
     def fwd(self, x):
-        """x [B, 65536] -> (KR, KI) planar [B, ncoef] workspace tensors"""
+        """x [B, N] (N = audio_len) -> (KR, KI) planar [B, ncoef] workspace tensors"""
         self._check_prec()
         B = x.shape[0]
         w = self._workspace(B)
@@ -65,7 +62,7 @@ class FusedOctCQT:
         return w["KR"], w["KI"]
 
     def bwd(self, KR, KI):
-        """(KR, KI) planar -> XO [B, 65536] workspace tensor"""
+        """(KR, KI) planar -> XO [B, N] workspace tensor"""
         self._check_prec()
         B = KR.shape[0]
         w = self._workspace(B)

@@ -27,6 +27,7 @@ import torch
 from .engine import SlicedEngine
 from .layout import periodic_hann
 from .oct_cqt import OctCQT
+from .tables import SLICE_LENS
 
 
 class _SlicedAnalysis(torch.autograd.Function):
@@ -110,7 +111,7 @@ class SlicedCQT:
 
     # the fused kernels serve the default engine on a CUDA device
     def _fused(self, device):
-        if (self.cqt is not self._fused_cqt or self.sl_len not in (65536, 32768)
+        if (self.cqt is not self._fused_cqt or self.sl_len not in SLICE_LENS
                 or device.type != "cuda"):
             return None
         if self._se is None or self._se.eng.dev != device:

@@ -22,7 +22,7 @@ import weakref
 
 import torch
 
-from .engine import N, Engine
+from .engine import Engine
 
 
 class _Analysis(torch.autograd.Function):
@@ -117,7 +117,7 @@ class TrainableCQT:
         return vs[:self.ngroups], vs[self.ngroups:]
 
     def fwd(self, x):
-        """x [..., 65536] real -> (blocks, side), complex64, gradients flow."""
+        """x [..., N] real (N = audio_len) -> (blocks, side), complex64, gradients flow."""
         ops = self.eng._ops
         if ops is not None:   # the same, from C++ (autograd nodes included)
             return ops.fwd(x)
@@ -178,7 +178,7 @@ class TrainableCQT:
         the engines: the synthesis sums the squared error as it stores y, and
         the backward forms 2 (y - target) / n inside the transposed
         synthesis' load (no elementwise kernels in between).  target
-        [..., 65536] float32 like the output; returns the 0-dim loss, or
+        [..., N] float32 like the output; returns the 0-dim loss, or
         (loss, y) with ``return_output`` (y carries no gradient)."""
         ops = self.eng._ops
         if ops is not None and side is not None:
