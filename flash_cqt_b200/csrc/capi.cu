@@ -286,8 +286,10 @@ struct cqt_halo {
 
 int cqt_halo_create(int device, int rows, int64_t hop, int wait_ms, cqt_halo** out,
                     void* handle) {
-    if (!out || !handle || rows < 1 || hop < 1 || wait_ms < 0)
-        return fail(CQT_ERR_ARG, "bad halo arguments (rows, hop >= 1, wait_ms >= 0, out, handle)");
+    // one CTA row per signal row: rows <= 65535 (the grid's y extent)
+    if (!out || !handle || rows < 1 || rows > 65535 || hop < 1 || wait_ms < 0)
+        return fail(CQT_ERR_ARG,
+                    "bad halo arguments (1 <= rows <= 65535, hop >= 1, wait_ms >= 0, out, handle)");
     *out = nullptr;
     int prev = -1;
     cudaGetDevice(&prev);

@@ -274,7 +274,8 @@ int cqt_wait_timeouts(unsigned int* count);
  * skipped); nothing hangs.  No multicast or switch reduction is used. */
 #define CQT_HALO_HANDLE_BYTES 64
 typedef struct cqt_halo cqt_halo;
-/* wait_ms: the bound of every wait on a neighbour (0: 10 s) */
+/* rows: 1..65535 signal rows; wait_ms: the bound of every wait on a
+ * neighbour (0: 10 s) */
 int cqt_halo_create(int device, int rows, int64_t hop, int wait_ms, cqt_halo** out,
                     void* handle);
 int cqt_halo_connect(cqt_halo* h, const void* left_handle, const void* right_handle);
