@@ -5,7 +5,9 @@ bookkeeping and ``exchange_halo`` on per-rank overlap-add buffers built from
 the oracle's per-slice synthesis; the owned output ranges, gathered, must equal
 the oracle's whole-buffer inverse.  This is the host-side logic of the
 multi-GPU sliced path; on GPUs the same functions run on the fused kernels'
-outputs over NCCL.
+outputs over NCCL.  Failures are made on the host: a rank that leaves without
+sending, and a stand-in for the peer-memory set-up that fails on one rank
+(every rank must then take the same transport).
 """
 import os
 import socket
@@ -143,3 +145,71 @@ def test_dropped_halo_times_out():
     assert got[1] == "dropped"
     assert got[0] not in ("no error",), got
     assert all(p.exitcode is not None for p in procs)
+
+
+def _agreement_worker(rank, world, port, q, fail_rank, fail_at, mode):
+    """PartitionedSlicedCQT's peer-memory halo set-up with a stand-in for the
+    CUDA IPC exchange: one rank's create or connect fails, and every rank must
+    take the same transport (or all raise), with no collective left unmatched"""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        import flash_cqt_b200.distributed as D
+
+        class FakeHalo:
+            def __init__(self, rows, hop, device, wait_ms=10000):
+                if rank == fail_rank and fail_at == "create":
+                    raise RuntimeError("no memory for the receive buffer")
+                self.handle = bytes([rank]) * 64
+                self.left = self.right = None
+
+            def connect(self, left=None, right=None):
+                if rank == fail_rank and fail_at == "connect":
+                    raise RuntimeError("no peer access")
+                self.left, self.right = left, right
+
+        D.PeerHalo = FakeHalo
+        part = D.PartitionedSlicedCQT(None, rank, world, halo=mode)
+        p = D.Partition(6 * 32768, 6, rank, world)
+        try:
+            h = part._peer_halo(2, p, torch.device("cpu"))
+            res = ("none" if h is None else "peer", part.halo,
+                   None if h is None else (h.left, h.right))
+        except RuntimeError:
+            res = ("raised", part.halo, None)
+        dist.barrier()   # every rank is still in step after the set-up
+        q.put((rank,) + res)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_rank,fail_at,mode", [
+    (None, None, "auto"), (1, "create", "auto"), (2, "connect", "auto"),
+    (0, "connect", "peer")])
+def test_peer_halo_setup_agrees(fail_rank, fail_at, mode):
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_agreement_worker,
+                         args=(r, world, port, q, fail_rank, fail_at, mode))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    outcomes = {g[1] for g in got}
+    if fail_rank is None:
+        assert outcomes == {"peer"} and all(g[2] == "auto" for g in got)
+        for r, _, _, (left, right) in got:   # the neighbours' handles, where they exist
+            assert left == (bytes([r - 1]) * 64 if r > 0 else None)
+            assert right == (bytes([r + 1]) * 64 if r < world - 1 else None)
+    elif mode == "auto":
+        assert outcomes == {"none"} and all(g[2] == "collective" for g in got)
+    else:
+        assert outcomes == {"raised"}
