@@ -119,3 +119,24 @@ def test_noalloc_rejects_batches_above_its_scratch(eng):
     rc, msg = _noalloc(eng, x, out)
     assert rc == -1
     assert "at most 8 slices" in msg
+
+
+def test_noalloc_32768_sample_slices():
+    """the same scratch serves the 8192-point spectrum rows of 32768-sample
+    slices (shorter rows, the same static array)"""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from flash_cqt_b200.engine import Engine
+    e32 = Engine.from_params([3, 4, 2], [8, 16, 32], 44100, 32768, torch.device("cuda:0"))
+    g = torch.Generator(device="cpu").manual_seed(32)
+    for batch in (8, 5):
+        x = torch.randn(batch, 32768, generator=g).to(e32.dev)
+        want = e32.analysis(x)
+        got = torch.full_like(want, float("nan"))
+        rc, msg = _noalloc(e32, x, got)
+        assert rc == 0, msg
+        torch.cuda.synchronize()
+        w, h = want.cpu().numpy(), got.cpu().numpy()
+        assert np.isfinite(h).all()
+        for b in range(batch):
+            assert snr_db(w[b], h[b]) >= COEF_DB, b
