@@ -2,7 +2,7 @@
 """Benchmark: 65536-sample CQT round trips/s on 1..8 B200 (+ train step ms).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
-    python bench.py --impl reference ...      # CPU reference-port arm
+    python bench.py --impl reference ...      # the reference's own CPU path
 
 One step = one analysis + synthesis round trip of B slices per GPU (default
 1024, inputs larger than L2) through the sm_100a engines, replayed as one CUDA
@@ -229,6 +229,70 @@ def cpu_baseline(seconds):
     return {"value": B * calls / el, "unit": "round_trips/s", "cores": cores, "kind": kind,
             "sample": "%d calls of a %d-slice round trip (%.0f s), %s, %.1f dB"
                       % (calls, B, el, what, -10 * math.log10(err))}
+
+
+def cpu_configs():
+    """configs 1, 3 and 5 through the reference's own CPU code (the package
+    built from its sources in oracle/_ref), on all host cores: medians after
+    warm-ups, with the GPU rows' seeds (config 5's noise comes from the CPU
+    generator, the GPU row's from the CUDA one).  None when the reference is
+    not built here."""
+    import statistics
+    import torch
+    from oracle import ref_loader
+    from oracle.cpu_port import cpu_model
+    if not ref_loader.available():
+        return None
+    fc = ref_loader.package()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+
+    def median_ms(fn, warm, reps):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return 1e3 * statistics.median(ts)
+
+    def snr(a, b):
+        a, b = a.double(), b.double()
+        return float(10 * torch.log10((a ** 2).sum() / ((b - a) ** 2).sum()))
+
+    out = {"kind": "reference", "cores": threads, "cpu": cpu_model(),
+           "what": "the reference's unmodified OctCQT / SlicedCQT (oracle/build_ref.py)"}
+    cqt = fc.OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=N)
+    # config 1: 4 slices of N(0, 1), seed 0, fwd -> bwd
+    x1 = torch.randn(4, N, generator=torch.Generator().manual_seed(0))
+    with torch.no_grad():
+        ms1 = median_ms(lambda: cqt.bwd(*cqt.fwd(x1)), 2, 10)
+        y1 = cqt.bwd(*cqt.fwd(x1))
+    out["config1_b4_round_trip"] = {"ms": ms1, "snr_db": snr(x1, y1), "runs": "median of 10"}
+    # config 3: B = 16 train step through torch autograd on OctCQT
+    x3 = torch.randn(16, N, generator=torch.Generator().manual_seed(2))
+    t3 = torch.randn(16, N, generator=torch.Generator().manual_seed(3))
+
+    def step():
+        xg = x3.detach().requires_grad_(True)
+        ((cqt.bwd(*cqt.fwd(xg)) - t3) ** 2).mean().backward()
+    out["config3_train_step_b16"] = {"ms": median_ms(step, 2, 10), "runs": "median of 10"}
+    # config 5: SlicedCQT fwd + bwd on 8 x 60 s of chirp + noise
+    sl = fc.SlicedCQT([3, 4, 2], [8, 16, 32], fs=44100, sl_len=N, device="cpu")
+    tt = torch.arange(SLICED_LEN, dtype=torch.float64) / 44100.0
+    k = math.log(18000.0 / 40.0) / 60.0
+    phase = 2 * math.pi * 40.0 * (torch.exp(k * tt) - 1.0) / k
+    x5 = (torch.sin(phase).float().expand(SLICED_SIGNALS, SLICED_LEN)
+          + 0.05 * torch.randn(SLICED_SIGNALS, SLICED_LEN,
+                               generator=torch.Generator().manual_seed(5)))
+    x5 = x5.reshape(SLICED_SIGNALS, 1, SLICED_LEN).contiguous()
+    with torch.no_grad():
+        ms5 = median_ms(lambda: sl.bwd(*sl.fwd(x5), length=SLICED_LEN), 1, 3)
+        y5 = sl.bwd(*sl.fwd(x5), length=SLICED_LEN)
+    out["config5_sliced_stream"] = {"ms": ms5, "snr_db": snr(x5, y5), "runs": "median of 3",
+                                    "signals": SLICED_SIGNALS, "samples": SLICED_LEN}
+    return out
 
 
 def reference_gpu(dev, batches=(1, 64, 256, 1024), reps=20):
@@ -518,6 +582,9 @@ def main():
         line.update(extras(args, eng, t, dev, world, rank, barrier, W, K, hbm))
         if world == 1 and rank == 0:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+            cfg = cpu_configs()
+            if cfg is not None:
+                line["cpu_baseline"]["configs"] = cfg
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
