@@ -1,13 +1,14 @@
 """Build the reference's own code for the checker and bench.py's reference
 arms -- TEST / BENCH INFRASTRUCTURE, never part of the product path.
 
-    python oracle/build_ref.py [--ref DIR]      (default: the reference checkout
-                                                  named by FLASH_CQT_REFERENCE)
+    python oracle/build_ref.py [--ref DIR]      (default: the checkout named by
+                                                  FLASH_CQT_REFERENCE, else the
+                                                  ``reference_path`` of BASELINE.json)
 
 Everything is built from the sources where they lie in the read-only reference
 checkout; every output goes under ``oracle/_ref/`` (git-ignored, so it stays
-out of history, and not gpurun-ignored, so it travels to the GPU box like the
-product's own built libraries).  No reference source file is copied:
+out of history, and not excluded from the snapshot that runs on the GPU box,
+so it travels there like the product's own built libraries).  No reference source file is copied:
 
 * ``flash_cqt/*.py`` (the pure-torch ``OctCQT`` / ``FusedOctCQT`` /
   ``TrainableCQT`` package, ``oct_cqt.py:18-117``, ``trainable.py:28-191``)
@@ -33,7 +34,22 @@ import sys
 
 HERE = pathlib.Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-DEFAULT_REF = os.environ.get("FLASH_CQT_REFERENCE", "/root/reference")
+
+
+def _default_ref():
+    """the reference checkout: FLASH_CQT_REFERENCE, else the ``reference_path``
+    recorded in the repository's BASELINE.json (None when neither names one)"""
+    env = os.environ.get("FLASH_CQT_REFERENCE")
+    if env:
+        return env
+    try:
+        import json
+        return json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path")
+    except (OSError, ValueError):
+        return None
+
+
+DEFAULT_REF = _default_ref()
 PY_MODULES = ["__init__", "ref_util", "filterbank", "oct_cqt", "sliced", "graphed",
               "fused", "trainable"]
 # name the reference's loaders give each extension (fused.py:63-132)
@@ -82,8 +98,8 @@ def main(argv=None):
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--force", action="store_true", help="rebuild the CUDA extensions")
     a = ap.parse_args(argv)
-    ref = pathlib.Path(a.ref)
-    if not (ref / "flash_cqt" / "oct_cqt.py").exists():
+    ref = pathlib.Path(a.ref) if a.ref else None
+    if ref is None or not (ref / "flash_cqt" / "oct_cqt.py").exists():
         print(f"no reference checkout at {ref}; nothing to build", file=sys.stderr)
         return 0
     print(build_python(ref))
