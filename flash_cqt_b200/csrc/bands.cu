@@ -92,6 +92,34 @@ struct TwLayout {
     static_assert(n2 + n3 <= kBandTw, "twiddle rows exceed their shared slot");
 };
 
+// Build-time switch FCQT_TW_TMA (1): every twiddle a band CTA reads in its
+// stages -- the stage-2 rows and the last stage's base powers W^k, W^2k, W^4k
+// -- sits in a per-length slot of a table in the device blob, laid out as
+// the CTA's shared slot, and arrives with one TMA bulk copy on the staging
+// barrier (0: the CTA's threads gather the stage-2 rows from W_2048 and the
+// last stage reads its powers from global memory per butterfly).  Both give
+// the same values: the slots are copied from the same W_2048 table.
+#ifndef FCQT_TW_TMA
+#define FCQT_TW_TMA 1
+#endif
+static_assert(!(FCQT_TW_TMA && FCQT_TW3_SMEM), "one place for the last-stage twiddles");
+
+template <int M>
+struct TwSlot {
+    using L = TwLayout<M>;
+    static constexpr int NS3 = L::R1 * L::R2;   // span of the last stage
+    static constexpr int npow = L::R3 >= 8 ? 3 : L::R3 >= 4 ? 2 : L::R3 >= 2 ? 1 : 0;
+    static constexpr int count = L::n2 + npow * NS3;   // float2
+    static constexpr unsigned bytes = count * 8u;
+    static_assert(count <= kBandTw && bytes % 16u == 0, "twiddle slot too small or unaligned");
+};
+// slot of block length M (16, 32, ..., 2048) in the table
+constexpr int tw_slot_index(int M) {
+    return M <= 16 ? 0 : M == 32 ? 1 : M == 64 ? 2 : M == 128 ? 3 : M == 256 ? 4
+           : M == 512 ? 5 : M == 1024 ? 6 : 7;
+}
+constexpr int kTwSlots = 8;
+
 template <int M>
 __device__ __forceinline__ void fill_twiddles(float2* tws, const float2* __restrict__ w2048) {
     using L = TwLayout<M>;
@@ -205,6 +233,37 @@ __device__ __forceinline__ void stage_compute_pow(float2 (&v)[P], int t, const T
     });
 }
 
+// the same, with W^k, W^2k, W^4k (k < NS) read from shared rows at
+// rows[k], rows[NS + k], rows[2 NS + k]
+template <int M, int T, int R, int NS, int S, int P>
+__device__ __forceinline__ void stage_compute_pow_rows(float2 (&v)[P], int t,
+                                                       const float2* rows) {
+    static_assert(R == 2 || R == 4 || R == 8, "power twiddles for radix 2, 4, 8");
+    static_for<0, P / R>([&](auto Bb) {
+        constexpr int b = decltype(Bb)::value;
+        const int k = (t + T * b) % NS;
+        float2 w[R];
+        w[1] = rows[k];
+        if constexpr (R >= 4) {
+            w[2] = rows[NS + k];
+            w[3] = cmul(w[1], w[2]);
+        }
+        if constexpr (R == 8) {
+            w[4] = rows[2 * NS + k];
+            w[5] = cmul(w[1], w[4]);
+            w[6] = cmul(w[2], w[4]);
+            w[7] = cmul(w[3], w[4]);
+        }
+#pragma unroll
+        for (int r = 1; r < R; ++r) {
+            float2 x = w[r];
+            if constexpr (S > 0) x.y = -x.y;
+            v[b * R + r] = cmul(v[b * R + r], x);
+        }
+        dft<R, S, b * R, 1>(v);
+    });
+}
+
 // stages 2 and 3 after stage 1's DFT; the last stage's outputs (index
 // n = j + r M / R_last, j = t + T b) go to `emit`
 struct Tw2048 {
@@ -236,6 +295,8 @@ __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const fl
             __syncthreads();
             if constexpr (FCQT_TW3_SMEM) {
                 stage_compute_rows<M, T, R3, R1 * R2, S>(v, t, tws + L::n2);
+            } else if constexpr (FCQT_TW_TMA) {
+                stage_compute_pow_rows<M, T, R3, R1 * R2, S>(v, t, tws + L::n2);
             } else if constexpr (FCQT_TW3_POW) {
                 stage_compute_pow<M, T, R3, R1 * R2, S, 2048>(v, t, Tw2048{bp_tw});
             } else {
@@ -413,10 +474,13 @@ __device__ void band_fwd(const float2* __restrict__ X, const FwdTab& tab, const 
     pdl_wait();   // the previous kernel of the stream has completed
     if (t == 0) {
         const int a = lo - sh, bytes = n > 0 ? (((lo + n + 1) & ~1) - a) * 8 : 0;
-        mbar_arrive_expect(mbar, (unsigned)bytes + (bp.expire_waits ? 16u : 0u));
+        // the CTA's first thread also brings the twiddle slot
+        const unsigned twb = (FCQT_TW_TMA && threadIdx.x == 0) ? TwSlot<M>::bytes : 0u;
+        mbar_arrive_expect(mbar, (unsigned)bytes + twb + (bp.expire_waits ? 16u : 0u));
         if (bytes) bulk_load(buf, Xs + a, (unsigned)bytes, mbar);
+        if (twb) bulk_load(tws, bp.twrows + tw_slot_index(M) * kBandTw, twb, mbar);
     }
-    fill_twiddles<M>(tws, bp.tw2048);
+    if constexpr (!FCQT_TW_TMA) fill_twiddles<M>(tws, bp.tw2048);
     // stage 1 taps: element r of butterfly b is tap t + T b + r M / R1.
     // Octave bands read segment entry (m + l) mod M inside the window
     // support; side bands go through the per-tap gather table (conjugated
@@ -578,7 +642,10 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
     __syncthreads();
     pdl_wait();   // the previous kernel of the stream has completed
     if (t == 0) {
-        mbar_arrive_expect(mbar, (bulk ? M * 8 : 0) + (bp.expire_waits ? 16u : 0u));
+        // the CTA's first thread also brings the twiddle slot
+        const unsigned twb = (FCQT_TW_TMA && threadIdx.x == 0) ? TwSlot<M>::bytes : 0u;
+        mbar_arrive_expect(mbar, (bulk ? M * 8 : 0) + twb + (bp.expire_waits ? 16u : 0u));
+        if (twb) bulk_load(tws, bp.twrows + tw_slot_index(M) * kBandTw, twb, mbar);
         if (bulk) {
             // smem [0, M - r) <- src [r, M), smem [M - r, M) <- src [0, r)
             const int r = SLICED ? (ca.roll & (M - 1)) : 0;
@@ -608,7 +675,7 @@ __device__ void band_inv(CoefPtr in_c, const InvTab& tab, int which, const BandP
             }
         }
     }
-    fill_twiddles<M>(tws, bp.tw2048);
+    if constexpr (!FCQT_TW_TMA) fill_twiddles<M>(tws, bp.tw2048);
     cp_async_wait_all();
     mbar_wait(mbar, 0, bp.status);
     __syncthreads();
@@ -819,6 +886,39 @@ cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const Ban
     if (bp.sl.S > 0)
         return bp.ext ? go(bands_inv_kernel<true, true>) : go(bands_inv_kernel<true, false>);
     return bp.ext ? go(bands_inv_kernel<false, true>) : go(bands_inv_kernel<false, false>);
+}
+
+namespace {
+// one block length's slot: stage-2 rows W_{R1 R2}^{r k} (r = 1..R2-1, k < R1)
+// as fill_twiddles gathers them, then the last stage's W^k, W^2k, W^4k
+// (k < R1 R2) as stage_compute_pow reads them -- entries of W_2048 (host)
+template <int M>
+void slot_rows(float2* out, const float2* w2048) {
+    using L = TwLayout<M>;
+    using Sl = TwSlot<M>;
+    for (int e = 0; e < L::n2; ++e) {
+        const int r = e / L::R1 + 1, k = e % L::R1;
+        out[e] = w2048[(r * k * (2048 / (L::R1 * L::R2))) & 2047];
+    }
+    const int scale3 = L::R3 > 1 ? 2048 / (Sl::NS3 * L::R3) : 0;
+    for (int pi = 0; pi < Sl::npow; ++pi)
+        for (int k = 0; k < Sl::NS3; ++k)
+            out[L::n2 + pi * Sl::NS3 + k] = w2048[(((1 << pi) * k) * scale3) & 2047];
+}
+}  // namespace
+
+int band_twiddle_count() { return kTwSlots * kBandTw; }
+
+void band_twiddle_rows(float2* out, const float2* w2048) {
+    for (int i = 0; i < kTwSlots * kBandTw; ++i) out[i] = make_float2(0.f, 0.f);
+    if constexpr (kP <= 16) slot_rows<16>(out + tw_slot_index(16) * kBandTw, w2048);
+    slot_rows<32>(out + tw_slot_index(32) * kBandTw, w2048);
+    slot_rows<64>(out + tw_slot_index(64) * kBandTw, w2048);
+    slot_rows<128>(out + tw_slot_index(128) * kBandTw, w2048);
+    slot_rows<256>(out + tw_slot_index(256) * kBandTw, w2048);
+    slot_rows<512>(out + tw_slot_index(512) * kBandTw, w2048);
+    slot_rows<1024>(out + tw_slot_index(1024) * kBandTw, w2048);
+    slot_rows<2048>(out + tw_slot_index(2048) * kBandTw, w2048);
 }
 
 cudaError_t read_wait_timeouts(unsigned* count) {

@@ -29,6 +29,7 @@ struct cqt_tables {
     FwdTab fwd[2];   // 0 analysis, 1 transpose of synthesis
     InvTab inv[2];   // 0 synthesis, 1 transpose of analysis
     const float2* tw2048;
+    const float2* twrows;   // band twiddle slots
     const int4* desc;       // device copy in the blob, class order, see BandParams
     int4 desc_host[kInlineBands];   // the inline head of the same array
     int ngroups;
@@ -134,6 +135,7 @@ BandParams band_params(const cqt_tables* t, int batch) {
     BandParams bp{};
     bp.sc = make_sched(t->ncls, t->cls_M, t->cls_nb, t->cls_first, t->cls_kind, batch);
     bp.tw2048 = t->tw2048;
+    bp.twrows = t->twrows;
     bp.ncoef = t->ncoef;
     bp.desc = t->desc;
     bp.ext = t->nbands > kInlineBands;
@@ -597,6 +599,9 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
     std::vector<float2> rows(spectrum_twiddle_count());
     spectrum_twiddle_rows(rows.data());
     size_t i_rows = add(rows.data(), rows.size() * sizeof(float2));
+    std::vector<float2> twrows(band_twiddle_count());
+    band_twiddle_rows(twrows.data(), reinterpret_cast<const float2*>(h->tw2048));
+    size_t i_twr = add(twrows.data(), twrows.size() * sizeof(float2));
 
     void* blob = nullptr;
     e = cudaMalloc(&blob, total);
@@ -641,6 +646,7 @@ int cqt_tables_upload(const cqt_host_tables* h, int device, cqt_tables** out) {
                        (const unsigned char*)P(i_aam), (const unsigned short*)P(i_qaa),
                        h->aa_nplanes};
     t->tw2048 = (const float2*)P(i_tw);
+    t->twrows = (const float2*)P(i_twr);
     t->ngroups = h->ngroups;
     for (int g = 0; g < h->ngroups; ++g) {
         t->group_count[g] = h->group_count[g];

@@ -95,6 +95,7 @@ enum SigMode { kSigPlain = 0, kSigSliced = 1, kSigSqErr = 2 };
 struct BandParams {
     BandSched sc;
     const float2* tw2048;  // W_2048^e, forward sign
+    const float2* twrows;  // per-block-length twiddle slots (band_twiddle_rows)
     int ncoef;
     // per band in class order: {heap offset, lo (octave) | band id (side),
     // l | Lg << 16, flags: bit 0 side band, bits 4-7 synthesis plane, bits
@@ -226,5 +227,9 @@ cudaError_t launch_bands_fwd(const float2* X, const FwdTab& tab, const BandParam
                              CoefPtr out, cudaStream_t s);
 cudaError_t launch_bands_inv(CoefPtr in, const InvTab& tab, int which, const BandParams& bp,
                              float2* E, cudaStream_t s);
+// the band kernels' twiddle slots, one per block length 16..2048, built on
+// the host from the W_2048 table (float2 count, then the rows)
+int band_twiddle_count();
+void band_twiddle_rows(float2* out, const float2* w2048);
 
 }  // namespace fcqt
