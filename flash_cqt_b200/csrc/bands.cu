@@ -35,7 +35,7 @@ namespace fcqt {
 namespace {
 
 #ifndef FCQT_PREFETCH_GAINS
-#define FCQT_PREFETCH_GAINS 1
+#define FCQT_PREFETCH_GAINS 0
 #endif
 
 constexpr int kP = kBandP;
@@ -56,7 +56,9 @@ static_assert(kBandData >= padded<kSH>(kBandCap), "instance buffers overlap");
 //   FCQT_TW3_SMEM   stage-3 twiddles as shared rows (1) or from the global
 //                   W_2048 table (0: less shared memory per CTA, faster);
 //   FCQT_TW3_POW    stage-3 twiddles W^k, W^2k, W^4k and their products (1);
-//   FCQT_PREFETCH_GAINS  bands_inv loads its scatter gains before the stages (1).
+//   FCQT_PREFETCH_GAINS  bands_inv loads its scatter gains before the stages
+//                   (1), or in the scatter (0: with the twiddles in shared
+//                   slots, 5 % faster -- the early loads cost registers).
 #ifndef FCQT_TW3_SMEM
 #define FCQT_TW3_SMEM 0
 #endif
