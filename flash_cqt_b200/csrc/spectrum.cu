@@ -129,15 +129,33 @@ struct Tw64k {
     __device__ __forceinline__ float2 operator()(int e) const { return tw64k(hi, lo, e); }
 };
 
-template <class C>
-__device__ __forceinline__ void load_tables(float2* sm_hilo, float2* sm_tw, const float2* ghi,
-                                            const float2* glo, const float2* gtw) {
+// the two-level W_65536 tables and the stage rows of schedule C, staged by
+// asynchronous copies (16 bytes each, no register round trip): issued at
+// kernel start, so that they arrive while the CTA's first global loads are in
+// flight; each thread waits for its own copies (cp_async_wait_all), and a CTA
+// barrier then publishes everyone's
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+template <class C, int NT = C::T>
+__device__ __forceinline__ void load_tables_async(float2* sm_hilo, float2* sm_tw,
+                                                  const float2* ghi, const float2* glo,
+                                                  const float2* gtw) {
+    static_assert(rowsOff<C>() % 2 == 0 && twTotal<C>() % 2 == 0, "16-byte copies");
     gtw += rowsOff<C>();
-    for (int i = threadIdx.x; i < 512 + twTotal<C>(); i += C::T) {
-        if (i < 256) sm_hilo[i] = __ldg(ghi + i);
-        else if (i < 512) sm_hilo[i] = __ldg(glo + i - 256);
-        else sm_tw[i - 512] = __ldg(gtw + i - 512);
+    constexpr int kChunks = (512 + twTotal<C>()) / 2;
+    for (int i = threadIdx.x; i < kChunks; i += NT) {
+        const int e = 2 * i;
+        const float2* src = e < 256 ? ghi + e : e < 512 ? glo + (e - 256) : gtw + (e - 512);
+        float2* dst = e < 512 ? sm_hilo + e : sm_tw + (e - 512);
+        cp_async16(dst, src);
     }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 
 // twiddle and DFT of stage s (all butterflies of the thread)
@@ -336,12 +354,12 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
     pdl_launch_dependents();
-    load_tables<C>(hl, tws, ghi, glo, gtw);
-    __syncthreads();
+    load_tables_async<C>(hl, tws, ghi, glo, gtw);
     pdl_wait();   // the previous kernel of the stream has completed
     const Tw64k tw{hl, hl + 256};
 
-    // stage 1 inputs straight from global: the radix-2 DIF split of z
+    // stage 1 inputs straight from global: the radix-2 DIF split of z (the
+    // odd half's twiddles once the tables have landed)
     const SliceReader z = make_reader<SLICED, G>(in, slice);
     float2 v[P];
     auto load = [&](auto&& zf) {
@@ -352,8 +370,19 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                 const int n = t + T * b + r * (kQuarter / C::R1);
                 const float2 a = zf(n);
                 const float2 c = zf(n + kQuarter);
-                v[b * C::R1 + r] = h == 0 ? cadd(a, c) : cmul(csub(a, c), tw(2 * n * G::TWM));
+                v[b * C::R1 + r] = h == 0 ? cadd(a, c) : csub(a, c);
             }
+        cp_async_wait_all();
+        __syncthreads();
+        if (h) {
+#pragma unroll
+            for (int b = 0; b < P / C::R1; ++b)
+#pragma unroll
+                for (int r = 0; r < C::R1; ++r) {
+                    const int n = t + T * b + r * (kQuarter / C::R1);
+                    v[b * C::R1 + r] = cmul(v[b * C::R1 + r], tw(2 * n * G::TWM));
+                }
+        }
     };
     if constexpr (MODE == kSigSqErr) {
         // the MSE gradient s (y - target) formed on load (s = 2 dL/dloss / n)
@@ -462,8 +491,8 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     const long slice = blockIdx.x >> 1;
     const int t = threadIdx.x;
     pdl_launch_dependents();
-    load_tables<C>(hl, tws, ghi, glo, gtw);
-    cl.sync();   // tables staged, and the partner is running (its buffer may be written)
+    load_tables_async<C>(hl, tws, ghi, glo, gtw);
+    cl.sync();   // the partner is running (its buffer may be written)
     pdl_wait();  // the previous kernel of the stream has completed
     const Tw64k tw{hl, hl + 256};
     const float2* Es = E + slice * (long)(nplanes * kPlaneStride);
@@ -498,6 +527,8 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
     int n = nlo + t;
     QuadIn cur;
     if (n < nhi) cur = load_quad(n);
+    cp_async_wait_all();   // the tables have landed (own copies; the barrier: all)
+    __syncthreads();
     for (; n < nhi; n += T) {
         QuadIn nxt;
         if (n + T < nhi) nxt = load_quad(n + T);
