@@ -343,7 +343,7 @@ spectrum_fwd_kernel(const SigMap in, float2* __restrict__ X,
                     const float2* __restrict__ ghi, const float2* __restrict__ glo,
                     const float2* __restrict__ gtw, int ahead) {
     using C = CFg<G>;
-    constexpr int kSlice = G::N, kHalf = G::L, kQuarter = G::Q, kPlaneStride = G::STRIDE;
+    constexpr int kHalf = G::L, kQuarter = G::Q, kPlaneStride = G::STRIDE;
     constexpr bool SLICED = MODE == kSigSliced;
     constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
     extern __shared__ float4 smem_raw[];
@@ -478,7 +478,6 @@ spectrum_inv_kernel(const float2* __restrict__ E, const unsigned short* __restri
                     int nplanes, int ahead) {
     using C = CIg<G>;
     constexpr int kSlice = G::N, kHalf = G::L, kQuarter = G::Q, kPlaneStride = G::STRIDE;
-    constexpr bool SLICED = MODE == kSigSliced;
     constexpr int P = C::P, T = C::T, SH = shiftOf<C>();
     namespace cg = cooperative_groups;
     extern __shared__ float4 smem_raw[];
