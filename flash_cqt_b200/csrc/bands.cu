@@ -102,7 +102,9 @@ struct TwLayout {
 // last stage reads its powers from global memory per butterfly).  Both give
 // the same values: the slots are copied from the same W_2048 table.
 #ifndef FCQT_TW_TMA
-#define FCQT_TW_TMA 1
+// the 32-point-per-thread build's M = 2048 schedule (32 x 32 x 2) needs 2016
+// twiddle entries, more than the slot holds: it gathers them as before
+#define FCQT_TW_TMA (FCQT_BAND_P <= 16)
 #endif
 static_assert(!(FCQT_TW_TMA && FCQT_TW3_SMEM), "one place for the last-stage twiddles");
 
@@ -113,7 +115,8 @@ struct TwSlot {
     static constexpr int npow = L::R3 >= 8 ? 3 : L::R3 >= 4 ? 2 : L::R3 >= 2 ? 1 : 0;
     static constexpr int count = L::n2 + npow * NS3;   // float2
     static constexpr unsigned bytes = count * 8u;
-    static_assert(count <= kBandTw && bytes % 16u == 0, "twiddle slot too small or unaligned");
+    static_assert(!FCQT_TW_TMA || (count <= kBandTw && bytes % 16u == 0),
+                  "twiddle slot too small or unaligned");
 };
 // slot of block length M (16, 32, ..., 2048) in the table
 constexpr int tw_slot_index(int M) {
@@ -913,6 +916,7 @@ int band_twiddle_count() { return kTwSlots * kBandTw; }
 
 void band_twiddle_rows(float2* out, const float2* w2048) {
     for (int i = 0; i < kTwSlots * kBandTw; ++i) out[i] = make_float2(0.f, 0.f);
+    if constexpr (!FCQT_TW_TMA) return;   // the kernels gather their twiddles
     if constexpr (kP <= 16) slot_rows<16>(out + tw_slot_index(16) * kBandTw, w2048);
     slot_rows<32>(out + tw_slot_index(32) * kBandTw, w2048);
     slot_rows<64>(out + tw_slot_index(64) * kBandTw, w2048);
