@@ -110,7 +110,7 @@ def spectrum_inv(F):
 BAND_CFG_P32 = {32: (32, (32,)), 64: (32, (32, 2)), 128: (32, (32, 4)),
                 256: (32, (32, 8)), 512: (32, (32, 16)), 1024: (32, (32, 32)),
                 2048: (32, (32, 32, 2))}
-BAND_CFG_P16 = {32: (16, (16, 2)), 64: (16, (16, 4)), 128: (16, (16, 8)),
+BAND_CFG_P16 = {16: (16, (16,)), 32: (16, (16, 2)), 64: (16, (16, 4)), 128: (16, (16, 8)),
                 256: (16, (16, 16)), 512: (16, (16, 16, 2)),
                 1024: (16, (16, 16, 4)), 2048: (16, (16, 16, 8))}
 BAND_CFG = BAND_CFG_P16

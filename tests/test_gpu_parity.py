@@ -471,6 +471,34 @@ def test_other_filterbanks(dev, i):
     assert snr_db(o.heap(o.adj_bwd(gy)), _np(gk)) >= GRAD_DB
 
 
+@pytest.mark.parametrize("bank", [([3, 4, 2], [12, 24, 48]), ([2, 2, 5], [16, 32, 48]),
+                                  ([5, 4], [8, 32])])
+def test_more_filterbanks_against_oracle(dev, bank):
+    """banks the reference's fixtures do not cover: 16-point bands at
+    65536-sample slices (230 bands), 338 bands (descriptors in device memory)
+    and an 8/32 two-group bank; analysis, round trip and both transposes
+    against the oracle"""
+    from flash_cqt_b200.engine import Engine
+    from oracle.cqt_oracle import OctCQTOracle
+    e = Engine.from_params(bank[0], bank[1], 44100, 65536, dev)
+    o = OctCQTOracle(bank[0], bank[1], 44100, 65536)
+    x = np.random.default_rng(41).standard_normal((2, 65536))
+    h = e.analysis(torch.from_numpy(x).float().to(dev))
+    want = o.heap(o.fwd(x))
+    assert snr_db(want, _np(h)) >= COEF_DB
+    for b in range(2):
+        assert snr_db(want[b], _np(h)[b]) >= COEF_DB, b
+    y = e.synthesis(h)
+    assert snr_db(x, _np(y)) >= RT_DB
+    g = np.random.default_rng(42).standard_normal((2, 2, e.ncoef))
+    gc = (g[0] + 1j * g[1]).astype(np.complex64)
+    gx = e.adj_analysis(torch.from_numpy(gc).to(dev))
+    assert snr_db(o.adj_fwd(o.unheap(gc.astype(np.complex128))), _np(gx)) >= GRAD_DB
+    gy = np.random.default_rng(43).standard_normal((2, 65536))
+    gk = e.adj_synthesis(torch.from_numpy(gy).float().to(dev))
+    assert snr_db(o.heap(o.adj_bwd(gy)), _np(gk)) >= GRAD_DB
+
+
 def test_host_pipeline_equals_device_round_trip(dev):
     """chunks through the overlapped host pipeline == one device round trip,
     bit for bit, with a ragged last chunk and slot reuse across calls"""

@@ -143,3 +143,31 @@ def test_pruned_taps_are_dead(bank):
         if M == 2048:   # last stage radix 8, span 256: outputs 3, 4 = taps 768..1279
             assert 3 * 256 == 6 * M // 16 and 5 * 256 == 10 * M // 16
     assert pruned > 0
+
+
+# more banks: 16- to 2048-point bands, 162 to 338 bands, 3 colour planes
+MORE_BANKS = [([3, 4, 2], [12, 24, 48]), ([2, 3, 4], [8, 16, 24]), ([5, 4], [8, 32]),
+              ([1, 2, 3, 3], [8, 12, 16, 32]), ([4, 5], [12, 24]), ([2, 2, 5], [16, 32, 48]),
+              ([2, 3, 4], [12, 24, 32]), ([4, 4, 1], [16, 32, 64]), ([3, 6], [8, 24])]
+
+
+@pytest.mark.parametrize("bank", MORE_BANKS)
+def test_more_banks_model_vs_oracle(bank):
+    """the product's tables for other banks, driven through the kernels'
+    dataflow model, reproduce the oracle's analysis and synthesis"""
+    from oracle.cqt_oracle import OctCQTOracle
+    heap = HeapLayout(Filterbank(bank[0], bank[1], 44100, 65536))
+    tabs = build_tables(heap)
+    lens = sorted(set(int(M) for _, M, _ in heap.gspec))
+    assert 16 <= lens[0] and lens[-1] <= 2048
+    o = OctCQTOracle(bank[0], bank[1], 44100, 65536)
+    x = np.random.default_rng(7).standard_normal((1, 65536))
+    src, gain = tabs["fwd"]["analysis"]
+    h = km.bands_fwd(km.spectrum_fwd(x), {"src": src, "gain": gain}, heap.bands)
+    ref = o.heap(o.fwd(x))
+    assert snr_db(ref, h) > 140
+    dest, gre, gim, mask, npl = tabs["inv"]["synth"]
+    E = km.bands_inv(ref, {"dest": dest, "gre": gre, "gim": gim}, heap.bands, npl,
+                     PLANE_STRIDE)
+    y = km.spectrum_inv(km.planes_reduce(E, mask, npl, PLANE_STRIDE))
+    assert snr_db(o.bwd(o.unheap(ref)), y) > 140
