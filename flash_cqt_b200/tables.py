@@ -72,6 +72,11 @@ def build_tables(heap):
     if N not in SLICE_LENS:
         raise ValueError("the CUDA engines are built for 65536- and 32768-sample "
                          "slices, got %d" % N)
+    lens = sorted({int(M) for _, M, _ in heap.gspec})
+    bad = [M for M in lens if M not in BAND_ORDER]
+    if bad:
+        raise ValueError("the band kernels take block lengths that are powers of two in "
+                         "16..2048; this filterbank needs %s" % bad)
     half = N // 2
     stride = plane_stride(N)
     nc = heap.ncoef

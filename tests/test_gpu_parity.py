@@ -499,6 +499,8 @@ def test_more_filterbanks_against_oracle(dev, bank):
     assert snr_db(o.heap(o.adj_bwd(gy)), _np(gk)) >= GRAD_DB
 
 
+
+
 def test_host_pipeline_equals_device_round_trip(dev):
     """chunks through the overlapped host pipeline == one device round trip,
     bit for bit, with a ragged last chunk and slot reuse across calls"""

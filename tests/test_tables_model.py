@@ -171,3 +171,12 @@ def test_more_banks_model_vs_oracle(bank):
                      PLANE_STRIDE)
     y = km.spectrum_inv(km.planes_reduce(E, mask, npl, PLANE_STRIDE))
     assert snr_db(o.bwd(o.unheap(ref)), y) > 140
+
+
+@pytest.mark.parametrize("bank", [([3, 3, 3], [16, 16, 16]), ([9], [24])])
+def test_unsupported_band_lengths_are_refused(bank):
+    """banks that need 4096- or 8-point bands are refused when the tables are
+    built, with the lengths named (the upload refuses them as well)"""
+    heap = HeapLayout(Filterbank(bank[0], bank[1], 44100, 65536))
+    with pytest.raises(ValueError, match="block lengths"):
+        build_tables(heap)
