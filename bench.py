@@ -662,6 +662,52 @@ def sliced_stream(dev, world, rank, W, K, hbm, halo="auto"):
                      else "torch.distributed send / receive" if world > 1 else None)}
 
 
+def slice32k_round_trip(dev, hbm, B=2048, reps=10):
+    """round trips/s of 32768-sample slices (default bank), graph replay,
+    B slices per step; algorithmic bytes per slice: x in, coefficients out
+    and in, y out"""
+    import torch
+    from flash_cqt_b200 import OctCQT, TrainableCQT
+    n = 32768
+    e32 = TrainableCQT(OctCQT([3, 4, 2], [8, 16, 32], fs=44100, audio_len=n, device=dev),
+                       dev).eng
+    xs = torch.randn(B, n, device=dev, generator=torch.Generator(device=dev).manual_seed(6))
+    cs = torch.empty(B, e32.ncoef, dtype=torch.complex64, device=dev)
+    ys = torch.empty(B, n, device=dev)
+
+    def rt():
+        e32.analysis(xs, out=cs)
+        e32.synthesis(cs, out=ys)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            rt()
+    torch.cuda.current_stream().wait_stream(s)
+    gg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gg):
+        rt()
+    for _ in range(3):
+        gg.replay()
+    ts = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        gg.replay()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    med = statistics.median(ts)
+    err = float(((ys.double() - xs.double()) ** 2).sum() / (xs.double() ** 2).sum())
+    per_slice = 2 * n * 4 + 2 * e32.ncoef * 8
+    gbs = B * per_slice / (med / 1e3) / 1e9
+    del gg
+    return {"batch": B, "ms": med, "round_trips_per_s": B / (med / 1e3),
+            "algorithmic_bytes_per_slice": per_slice, "achieved_gbs": gbs,
+            "frac_of_hbm": gbs / hbm, "round_trip_snr_db": -10 * math.log10(err)}
+
+
 def extras(args, eng, t, dev, world, rank, barrier, W, K, hbm=6549.1):
     """e2e through the public API, the batch sweep, the train step and the
     sliced stream."""
@@ -757,6 +803,9 @@ def extras(args, eng, t, dev, world, rank, barrier, W, K, hbm=6549.1):
         sweep[str(Bs)] = {"ms": med, "round_trips_per_s": Bs / (med / 1e3)}
         del gg
     out["sweep_per_gpu"] = sweep
+    # 32768-sample slices (the same engines, 8192-point spectrum CTAs): 2048
+    # slices per step move the bytes of the 1024-slice headline step
+    out["slice_32768"] = slice32k_round_trip(dev, hbm)
     # same-box GPU baseline: the reference's own factored kernels and its
     # resident pair, built from its sources (oracle/build_ref.py)
     if world == 1:
