@@ -68,6 +68,8 @@ constexpr int kBandSmem = (kBandData + kBandTw) * 8;
 constexpr int kBandMinBlocks = (kP == 32 ? 2 : 4) * 256 / kBandThreads;
 
 template <int M, int P = kP> struct Sched;   // stage radices per block length
+// (only the build's own points-per-thread set is compiled in)
+#if FCQT_BAND_P == 32
 template <> struct Sched<32, 32>   { static constexpr int R1 = 32, R2 = 1,  R3 = 1; };
 template <> struct Sched<64, 32>   { static constexpr int R1 = 32, R2 = 2,  R3 = 1; };
 template <> struct Sched<128, 32>  { static constexpr int R1 = 32, R2 = 4,  R3 = 1; };
@@ -75,6 +77,7 @@ template <> struct Sched<256, 32>  { static constexpr int R1 = 32, R2 = 8,  R3 =
 template <> struct Sched<512, 32>  { static constexpr int R1 = 32, R2 = 16, R3 = 1; };
 template <> struct Sched<1024, 32> { static constexpr int R1 = 32, R2 = 32, R3 = 1; };
 template <> struct Sched<2048, 32> { static constexpr int R1 = 32, R2 = 32, R3 = 2; };
+#else
 template <> struct Sched<16, 16>   { static constexpr int R1 = 16, R2 = 1,  R3 = 1; };
 template <> struct Sched<32, 16>   { static constexpr int R1 = 16, R2 = 2,  R3 = 1; };
 template <> struct Sched<64, 16>   { static constexpr int R1 = 16, R2 = 4,  R3 = 1; };
@@ -83,6 +86,7 @@ template <> struct Sched<256, 16>  { static constexpr int R1 = 16, R2 = 16, R3 =
 template <> struct Sched<512, 16>  { static constexpr int R1 = 16, R2 = 16, R3 = 2; };
 template <> struct Sched<1024, 16> { static constexpr int R1 = 16, R2 = 16, R3 = 4; };
 template <> struct Sched<2048, 16> { static constexpr int R1 = 16, R2 = 16, R3 = 8; };
+#endif
 
 // shared twiddle rows of one block length: stage 2 rows W_{NS R}^{r k}
 // (r = 1..R2-1, k < NS2 = R1), then stage 3 rows (r = 1..R3-1, k < R1 R2)
@@ -271,10 +275,14 @@ __device__ __forceinline__ void stage_compute_pow_rows(float2 (&v)[P], int t,
 
 // stages 2 and 3 after stage 1's DFT; the last stage's outputs (index
 // n = j + r M / R_last, j = t + T b) go to `emit`
+// (only the build switches that read the last stage's twiddles from global
+// memory call it)
+#pragma nv_diag_suppress 177
 struct Tw2048 {
     const float2* w;
     __device__ __forceinline__ float2 operator()(int e) const { return __ldg(w + (e & 2047)); }
 };
+#pragma nv_diag_default 177
 
 template <int M, int S, class Emit>
 __device__ __forceinline__ void band_rest(float2 (&v)[kP], float2* buf, const float2* tws,
@@ -430,7 +438,6 @@ __device__ __forceinline__ CoefAddr coef_addr(const BandParams& bp, int slice, i
 
 // descriptor fields: {heap offset, lo (octave) | band id (side), l | Lg << 16,
 // flags: bit 0 side band, bits 4-7 synthesis plane, bits 8-11 adjoint plane}
-__device__ __forceinline__ bool d_side(int4 d) { return d.w & 1; }
 __device__ __forceinline__ int d_l(int4 d) { return d.z & 0xFFFF; }
 __device__ __forceinline__ int d_lg(int4 d) { return d.z >> 16; }
 __device__ __forceinline__ int d_plane(int4 d, int which) { return (d.w >> (4 + 4 * which)) & 15; }
